@@ -1,0 +1,148 @@
+/*
+ * potpori_b200 — C ABI of the B200 (sm_100a) per-shard Qwen3 verify pass.
+ *
+ * One handle is one shard: a contiguous layer range [layer_begin, layer_end) of a Qwen3
+ * model with its own F32 KV cache, on one CUDA device. It replaces the reference's
+ * `Shard<R: QwenRuntime>` (src/qwen/shard.rs:17-133) and the CUDA `QwenRuntime` adapter
+ * behind it (src/qwen/runtime/mod.rs:24-43, src/qwen/runtime/cuda.rs:54-190), and offers
+ * the `ShardEngine` surface (src/node.rs:55-86) as plain functions over plain pointers.
+ *
+ * Threading: a handle is used from one host thread at a time (the reference's runtime is
+ * not Sync either). Handles on different devices may run concurrently.
+ * Memory: all device memory is owned by the handle; host buffers are owned by the caller.
+ * Errors: every call returns a pp_status; pp_last_error() gives the message of the last
+ * failure on a handle (or of pp_shard_create when the handle is NULL).
+ */
+#ifndef POTPORI_B200_H
+#define POTPORI_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum pp_status {
+  PP_OK = 0,
+  PP_E_INVALID = 1,     /* rejected before launch: src/qwen/model.rs:373-395 rules */
+  PP_E_NONFINITE = 2,   /* non-finite logits at the tail (src/node.rs:266-272) */
+  PP_E_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  PP_E_TIMEOUT = 4,     /* a bounded device wait expired */
+  PP_E_OOM = 5,         /* device allocation failed */
+  PP_E_UNSUPPORTED = 6, /* a geometry this build does not run */
+  PP_E_MISSING = 7      /* a parameter of the shard was never loaded */
+} pp_status;
+
+typedef enum pp_dtype { PP_F32 = 0, PP_BF16 = 1 } pp_dtype;
+
+/* Model geometry: src/qwen/model.rs:11-21 (QwenConfig), field for field. */
+typedef struct pp_config {
+  uint32_t layers, hidden, intermediate, head_dim, n_heads, n_kv_heads, vocab_size;
+  float rms_norm_eps, rope_theta;
+} pp_config;
+
+/* Shard description: the arguments of QwenGraph::build (src/qwen/model.rs:198-205) and
+ * Shard::load_chunked (src/qwen/shard.rs:28-38). first/last are implied by the range. */
+typedef struct pp_shard_desc {
+  pp_config cfg;
+  uint32_t layer_begin, layer_end;
+  uint32_t capacity; /* KV positions (max_seq) */
+  uint32_t chunk;    /* verify chunk (gamma + 1); 0 = any size up to 8 */
+  int32_t cuda_device;
+} pp_shard_desc;
+
+/* What the tail returns for one chunk (src/node.rs:265-278, src/engine.rs:14-29,
+ * src/specdecode.rs:92-98). Arrays have one entry per chunk row. */
+typedef struct pp_verify_out {
+  int32_t* argmax;  /* [m], or NULL; -1 for a row with a non-finite logit */
+  float* top1;      /* [m], or NULL: largest logit */
+  float* top2;      /* [m], or NULL: second largest logit (a tie counts twice) */
+  float* logits;    /* [m][vocab] row form, or NULL (not computed when NULL) */
+  int32_t n_accepted; /* longest prefix with drafts[i] == argmax[i] */
+  int32_t correction; /* argmax[n_accepted] */
+  int32_t nonfinite_rows; /* bit r set when row r had a non-finite logit */
+} pp_verify_out;
+
+typedef struct pp_shard pp_shard;
+
+/* QwenGraph::build + QwenRuntime::compile (src/qwen/model.rs:198-337,
+ * src/qwen/runtime/cuda.rs:64-147): validates the range (model.rs:206-217), allocates the
+ * device arena (weights, KV cache, RoPE table, activations) and zeroes the KV cache. */
+pp_status pp_shard_create(const pp_shard_desc* desc, pp_shard** out);
+void pp_shard_destroy(pp_shard* shard);
+
+/* One parameter by checkpoint name and shape (src/qwen/hf.rs:227-272 load_inputs): matrices
+ * as BF16 bits or F32 (rounded to BF16), names containing "norm" as F32 or BF16 (widened).
+ * Names of other shards' parameters are accepted and ignored. */
+pp_status pp_shard_set_tensor(pp_shard* shard, const char* name, pp_dtype dtype,
+                              const void* host_data, uint64_t elements);
+/* Every parameter of the shard from a prepared safetensors file
+ * (model_combined_bf16_v1.safetensors layout, src/qwen/hf.rs:20,85-91,227-272). */
+pp_status pp_shard_load_safetensors(pp_shard* shard, const char* path);
+/* Every parameter from the seeded generator: matrices N(0, std) rounded to BF16 (Irwin-Hall
+ * of twelve 16-bit uniforms, counter-based by tensor name), norms 1. */
+pp_status pp_shard_init_random(pp_shard* shard, uint64_t seed, float std);
+/* Number of parameters not yet loaded; names ';'-separated into buf when given. */
+int32_t pp_shard_missing(const pp_shard* shard, char* buf, size_t len);
+
+/* ShardEngine::forward_tokens (src/node.rs:70, src/qwen/shard.rs:124-126): first shard.
+ * m tokens at absolute positions pos..pos+m-1. out_hidden: [m][hidden] for a non-last shard
+ * (may be NULL). verify: results on the last shard (may be NULL); drafts for the accept
+ * compare are tokens[1..m-1]. */
+pp_status pp_shard_forward_tokens(pp_shard* shard, uint32_t pos, const int32_t* tokens,
+                                  uint32_t m, float* out_hidden, pp_verify_out* verify);
+/* ShardEngine::forward_hidden (src/node.rs:73, src/qwen/shard.rs:127-129): non-first shard.
+ * hidden: [m][hidden] F32 (finite, src/qwen/model.rs:390-392). drafts: [n_drafts] tokens
+ * for the tail's accept compare (may be NULL). */
+pp_status pp_shard_forward_hidden(pp_shard* shard, uint32_t pos, uint32_t m, const float* hidden,
+                                  const int32_t* drafts, uint32_t n_drafts, float* out_hidden,
+                                  pp_verify_out* verify);
+
+/* Device-resident step for in-box pipeline stages (replaces the QUIC hop of
+ * src/node.rs:466-496 with device buffers). The step reads its input from the shard's own
+ * input buffer (pp_shard_buffers) and its step header from the device header buffer, both
+ * of which a peer copy or NCCL receive may fill; no host synchronisation. stream: a
+ * cudaStream_t (NULL = the shard's stream). max_rows selects the compiled chunk width. */
+pp_status pp_shard_step_device(pp_shard* shard, uint32_t max_rows, void* stream);
+/* Host-side enqueue of the step header (pos, m, drafts) for pp_shard_step_device. */
+pp_status pp_shard_set_step(pp_shard* shard, uint32_t pos, uint32_t m, const int32_t* tokens,
+                            const int32_t* drafts, uint32_t n_drafts, int32_t want_logits,
+                            void* stream);
+/* Device pointers of the shard's resident buffers: hidden [max_rows][hidden] F32 (input of
+ * a non-first shard, output of a non-last one), the step header (pp_step_header layout, 144
+ * bytes) and the step result (pp_step_result layout). */
+pp_status pp_shard_buffers(pp_shard* shard, void** hidden, void** header, void** result);
+/* Read the device step result after a device step (synchronises the stream). */
+pp_status pp_shard_read_result(pp_shard* shard, uint32_t m, pp_verify_out* verify, void* stream);
+
+/* ShardEngine::reset (src/qwen/runtime/cuda.rs:181-189): KV cache back to zeros. */
+pp_status pp_shard_reset(pp_shard* shard);
+/* Seeded N(0,1) KV rows [0, rows) in every layer (benchmark warm context; the oracle's
+ * or_shard_fill_kv writes the same values). */
+pp_status pp_shard_fill_kv(pp_shard* shard, uint64_t seed, uint32_t rows);
+
+/* ShardEngine getters (src/node.rs:57-67, src/qwen/shard.rs:106-123). */
+uint32_t pp_shard_capacity(const pp_shard* shard);
+uint32_t pp_shard_chunk_size(const pp_shard* shard);
+void pp_shard_range(const pp_shard* shard, uint32_t* begin, uint32_t* end);
+uint32_t pp_shard_hidden_dim(const pp_shard* shard);
+uint32_t pp_shard_vocab_size(const pp_shard* shard);
+uint32_t pp_shard_model_layers(const pp_shard* shard);
+/* Bytes of device memory the handle holds. */
+uint64_t pp_shard_device_bytes(const pp_shard* shard);
+
+/* Kernel launches of the last forward (for the benchmark's launch count). */
+uint32_t pp_shard_last_launches(const pp_shard* shard);
+/* Enable (1) / disable (0) CUDA-graph replay of the step (default on) and programmatic
+ * dependent launch between kernels (default on). */
+pp_status pp_shard_set_graphs(pp_shard* shard, int32_t enabled);
+pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
+
+/* Message of the last error on the handle (or of the last failed create when NULL). */
+size_t pp_last_error(const pp_shard* shard, char* buf, size_t len);
+/* Library version string. */
+const char* pp_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,155 @@
+// Shared device helpers for the sm_100a verify-pass kernels: BF16 decode, packed F32x2 FMA,
+// mbarrier + TMA wrappers (plain, non-multicast loads only), programmatic dependent launch
+// controls and the bounded waits every kernel uses.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pp {
+
+// ---- limits and layout constants -------------------------------------------------------
+constexpr int kMaxRows = 16;        // largest chunk (rows of the activation) a launch takes
+constexpr int kTileRows = 128;      // GEMV output rows per tile (= one head of 128 for QKV)
+constexpr int kChunkK = 64;         // K columns per pipeline stage (128 B of BF16)
+constexpr int kConsumerWarps = 8;   // GEMV math warps; one more warp issues TMA
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kAttnTile = 32;       // keys per attention tile
+constexpr int kAttnThreads = 256;
+constexpr int kMaxHeadDim = 128;
+
+// Bounded-wait budget: every spin on an mbarrier or a counter gives up after this many
+// polls (far beyond any legitimate wait, which ends in microseconds), records ST_TIMEOUT in
+// the step status word and returns.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// Status bits written to StepResult::status by the kernels.
+enum : int32_t {
+  ST_BAD_STEP = 1,       // pos/m outside [0, capacity) or the chunk limits
+  ST_NONFINITE_IN = 2,   // a non-finite value in the hidden input
+  ST_TIMEOUT = 4,        // a bounded wait expired
+  ST_NONFINITE_OUT = 8,  // non-finite logits in some row
+};
+
+// Per-step inputs, resident in device memory so captured graphs stay position independent.
+struct StepDesc {
+  int32_t pos;
+  int32_t m;
+  int32_t n_drafts;
+  int32_t flags;  // bit 0: write full logits
+  int32_t tokens[kMaxRows];
+  int32_t drafts[kMaxRows];
+};
+
+// Per-step results of the tail (argmax, top-2, accept/mismatch) and the status word.
+struct StepResult {
+  int32_t argmax[kMaxRows];
+  float top1[kMaxRows];
+  float top2[kMaxRows];
+  int32_t nonfinite_rows;  // bit r set when row r had a non-finite logit
+  int32_t n_accepted;
+  int32_t correction;
+  int32_t status;
+};
+
+// A malformed step header (one that did not come through the host checks) makes every
+// kernel of the step return before touching memory; step_begin_kernel reports it.
+__device__ __forceinline__ bool bad_step(const StepDesc* d, int32_t capacity, int32_t max_rows) {
+  const int32_t pos = d->pos, m = d->m;
+  return pos < 0 || m < 1 || m > max_rows || (int64_t)pos + m > capacity;
+}
+
+// ---- scalar helpers ---------------------------------------------------------------------
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// d += a * b on two F32 lanes with one sm_100 FFMA2 instruction (IEEE fma per lane).
+__device__ __forceinline__ void ffma2(float2& d, float2 a, float2 b) { d = __ffma2_rn(a, b, d); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- programmatic dependent launch -------------------------------------------------------
+// Everything a kernel does before pdl_wait() may only touch read-only data (weights,
+// tables). pdl_wait() returns once the previous kernel in the stream has completed and its
+// writes are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- mbarrier -------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the phase did not complete within kSpinLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// ---- TMA (tiled, no multicast) ------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- named barrier among the consumer warps ----------------------------------------------
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+}  // namespace pp

@@ -1,0 +1,511 @@
+// Skinny GEMV for the verify chunk: out[m][n] = sum_k W[n][k] * x[m][k] for m < M <= 8 rows of
+// F32 activations against a BF16 weight matrix W[N][K] (checkpoint orientation, row-major).
+//
+// This is the arithmetic of the reference's `linear` (src/qwen/model.rs:166-183): F32
+// products of BF16-decoded weights, summed in F32. It is HBM bound (about M flops per weight
+// byte), so the kernel is organised around streaming every weight byte exactly once:
+//
+//  * Stream-K over the GPU. The (tile of 128 output rows) x (64-column K chunk) iteration
+//    space is cut into one contiguous, equal range per CTA, so all 148 SMs get the same
+//    number of weight bytes whatever N and K are. A tile split between CTAs is finished
+//    by the last contributor, which sums the partial results in K order (deterministic).
+//  * One producer warp streams [128 x 64] BF16 weight boxes (16 KB, 128-byte swizzle) into
+//    a ring of shared-memory stages with TMA (no multicast) and mbarriers; it starts before
+//    the previous kernel has finished (programmatic dependent launch), since weights do not
+//    depend on it.
+//  * Eight consumer warps: lane = (row r4 in 0..3, 16-byte K slice kq in 0..7); each lane
+//    owns 4 rows x 8 K values per stage and multiplies them into M rows with packed FFMA2
+//    (even/odd K lanes), then an 8-lane shuffle reduction.
+//  * x is either resident in shared memory for the whole K (the input RMSNorm is applied
+//    while staging it, src/qwen/tiny.rs:20-23) or streamed next to the weights with TMA.
+//  * Fused epilogues: QK-RMSNorm + RoPE + KV write (QKV), residual add (O, down), SwiGLU
+//    (gate/up interleaved in 64-row blocks), and argmax/top-2/accept for the vocab head.
+#pragma once
+#include "pp_common.cuh"
+
+namespace pp {
+
+enum XMode : int { X_RESIDENT_NORM = 0, X_STREAM = 1 };
+enum Epi : int { EPI_QKV = 0, EPI_RESADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_STORE = 4 };
+
+struct ArgRec {
+  float best;
+  int32_t idx;
+  float second;
+  int32_t nonfinite;
+};
+
+struct GemvArgs {
+  int32_t n_out;     // valid output columns (after the SwiGLU pairing: intermediate)
+  int32_t n_packed;  // rows of the packed weight matrix
+  int32_t k;         // valid K
+  int32_t kp;        // padded K (multiple of 64): row stride of W and x
+  int32_t tiles;     // ceil(n_packed / 128)
+  int32_t kchunks;   // kp / 64
+  int32_t nstages;
+  // resident x
+  const float* x;
+  int32_t ldx;
+  const float* norm_w;
+  float eps;
+  int32_t check_input;  // flag non-finite x values (the shard's hidden input)
+  // output
+  float* out;
+  int32_t ldo;
+  // QKV epilogue
+  const float* qn;
+  const float* kn;
+  const float2* rope;  // [capacity][head_dim/2] (cos, sin)
+  float* kcache;       // [n_kv][capacity][head_dim]
+  float* vcache;
+  int32_t q_dim, kv_dim, head_dim, capacity;
+  // argmax epilogue
+  float* logits;  // [M][vocab] when requested by the step flags
+  // scratch
+  float* partials;      // [grid][2][128][MT]
+  uint32_t* tile_cnt;   // [tiles], zero between launches
+  ArgRec* recs;         // [grid][MT]
+  uint32_t* done_cnt;   // zero between launches
+  const StepDesc* desc;
+  StepResult* res;
+};
+
+template <int MT, int XM>
+struct GemvSmem {
+  static constexpr int kWBytes = kTileRows * kChunkK * 2;  // 16 KB per stage
+  static constexpr int kXBytes = (XM == X_STREAM) ? MT * kChunkK * 4 : 0;
+  static __host__ __device__ size_t x_off(int ns) { return (size_t)ns * kWBytes; }
+  static __host__ __device__ size_t xs_off(int ns) { return x_off(ns) + (size_t)ns * kXBytes; }
+  static __host__ __device__ size_t tile_off(int ns, int kp) {
+    return xs_off(ns) + (XM == X_RESIDENT_NORM ? (size_t)MT * kp * 4 : 0);
+  }
+  static __host__ __device__ size_t bar_off(int ns, int kp) {
+    return tile_off(ns, kp) + (size_t)kTileRows * MT * 4;
+  }
+  static __host__ __device__ size_t misc_off(int ns, int kp) { return bar_off(ns, kp) + 16 * ns; }
+  static __host__ __device__ size_t total(int ns, int kp) { return misc_off(ns, kp) + 512 + 1024; }
+};
+
+__device__ __forceinline__ int64_t sk_start(int64_t b, int64_t T, int64_t G) { return b * T / G; }
+__device__ __forceinline__ int64_t sk_owner(int64_t i, int64_t T, int64_t G) {
+  return ((i + 1) * G + T - 1) / T - 1;
+}
+
+__device__ __forceinline__ void argrec_merge(float& b1, int32_t& i1, float& s1, float b2,
+                                             int32_t i2, float s2) {
+  if (b2 > b1 || (b2 == b1 && i2 < i1)) {
+    s1 = fmaxf(fmaxf(b1, s1), s2);
+    b1 = b2;
+    i1 = i2;
+  } else {
+    s1 = fmaxf(fmaxf(b2, s1), s2);
+  }
+}
+
+template <int MT, int XM, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    gemv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                const GemvArgs a) {
+  using L = GemvSmem<MT, XM>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int ns = a.nstages;
+  uint8_t* wst = smem;
+  uint8_t* xst = smem + L::x_off(ns);
+  float* xs = (float*)(smem + L::xs_off(ns));
+  float* tile_out = (float*)(smem + L::tile_off(ns, a.kp));
+  uint64_t* full = (uint64_t*)(smem + L::bar_off(ns, a.kp));
+  uint64_t* empty = full + ns;
+  int32_t* misc = (int32_t*)(smem + L::misc_off(ns, a.kp));
+  // misc: [0] fixup flag, [1] status bits, [2..] argmax running state (4 x MT words)
+  float* st_best = (float*)(misc + 8);
+  int32_t* st_idx = misc + 8 + MT;
+  float* st_second = (float*)(misc + 8 + 2 * MT);
+  int32_t* st_nonf = misc + 8 + 3 * MT;
+
+  if (bad_step(a.desc, a.capacity, MT)) return;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int64_t T = (int64_t)a.tiles * a.kchunks;
+  const int64_t G = gridDim.x;
+  const int64_t i0 = sk_start(blockIdx.x, T, G), i1 = sk_start(blockIdx.x + 1, T, G);
+  const int first_tile = (int)(i0 / a.kchunks);
+
+  if (tid == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+    misc[0] = 0;
+    misc[1] = 0;
+    pdl_launch_dependents();
+  }
+  if (tid < MT) {
+    st_best[tid] = -INFINITY;
+    st_idx[tid] = 0x7fffffff;
+    st_second[tid] = -INFINITY;
+    st_nonf[tid] = 0;
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ producer warp
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      tma_prefetch_desc(&wmap);
+      if (XM == X_STREAM) tma_prefetch_desc(&xmap);
+      const int64_t n_it = i1 - i0;
+      const int pre = (int)(n_it < ns ? n_it : ns);
+      const uint32_t bytes = L::kWBytes + L::kXBytes;
+      for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
+        const int64_t it = i0 + i;
+        const int t = (int)(it / a.kchunks), c = (int)(it % a.kchunks);
+        mbar_arrive_expect_tx(&full[i], bytes);
+        tma_load_2d(wst + (size_t)i * L::kWBytes, &wmap, &full[i], c * kChunkK, t * kTileRows);
+      }
+      pdl_wait();
+      if (XM == X_STREAM)
+        for (int i = 0; i < pre; ++i) {
+          const int c = (int)((i0 + i) % a.kchunks);
+          tma_load_2d(xst + (size_t)i * L::kXBytes, &xmap, &full[i], c * kChunkK, 0);
+        }
+      int64_t issued = pre;
+      for (int64_t i = pre; i < n_it; ++i) {
+        const int s = (int)(i % ns);
+        const uint32_t use = (uint32_t)(i / ns);
+        if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
+        const int64_t it = i0 + i;
+        const int t = (int)(it / a.kchunks), c = (int)(it % a.kchunks);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d(wst + (size_t)s * L::kWBytes, &wmap, &full[s], c * kChunkK, t * kTileRows);
+        if (XM == X_STREAM)
+          tma_load_2d(xst + (size_t)s * L::kXBytes, &xmap, &full[s], c * kChunkK, 0);
+        issued = i + 1;
+      }
+      if (issued < n_it) {
+        atomicOr(&a.res->status, ST_TIMEOUT);
+        // Let the copies already issued land before the CTA's shared memory goes away.
+        for (int64_t j = (issued > ns ? issued - ns : 0); j < issued; ++j)
+          mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumer warps
+  pdl_wait();
+  const StepDesc& d = *a.desc;
+  const int mv = d.m;  // rows that matter; the launch guarantees 1 <= m <= MT
+  const int r4 = lane >> 3, kq = lane & 7;
+
+  if (XM == X_RESIDENT_NORM) {
+    // RMSNorm (tiny.rs:20-23): x / sqrt(mean(x^2) + eps) * w, staged as [chunk][m][h][kq][4]
+    // so that the lanes of a warp read 128 contiguous bytes per load.
+    __shared__ float red[kConsumerWarps][MT];
+    __shared__ float rms_s[MT];
+    float ss[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) ss[m] = 0.f;
+    int bad = 0;
+    for (int k = tid; k < a.k; k += kConsumerWarps * 32) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+        if (m < mv) {
+          const float v = a.x[(size_t)m * a.ldx + k];
+          bad |= !isfinite(v);
+          ss[m] += v * v;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float w = warp_sum(ss[m]);
+      if (lane == 0) red[warp][m] = w;
+    }
+    if (a.check_input && bad) atomicOr(&misc[1], ST_NONFINITE_IN);
+    consumer_sync();
+    if (tid < MT) {
+      float t = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) t += red[w][tid];
+      rms_s[tid] = sqrtf(t / (float)a.k + a.eps);
+    }
+    consumer_sync();
+    for (int e = tid; e < MT * a.kp; e += kConsumerWarps * 32) {
+      const int m = e / a.kp, k = e - m * a.kp;
+      float v = 0.f;
+      if (m < mv && k < a.k) v = a.x[(size_t)m * a.ldx + k] / rms_s[m] * a.norm_w[k];
+      const int c = k >> 6, kl = k & 63;
+      const int kqq = kl >> 3, h = (kl >> 2) & 1, e4 = kl & 3;
+      xs[((size_t)(c * MT + m) * 64) + (h * 8 + kqq) * 4 + e4] = v;
+    }
+    consumer_sync();
+    if (tid == 0 && misc[1]) atomicOr(&a.res->status, misc[1]);
+  }
+
+  int64_t it = i0;
+  int local = 0;  // iterations consumed so far by this CTA
+  bool ok = true;
+  while (it < i1 && ok) {
+    const int t = (int)(it / a.kchunks);
+    const int64_t tile_begin = (int64_t)t * a.kchunks, tile_end = tile_begin + a.kchunks;
+    const int64_t seg_begin = it, seg_end = i1 < tile_end ? i1 : tile_end;
+    float2 acc[4][MT];
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[g][m] = make_float2(0.f, 0.f);
+
+    for (; it < seg_end; ++it, ++local) {
+      const int s = local % ns;
+      if (!mbar_wait(&full[s], (uint32_t)(local / ns) & 1)) {
+        ok = false;
+        break;
+      }
+      const int c = (int)(it - tile_begin);
+      const uint8_t* wb = wst + (size_t)s * L::kWBytes;
+      uint4 wv[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int rr = warp * 16 + g * 4 + r4;
+        wv[g] = *(const uint4*)(wb + rr * 128 + ((kq ^ (rr & 7)) << 4));
+      }
+      float4 xa[MT], xb[MT];
+      if (XM == X_STREAM) {
+        const float* xb_s = (const float*)(xst + (size_t)s * L::kXBytes);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          xa[m] = *(const float4*)(xb_s + m * 64 + kq * 8);
+          xb[m] = *(const float4*)(xb_s + m * 64 + kq * 8 + 4);
+        }
+      } else {
+        const float* base = xs + (size_t)c * MT * 64;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          xa[m] = *(const float4*)(base + m * 64 + kq * 4);
+          xb[m] = *(const float4*)(base + m * 64 + 32 + kq * 4);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const float2 w01 = make_float2(bf16lo(wv[g].x), bf16hi(wv[g].x));
+        const float2 w23 = make_float2(bf16lo(wv[g].y), bf16hi(wv[g].y));
+        const float2 w45 = make_float2(bf16lo(wv[g].z), bf16hi(wv[g].z));
+        const float2 w67 = make_float2(bf16lo(wv[g].w), bf16hi(wv[g].w));
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          ffma2(acc[g][m], w01, make_float2(xa[m].x, xa[m].y));
+          ffma2(acc[g][m], w23, make_float2(xa[m].z, xa[m].w));
+          ffma2(acc[g][m], w45, make_float2(xb[m].x, xb[m].y));
+          ffma2(acc[g][m], w67, make_float2(xb[m].z, xb[m].w));
+        }
+      }
+    }
+    if (!ok) break;
+
+    // Sum even/odd lanes and the eight K slices of each row.
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int rr = warp * 16 + g * 4 + r4;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float v = acc[g][m].x + acc[g][m].y;
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if ((m & 7) == kq) tile_out[rr * MT + m] = v;
+      }
+    }
+    consumer_sync();
+
+    const bool whole = seg_begin == tile_begin && seg_end == tile_end;
+    if (!whole) {
+      // Split tile: publish this CTA's partial; the last contributor finishes the tile.
+      const int slot = (t == first_tile) ? 0 : 1;
+      float* mine = a.partials + ((size_t)blockIdx.x * 2 + slot) * kTileRows * MT;
+      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) mine[e] = tile_out[e];
+      __threadfence();
+      consumer_sync();
+      const int64_t b_lo = sk_owner(tile_begin, T, G), b_hi = sk_owner(tile_end - 1, T, G);
+      if (tid == 0) {
+        const uint32_t old = atomicAdd(&a.tile_cnt[t], 1u);
+        misc[0] = (old == (uint32_t)(b_hi - b_lo));
+      }
+      consumer_sync();
+      if (!misc[0]) continue;
+      __threadfence();
+      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
+        float v = 0.f;
+        for (int64_t b = b_lo; b <= b_hi; ++b) {
+          const int bslot = (sk_start(b, T, G) / a.kchunks == t) ? 0 : 1;
+          v += __ldcg(a.partials + ((size_t)b * 2 + bslot) * kTileRows * MT + e);
+        }
+        tile_out[e] = v;
+      }
+      if (tid == 0) a.tile_cnt[t] = 0u;
+      consumer_sync();
+    }
+
+    // ---------------------------------------------------------------- epilogues
+    if (EPI == EPI_STORE || EPI == EPI_RESADD) {
+      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
+        const int m = e / kTileRows, r = e - m * kTileRows;
+        const int n = t * kTileRows + r;
+        if (m < mv && n < a.n_out) {
+          float* o = a.out + (size_t)m * a.ldo + n;
+          if (EPI == EPI_RESADD)
+            *o += tile_out[r * MT + m];
+          else
+            *o = tile_out[r * MT + m];
+        }
+      }
+    } else if (EPI == EPI_SWIGLU) {
+      constexpr int half = kTileRows / 2;
+      for (int e = tid; e < half * MT; e += kConsumerWarps * 32) {
+        const int m = e / half, r = e - m * half;
+        const int n = t * half + r;
+        if (m < mv && n < a.n_out) {
+          const float g = tile_out[r * MT + m], u = tile_out[(r + half) * MT + m];
+          a.out[(size_t)m * a.ldo + n] = g / (1.0f + expf(-g)) * u;  // tiny.rs:111-115
+        }
+      }
+    } else if (EPI == EPI_QKV) {
+      // Heads of this tile: per-head RMSNorm with q_norm/k_norm, rotate-half RoPE at the
+      // absolute position, K and V rows written into the cache (src/qwen/model.rs:267-302,
+      // tiny.rs:24-37). A warp handles one (head, row) pair.
+      const int hd = a.head_dim, half = hd >> 1;
+      const int heads = kTileRows / hd;
+      for (int p = warp; p < heads * mv; p += kConsumerWarps) {
+        const int hl = p / mv, m = p - hl * mv;
+        const int n0 = t * kTileRows + hl * hd;
+        const int pos = d.pos + m;
+        const float* v = tile_out + (size_t)(hl * hd) * MT + m;  // v[i * MT]
+        if (n0 < a.q_dim + a.kv_dim) {
+          const bool isq = n0 < a.q_dim;
+          const float* w = isq ? a.qn : a.kn;
+          float ssq = 0.f;
+          for (int i = lane; i < hd; i += 32) ssq += v[i * MT] * v[i * MT];
+          ssq = warp_sum(ssq);
+          const float rms = sqrtf(ssq / (float)hd + a.eps);
+          float* dst;
+          if (isq)
+            dst = a.out + (size_t)m * a.ldo + n0;
+          else
+            dst = a.kcache + ((size_t)((n0 - a.q_dim) / hd) * a.capacity + pos) * hd;
+          const float2* rp = a.rope + (size_t)pos * half;
+          for (int i = lane; i < half; i += 32) {
+            const float x0 = v[i * MT] / rms * w[i];
+            const float x1 = v[(i + half) * MT] / rms * w[i + half];
+            const float2 cs = rp[i];
+            dst[i] = x0 * cs.x - x1 * cs.y;
+            dst[i + half] = x1 * cs.x + x0 * cs.y;
+          }
+        } else if (n0 < a.q_dim + 2 * a.kv_dim) {
+          float* dst = a.vcache + ((size_t)((n0 - a.q_dim - a.kv_dim) / hd) * a.capacity + pos) * hd;
+          for (int i = lane; i < hd; i += 32) dst[i] = v[i * MT];
+        }
+      }
+    } else if (EPI == EPI_ARGMAX) {
+      // Greedy pick of src/engine.rs:14-29 over this tile's vocab rows: first index of the
+      // strict maximum; any non-finite value marks the row.
+      for (int m = warp; m < mv; m += kConsumerWarps) {
+        float b = -INFINITY, s2 = -INFINITY;
+        int32_t bi = 0x7fffffff;
+        int nf = 0;
+        const bool dump = d.flags & 1;
+        for (int r = lane; r < kTileRows; r += 32) {
+          const int n = t * kTileRows + r;
+          if (n >= a.n_out) break;
+          const float v = tile_out[r * MT + m];
+          if (dump) a.logits[(size_t)m * a.n_out + n] = v;
+          if (!isfinite(v)) {
+            nf = 1;
+            continue;
+          }
+          argrec_merge(b, bi, s2, v, n, -INFINITY);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+          const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          const float os = __shfl_xor_sync(0xffffffffu, s2, o);
+          argrec_merge(b, bi, s2, ob, oi, os);
+          nf |= __shfl_xor_sync(0xffffffffu, nf, o);
+        }
+        if (lane == 0) {
+          argrec_merge(st_best[m], st_idx[m], st_second[m], b, bi, s2);
+          st_nonf[m] |= nf;
+        }
+      }
+    }
+    consumer_sync();  // tile_out is reused by the next tile
+  }
+
+  if (!ok) {
+    if (tid == 0) atomicOr(&a.res->status, ST_TIMEOUT);
+    return;
+  }
+
+  if (EPI == EPI_ARGMAX) {
+    consumer_sync();
+    if (tid < MT) {
+      ArgRec r;
+      r.best = st_best[tid];
+      r.idx = st_idx[tid];
+      r.second = st_second[tid];
+      r.nonfinite = st_nonf[tid];
+      a.recs[(size_t)blockIdx.x * MT + tid] = r;
+    }
+    __threadfence();
+    consumer_sync();
+    if (tid == 0) {
+      const uint32_t old = atomicAdd(a.done_cnt, 1u);
+      misc[0] = (old == (uint32_t)(G - 1));
+    }
+    consumer_sync();
+    if (!misc[0]) return;
+    __threadfence();
+    // Last CTA: reduce every CTA's record, then the accept/mismatch compare of
+    // src/specdecode.rs:92-98.
+    for (int m = warp; m < mv; m += kConsumerWarps) {
+      float b = -INFINITY, s2 = -INFINITY;
+      int32_t bi = 0x7fffffff;
+      int nf = 0;
+      for (int64_t g = lane; g < G; g += 32) {
+        const ArgRec* rp = a.recs + (size_t)g * MT + m;
+        const float rb = __ldcg(&rp->best), rs = __ldcg(&rp->second);
+        const int32_t ri = __ldcg(&rp->idx), rn = __ldcg(&rp->nonfinite);
+        argrec_merge(b, bi, s2, rb, ri, rs);
+        nf |= rn;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float os = __shfl_xor_sync(0xffffffffu, s2, o);
+        argrec_merge(b, bi, s2, ob, oi, os);
+        nf |= __shfl_xor_sync(0xffffffffu, nf, o);
+      }
+      if (lane == 0) {
+        a.res->argmax[m] = nf ? -1 : bi;
+        a.res->top1[m] = b;
+        a.res->top2[m] = s2;
+        if (nf) {
+          atomicOr(&a.res->nonfinite_rows, 1 << m);
+          atomicOr(&a.res->status, ST_NONFINITE_OUT);
+        }
+      }
+    }
+    consumer_sync();
+    if (tid == 0) {
+      int n = 0;
+      while (n < d.n_drafts && n < mv && d.drafts[n] == a.res->argmax[n]) ++n;
+      if (n >= mv) n = mv - 1;
+      a.res->n_accepted = n;
+      a.res->correction = a.res->argmax[n];
+      *a.done_cnt = 0u;
+    }
+  }
+}
+
+}  // namespace pp

@@ -1,0 +1,101 @@
+// Small kernels around the verify pass: the embedding gather of the first shard, the seeded
+// weight generator, packing uploaded parameters into the shard's HBM layout, and fills.
+#pragma once
+#include "pp_common.cuh"
+
+namespace pp {
+
+// Embedding rows of the chunk's tokens, BF16 decoded to F32 (src/qwen/model.rs:239-241).
+// Grid (MT); a row past m is left alone.
+__global__ void embed_kernel(const uint16_t* __restrict__ table, int32_t hidden, int32_t vocab,
+                             float* __restrict__ x, int32_t ldx, const StepDesc* desc,
+                             StepResult* res, int32_t capacity, int32_t max_rows) {
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (bad_step(desc, capacity, max_rows)) return;
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= desc->m) return;
+  const int tok = desc->tokens[r];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
+    return;
+  }
+  const uint16_t* row = table + (size_t)tok * hidden;
+  for (int k = threadIdx.x; k < hidden; k += blockDim.x)
+    x[(size_t)r * ldx + k] = __uint_as_float((uint32_t)row[k] << 16);
+}
+
+// ---- seeded generator (bit-identical to the oracle's or_gen_bf16) -------------------------
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint16_t gen_bf16(uint64_t key, int64_t i, float scale) {
+  int32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const uint64_t r = mix64(key + (uint64_t)(3 * i + j + 1) * 0x9E3779B97F4A7C15ull);
+    s += (int32_t)(r & 0xffff) + (int32_t)((r >> 16) & 0xffff) + (int32_t)((r >> 32) & 0xffff) +
+         (int32_t)(r >> 48);
+  }
+  return f32_to_bf16_rne(__fmul_rn((float)(s - 393210), scale));
+}
+
+// Where logical row r of a checkpoint matrix lands in the packed matrix:
+// (r / blk) * blk_stride + r % blk + offset. QKV sections use blk = rows (one block);
+// gate/up are interleaved in 64-row blocks so one 128-row tile holds both halves.
+struct RowMap {
+  int32_t blk, blk_stride, offset;
+  __host__ __device__ int64_t operator()(int64_t r) const {
+    return (r / blk) * blk_stride + (r % blk) + offset;
+  }
+};
+
+// Fill a [rows][cols] logical matrix from the generator into the packed layout (row stride ld).
+__global__ void gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int64_t ld,
+                                  RowMap map, uint64_t key, float scale) {
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[map(r) * ld + c] = gen_bf16(key, i, scale);
+  }
+}
+
+// Copy an uploaded [rows][cols] matrix (BF16 bits, or F32 rounded to BF16 as the reference's
+// loader does, src/qwen/hf.rs:248-253) into the packed layout.
+__global__ void pack_matrix_kernel(uint16_t* dst, const void* src, int32_t src_f32, int64_t rows,
+                                   int64_t cols, int64_t ld, RowMap map) {
+  const int64_t n = rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const uint16_t v = src_f32 ? f32_to_bf16_rne(((const float*)src)[i]) : ((const uint16_t*)src)[i];
+    dst[map(r) * ld + c] = v;
+  }
+}
+
+__global__ void fill_f32_kernel(float* dst, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = v;
+}
+
+// Seeded N(0,1) values (rounded through BF16) for KV rows [0, rows) of one layer: a warm
+// context for benchmarks; the oracle's or_shard_fill_kv writes the same values.
+__global__ void fill_kv_kernel(float* kc, float* vc, int64_t rows, int32_t kv_dim, int32_t n_kv,
+                               int32_t hd, int64_t capacity, uint64_t key) {
+  const int64_t n = rows * kv_dim;
+  const float scale = 1.0f / 65536.0f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / kv_dim, col = i - row * kv_dim;
+    const int64_t h = col / hd, dd = col - h * hd;
+    const size_t dst = ((size_t)h * capacity + row) * hd + dd;
+    kc[dst] = __uint_as_float((uint32_t)gen_bf16(key, 2 * i, scale) << 16);
+    vc[dst] = __uint_as_float((uint32_t)gen_bf16(key, 2 * i + 1, scale) << 16);
+  }
+}
+
+}  // namespace pp

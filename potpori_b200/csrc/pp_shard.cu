@@ -1,0 +1,1200 @@
+// Host side of the verify pass: the shard object behind the C ABI of include/potpori_b200.h.
+//
+// A shard owns, on one device: the packed BF16 weights of its layers (QKV concatenated,
+// gate/up interleaved in 64-row blocks, rows padded to 128 and K to 64 with zeros so every
+// TMA box is in bounds), F32 norms, the F32 KV cache in head-major [n_kv][capacity][128]
+// layout, a RoPE table [capacity][head_dim/2] of (cos, sin) computed once in double precision,
+// activation buffers for up to 8 rows, and the scratch of the stream-K GEMV and split-KV
+// attention. One step is a fixed sequence of kernels that reads pos/m/tokens from a device
+// header, so it is captured once per chunk width into a CUDA graph and replayed; kernels are
+// chained with programmatic dependent launch so each GEMV streams its weights while the
+// previous kernel drains.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/potpori_b200.h"
+#include "pp_attn.cuh"
+#include "pp_common.cuh"
+#include "pp_gemv.cuh"
+#include "pp_misc.cuh"
+
+using namespace pp;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+inline float bits_to_float(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+uint64_t mix64h(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+uint64_t fnv1a(const char* s) {
+  uint64_t h = 0xcbf29ce484222325ull;
+  for (const unsigned char* p = (const unsigned char*)s; *p; ++p) {
+    h ^= *p;
+    h *= 0x100000001b3ull;
+  }
+  return h;
+}
+uint64_t tensor_key(uint64_t seed, const char* name) {
+  return mix64h(seed * 0x9E3779B97F4A7C15ull ^ fnv1a(name));
+}
+
+enum MatId { M_Q, M_K, M_V, M_O, M_G, M_U, M_D, M_COUNT };
+enum NormId { N_ATTN, N_QN, N_KN, N_FFN, N_COUNT };
+const char* kMatNames[M_COUNT] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                                  "self_attn.o_proj", "mlp.gate_proj",    "mlp.up_proj",
+                                  "mlp.down_proj"};
+const char* kNormNames[N_COUNT] = {"input_layernorm", "self_attn.q_norm", "self_attn.k_norm",
+                                   "post_attention_layernorm"};
+
+struct LayerDev {
+  uint16_t* wqkv = nullptr;  // [qkv_rows][Hp]
+  uint16_t* wo = nullptr;    // [o_rows][Qp]
+  uint16_t* wgu = nullptr;   // [gu_rows][Hp]
+  uint16_t* wd = nullptr;    // [d_rows][Ip]
+  float* norm[N_COUNT] = {};
+  float* kc = nullptr;  // [n_kv][capacity][hd]
+  float* vc = nullptr;
+  CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;
+  bool mat_set[M_COUNT] = {};
+  bool norm_set[N_COUNT] = {};
+};
+
+constexpr int kVariants = 4;  // chunk widths 1, 2, 4, 8
+inline int variant_of(int m) { return m <= 1 ? 0 : m <= 2 ? 1 : m <= 4 ? 2 : 3; }
+inline int width_of(int v) { return 1 << v; }
+
+}  // namespace
+
+struct pp_shard {
+  pp_shard_desc d;
+  int H, Q, KV, I, hd, V, nh, nkv, G;
+  int64_t Hp, Qp, Ip, Vp;
+  int64_t qkv_rows, o_rows, gu_rows, d_rows;
+  int first, last, nl;
+  int dev = 0, num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  uint64_t bytes = 0;
+  std::vector<LayerDev> L;
+  uint16_t* embed = nullptr;  // [Vp][Hp]
+  float* final_norm = nullptr;
+  CUtensorMap tm_embed;
+  bool embed_set = false, final_norm_set = false;
+  float2* rope = nullptr;
+  float* x = nullptr;      // [kMaxRows][Hp]
+  float* qbuf = nullptr;   // [kMaxRows][Q]
+  float* attn = nullptr;   // [kMaxRows][Qp]
+  float* act = nullptr;    // [kMaxRows][Ip]
+  float* logits = nullptr; // [kMaxRows][V]
+  float* apart = nullptr;
+  float* gpart = nullptr;
+  uint32_t* tile_cnt = nullptr;
+  ArgRec* recs = nullptr;
+  uint32_t* done = nullptr;
+  StepDesc* d_desc = nullptr;
+  StepResult* d_res = nullptr;
+  StepDesc* h_desc = nullptr;
+  StepResult* h_res = nullptr;
+  float* h_stage = nullptr;  // pinned [kMaxRows][H]
+  CUtensorMap tm_x_attn[kVariants], tm_x_act[kVariants];
+  int splits = 1, nq_max = 1;
+  int max_grid = 148;
+  bool use_graphs = true, use_pdl = true;
+  cudaGraphExec_t exec[kVariants] = {};
+  uint32_t launches = 0;                 // kernels of the step being enqueued
+  uint32_t variant_launches[kVariants] = {};
+  int last_variant = 0;
+  std::string err;
+};
+
+namespace {
+
+pp_status fail(pp_shard* s, pp_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (s)
+    s->err = buf;
+  else
+    g_create_error = buf;
+  return st;
+}
+
+#define CK(call)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(s, e_ == cudaErrorMemoryAllocation ? PP_E_OOM : PP_E_CUDA, "%s: %s", #call, \
+                  cudaGetErrorString(e_));                                               \
+  } while (0)
+
+template <typename T>
+pp_status dalloc(pp_shard* s, T** p, size_t bytes) {
+  void* q = nullptr;
+  CK(cudaMalloc(&q, bytes ? bytes : 16));
+  CK(cudaMemsetAsync(q, 0, bytes ? bytes : 16, s->stream));
+  s->allocs.push_back(q);
+  s->bytes += bytes;
+  *p = (T*)q;
+  return PP_OK;
+}
+
+pp_status make_map(pp_shard* s, CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t cols,
+                   uint64_t rows, uint32_t elem_bytes, uint32_t box_cols, uint32_t box_rows,
+                   CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(s, PP_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(s, PP_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PP_OK;
+}
+
+pp_status make_wmap(pp_shard* s, CUtensorMap* map, uint16_t* base, int64_t cols, int64_t rows) {
+  return make_map(s, map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, rows, 2, kChunkK,
+                  kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// ---- kernel table ---------------------------------------------------------------------------
+template <int MT, int XM>
+int gemv_stages(int64_t kp) {
+  using Lay = GemvSmem<MT, XM>;
+  const size_t budget = 227 * 1024;
+  int ns = 12;
+  while (ns > 2 && Lay::total(ns, (int)kp) > budget) --ns;
+  return ns;
+}
+
+template <int MT, int XM, int EPI>
+pp_status launch_gemv(pp_shard* s, cudaStream_t st, const CUtensorMap& wmap, const CUtensorMap& xmap,
+                      GemvArgs a) {
+  using Lay = GemvSmem<MT, XM>;
+  a.nstages = gemv_stages<MT, XM>(a.kp);
+  const size_t smem = Lay::total(a.nstages, a.kp);
+  if (smem > 227 * 1024)
+    return fail(s, PP_E_UNSUPPORTED, "GEMV with K=%d needs %zu bytes of shared memory", a.k, smem);
+  auto kern = gemv_kernel<MT, XM, EPI>;
+  const int64_t T = (int64_t)a.tiles * a.kchunks;
+  const int grid = (int)(T < s->max_grid ? T : s->max_grid);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = s->use_pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a));
+  ++s->launches;
+  return PP_OK;
+}
+
+template <typename... KArgs, typename... Args>
+pp_status launch_plain(pp_shard* s, cudaStream_t st, bool pdl, dim3 grid, dim3 block, size_t smem,
+                       void (*kern)(KArgs...), Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (pdl && s->use_pdl) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, args...));
+  ++s->launches;
+  return PP_OK;
+}
+
+}  // namespace
+
+// Validates the step header on the device, clears the result and stops every later kernel
+// of a malformed step (a header that came from a peer instead of the host checks).
+__global__ void step_begin_kernel(const StepDesc* desc, StepResult* res, int32_t capacity,
+                                  int32_t max_rows, int32_t vocab, int32_t first) {
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  pdl_wait();
+  const int t = threadIdx.x;
+  if (t < kMaxRows) {
+    res->argmax[t] = -1;
+    res->top1[t] = 0.f;
+    res->top2[t] = 0.f;
+  }
+  if (t == 0) {
+    res->nonfinite_rows = 0;
+    res->n_accepted = 0;
+    res->correction = -1;
+    const StepDesc d = *desc;
+    bool bad = d.pos < 0 || d.m < 1 || d.m > max_rows || (int64_t)d.pos + d.m > capacity ||
+               d.n_drafts < 0 || d.n_drafts > kMaxRows;
+    if (first && !bad)
+      for (int r = 0; r < d.m; ++r) bad |= d.tokens[r] < 0 || d.tokens[r] >= vocab;
+    res->status = bad ? ST_BAD_STEP : 0;
+  }
+}
+
+namespace {
+
+// The kernels of one step for chunk width MT, in stream order.
+template <int MT>
+pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
+  s->launches = 0;
+  pp_status r;
+  if ((r = launch_plain(s, st, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
+                        (int32_t)s->d.capacity, (int32_t)MT, (int32_t)s->V, (int32_t)s->first)))
+    return r;
+  if (s->first)
+    if ((r = launch_plain(s, st, true, dim3(MT), dim3(256), 0, embed_kernel, (const uint16_t*)s->embed,
+                          (int32_t)s->Hp, (int32_t)s->V, s->x, (int32_t)s->Hp,
+                          (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity,
+                          (int32_t)MT)))
+      return r;
+  const int vi = variant_of(MT);
+  for (int l = 0; l < s->nl; ++l) {
+    LayerDev& Ld = s->L[l];
+    GemvArgs a = {};
+    a.desc = s->d_desc;
+    a.res = s->d_res;
+    a.partials = s->gpart;
+    a.tile_cnt = s->tile_cnt;
+    a.recs = s->recs;
+    a.done_cnt = s->done;
+    a.eps = s->d.cfg.rms_norm_eps;
+    a.capacity = (int32_t)s->d.capacity;
+    a.q_dim = s->Q;
+    a.kv_dim = s->KV;
+    a.head_dim = s->hd;
+    // QKV with the input norm, QK-norm, RoPE and KV write.
+    GemvArgs q = a;
+    q.n_out = s->Q + 2 * s->KV;
+    q.n_packed = (int32_t)s->qkv_rows;
+    q.k = s->H;
+    q.kp = (int32_t)s->Hp;
+    q.tiles = (int32_t)(s->qkv_rows / kTileRows);
+    q.kchunks = (int32_t)(s->Hp / kChunkK);
+    q.x = s->x;
+    q.ldx = (int32_t)s->Hp;
+    q.norm_w = Ld.norm[N_ATTN];
+    q.check_input = (!s->first && l == 0) ? 1 : 0;
+    q.out = s->qbuf;
+    q.ldo = s->Q;
+    q.qn = Ld.norm[N_QN];
+    q.kn = Ld.norm[N_KN];
+    q.rope = s->rope;
+    q.kcache = Ld.kc;
+    q.vcache = Ld.vc;
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_QKV>(s, st, Ld.tm_qkv, Ld.tm_qkv, q))) return r;
+    // Attention.
+    AttnArgs at = {};
+    at.q = s->qbuf;
+    at.kcache = Ld.kc;
+    at.vcache = Ld.vc;
+    at.part = s->apart;
+    at.out = s->attn;
+    at.n_heads = s->nh;
+    at.n_kv = s->nkv;
+    at.head_dim = s->hd;
+    at.capacity = (int32_t)s->d.capacity;
+    at.splits = s->splits;
+    at.q_dim = (int32_t)s->Qp;
+    at.nq_max = s->nq_max;
+    at.scale = sqrtf((float)s->hd);
+    at.desc = s->d_desc;
+    at.res = s->d_res;
+    AttnArgs atq = at;
+    atq.q_dim = s->Q;  // the query buffer is [rows][Q]
+    {
+      // Split kernel reads q with stride Q; combine writes attn with stride Qp.
+      const size_t smem = attn_smem_bytes(s->hd);
+      if ((r = launch_plain(s, st, true, dim3(s->nkv, s->splits), dim3(kAttnThreads), smem,
+                            attn_split_kernel<MT>, atq)))
+        return r;
+      const int tb = s->hd < 32 ? 32 : s->hd;
+      if ((r = launch_plain(s, st, true, dim3(s->nh, MT), dim3(tb), 0, attn_combine_kernel<MT>, at)))
+        return r;
+    }
+    // O projection + residual.
+    GemvArgs o = a;
+    o.n_out = s->H;
+    o.n_packed = (int32_t)s->o_rows;
+    o.k = s->Q;
+    o.kp = (int32_t)s->Qp;
+    o.tiles = (int32_t)(s->o_rows / kTileRows);
+    o.kchunks = (int32_t)(s->Qp / kChunkK);
+    o.out = s->x;
+    o.ldo = (int32_t)s->Hp;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.tm_o, s->tm_x_attn[vi], o))) return r;
+    // gate/up with the post-attention norm and SwiGLU.
+    GemvArgs g = a;
+    g.n_out = s->I;
+    g.n_packed = (int32_t)s->gu_rows;
+    g.k = s->H;
+    g.kp = (int32_t)s->Hp;
+    g.tiles = (int32_t)(s->gu_rows / kTileRows);
+    g.kchunks = (int32_t)(s->Hp / kChunkK);
+    g.x = s->x;
+    g.ldx = (int32_t)s->Hp;
+    g.norm_w = Ld.norm[N_FFN];
+    g.out = s->act;
+    g.ldo = (int32_t)s->Ip;
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_SWIGLU>(s, st, Ld.tm_gu, Ld.tm_gu, g))) return r;
+    // down + residual.
+    GemvArgs dn = a;
+    dn.n_out = s->H;
+    dn.n_packed = (int32_t)s->d_rows;
+    dn.k = s->I;
+    dn.kp = (int32_t)s->Ip;
+    dn.tiles = (int32_t)(s->d_rows / kTileRows);
+    dn.kchunks = (int32_t)(s->Ip / kChunkK);
+    dn.out = s->x;
+    dn.ldo = (int32_t)s->Hp;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.tm_d, s->tm_x_act[vi], dn))) return r;
+  }
+  if (s->last) {
+    GemvArgs h = {};
+    h.desc = s->d_desc;
+    h.res = s->d_res;
+    h.partials = s->gpart;
+    h.tile_cnt = s->tile_cnt;
+    h.recs = s->recs;
+    h.done_cnt = s->done;
+    h.eps = s->d.cfg.rms_norm_eps;
+    h.capacity = (int32_t)s->d.capacity;
+    h.n_out = s->V;
+    h.n_packed = (int32_t)s->Vp;
+    h.k = s->H;
+    h.kp = (int32_t)s->Hp;
+    h.tiles = (int32_t)(s->Vp / kTileRows);
+    h.kchunks = (int32_t)(s->Hp / kChunkK);
+    h.x = s->x;
+    h.ldx = (int32_t)s->Hp;
+    h.norm_w = s->final_norm;
+    h.check_input = (!s->first && s->nl == 0) ? 1 : 0;
+    h.logits = s->logits;
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_ARGMAX>(s, st, s->tm_embed, s->tm_embed, h)))
+      return r;
+  }
+  return PP_OK;
+}
+
+template <int MT>
+pp_status set_attrs_mt(pp_shard* s) {
+  const int big = 227 * 1024;
+  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_QKV>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_STREAM, EPI_RESADD>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_SWIGLU>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_ARGMAX>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  CK(cudaFuncSetAttribute(attn_split_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)attn_smem_bytes(kMaxHeadDim)));
+  return PP_OK;
+}
+
+pp_status set_attrs(pp_shard* s) {
+  pp_status r;
+  if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
+      (r = set_attrs_mt<8>(s)))
+    return r;
+  return PP_OK;
+}
+
+pp_status enqueue_variant(pp_shard* s, int vi, cudaStream_t st) {
+  pp_status r;
+  switch (vi) {
+    case 0: r = enqueue_step<1>(s, st); break;
+    case 1: r = enqueue_step<2>(s, st); break;
+    case 2: r = enqueue_step<4>(s, st); break;
+    default: r = enqueue_step<8>(s, st); break;
+  }
+  s->variant_launches[vi] = s->launches;
+  return r;
+}
+
+// Launch one step of width variant vi on stream st: graph replay, or direct launches.
+pp_status run_step(pp_shard* s, int vi, cudaStream_t st) {
+  if (pp_shard_missing(s, nullptr, 0))
+    return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
+  s->last_variant = vi;
+  if (!s->use_graphs) return enqueue_variant(s, vi, st);
+  if (!s->exec[vi]) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    pp_status r = enqueue_variant(s, vi, s->stream);
+    cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+    if (r) {
+      if (g) cudaGraphDestroy(g);
+      return r;
+    }
+    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&s->exec[vi], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  }
+  CK(cudaGraphLaunch(s->exec[vi], st));
+  s->last_variant = vi;
+  return PP_OK;
+}
+
+pp_status status_of(pp_shard* s, const StepResult& r) {
+  if (r.status & ST_TIMEOUT) return fail(s, PP_E_TIMEOUT, "a bounded device wait expired");
+  if (r.status & ST_BAD_STEP) return fail(s, PP_E_INVALID, "invalid step header");
+  if (r.status & ST_NONFINITE_IN) return fail(s, PP_E_INVALID, "invalid hidden input");
+  if (r.status & ST_NONFINITE_OUT)
+    return fail(s, PP_E_NONFINITE, "the shard produced missing or non-finite logits");
+  return PP_OK;
+}
+
+void fill_verify(pp_shard* s, uint32_t m, pp_verify_out* v) {
+  const StepResult& r = *s->h_res;
+  for (uint32_t i = 0; i < m; ++i) {
+    if (v->argmax) v->argmax[i] = r.argmax[i];
+    if (v->top1) v->top1[i] = r.top1[i];
+    if (v->top2) v->top2[i] = r.top2[i];
+  }
+  v->n_accepted = r.n_accepted;
+  v->correction = r.correction;
+  v->nonfinite_rows = r.nonfinite_rows;
+}
+
+pp_status check_step(pp_shard* s, uint32_t pos, uint32_t m) {
+  // src/qwen/model.rs:373-381
+  if (m == 0 || (uint64_t)pos + m > s->d.capacity)
+    return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
+  if (s->d.chunk != 0 && m != 1 && m != s->d.chunk)
+    return fail(s, PP_E_INVALID, "unsupported verify chunk size");
+  if (m > 8) return fail(s, PP_E_UNSUPPORTED, "chunks above 8 rows are not built");
+  return PP_OK;
+}
+
+// Common tail of the host-buffer forwards: enqueue, copy out, synchronise, report.
+pp_status finish_host_step(pp_shard* s, uint32_t m, float* out_hidden, pp_verify_out* verify) {
+  const int vi = variant_of((int)m);
+  pp_status r = run_step(s, vi, s->stream);
+  if (r) return r;
+  if (!s->last && out_hidden)
+    CK(cudaMemcpy2DAsync(s->h_stage, (size_t)s->H * 4, s->x, (size_t)s->Hp * 4, (size_t)s->H * 4, m,
+                         cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(StepResult), cudaMemcpyDeviceToHost, s->stream));
+  if (s->last && verify && verify->logits)
+    CK(cudaMemcpyAsync(verify->logits, s->logits, (size_t)m * s->V * 4, cudaMemcpyDeviceToHost,
+                       s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  if (!s->last && out_hidden) memcpy(out_hidden, s->h_stage, (size_t)m * s->H * 4);
+  if (s->last && verify) fill_verify(s, m, verify);
+  return status_of(s, *s->h_res);
+}
+
+// ---- minimal safetensors header reader ---------------------------------------------------
+struct StEntry {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  int64_t begin = 0, end = 0;
+};
+
+struct JsonCursor {
+  const char* p;
+  const char* e;
+  void ws() {
+    while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  bool str(std::string& out) {
+    ws();
+    if (p >= e || *p != '"') return false;
+    ++p;
+    out.clear();
+    while (p < e && *p != '"') {
+      if (*p == '\\' && p + 1 < e) ++p;
+      out.push_back(*p++);
+    }
+    if (p >= e) return false;
+    ++p;
+    return true;
+  }
+  bool num(int64_t& v) {
+    ws();
+    char* end = nullptr;
+    v = strtoll(p, &end, 10);
+    if (end == p) return false;
+    p = end;
+    return true;
+  }
+  bool skip() {  // skip any value
+    ws();
+    if (p >= e) return false;
+    if (*p == '"') {
+      std::string t;
+      return str(t);
+    }
+    if (*p == '{' || *p == '[') {
+      const char open = *p, close = open == '{' ? '}' : ']';
+      int depth = 0;
+      bool in_str = false;
+      for (; p < e; ++p) {
+        if (in_str) {
+          if (*p == '\\') ++p;
+          else if (*p == '"') in_str = false;
+        } else if (*p == '"') in_str = true;
+        else if (*p == open) ++depth;
+        else if (*p == close && --depth == 0) {
+          ++p;
+          return true;
+        }
+      }
+      return false;
+    }
+    while (p < e && *p != ',' && *p != '}' && *p != ']') ++p;
+    return true;
+  }
+  bool lit(char c) {
+    ws();
+    if (p < e && *p == c) {
+      ++p;
+      return true;
+    }
+    return false;
+  }
+};
+
+bool parse_entry(JsonCursor& j, StEntry& out) {
+  if (!j.lit('{')) return false;
+  while (true) {
+    std::string key;
+    if (!j.str(key) || !j.lit(':')) return false;
+    if (key == "dtype") {
+      if (!j.str(out.dtype)) return false;
+    } else if (key == "shape") {
+      if (!j.lit('[')) return false;
+      if (!j.lit(']')) {
+        while (true) {
+          int64_t v;
+          if (!j.num(v)) return false;
+          out.shape.push_back(v);
+          if (j.lit(']')) break;
+          if (!j.lit(',')) return false;
+        }
+      }
+    } else if (key == "data_offsets") {
+      if (!j.lit('[') || !j.num(out.begin) || !j.lit(',') || !j.num(out.end) || !j.lit(']'))
+        return false;
+    } else if (!j.skip()) {
+      return false;
+    }
+    if (j.lit('}')) return true;
+    if (!j.lit(',')) return false;
+  }
+}
+
+bool parse_header(const char* p, size_t n, std::map<std::string, StEntry>& out) {
+  JsonCursor j{p, p + n};
+  if (!j.lit('{')) return false;
+  if (j.lit('}')) return true;
+  while (true) {
+    std::string name;
+    if (!j.str(name) || !j.lit(':')) return false;
+    if (name == "__metadata__") {
+      if (!j.skip()) return false;
+    } else {
+      StEntry en;
+      if (!parse_entry(j, en)) return false;
+      out[name] = en;
+    }
+    if (j.lit('}')) return true;
+    if (!j.lit(',')) return false;
+  }
+}
+
+}  // namespace
+
+// =========================================================================== C ABI
+extern "C" {
+
+const char* pp_version(void) { return "potpori_b200 0.1 (sm_100a)"; }
+
+size_t pp_last_error(const pp_shard* s, char* buf, size_t len) {
+  const std::string& e = s ? s->err : g_create_error;
+  if (buf && len) {
+    size_t n = e.size() < len - 1 ? e.size() : len - 1;
+    memcpy(buf, e.data(), n);
+    buf[n] = 0;
+  }
+  return e.size();
+}
+
+void pp_shard_destroy(pp_shard* s) {
+  if (!s) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(s->dev);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  for (auto& e : s->exec)
+    if (e) cudaGraphExecDestroy(e);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->h_desc) cudaFreeHost(s->h_desc);
+  if (s->h_res) cudaFreeHost(s->h_res);
+  if (s->h_stage) cudaFreeHost(s->h_stage);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  cudaSetDevice(prev);
+  delete s;
+}
+
+static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
+  const pp_config& c = desc->cfg;
+  s->d = *desc;
+  s->H = c.hidden;
+  s->nh = c.n_heads;
+  s->nkv = c.n_kv_heads;
+  s->hd = c.head_dim;
+  s->Q = c.n_heads * c.head_dim;
+  s->KV = c.n_kv_heads * c.head_dim;
+  s->I = c.intermediate;
+  s->V = c.vocab_size;
+  s->G = c.n_heads / c.n_kv_heads;
+  s->first = desc->layer_begin == 0;
+  s->last = desc->layer_end == c.layers;
+  s->nl = desc->layer_end - desc->layer_begin;
+  s->Hp = round_up(s->H, kChunkK);
+  s->Qp = round_up(s->Q, kChunkK);
+  s->Ip = round_up(s->I, kChunkK);
+  s->Vp = round_up(s->V, kTileRows);
+  s->qkv_rows = round_up(s->Q + 2 * s->KV, kTileRows);
+  s->o_rows = round_up(s->H, kTileRows);
+  s->gu_rows = round_up(s->I, kTileRows / 2) * 2;
+  s->d_rows = round_up(s->H, kTileRows);
+  s->dev = desc->cuda_device;
+  CK(cudaSetDevice(s->dev));
+  CK(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->dev));
+  s->max_grid = s->num_sms;
+  CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  pp_status r0 = set_attrs(s);
+  if (r0) return r0;
+  s->splits = s->num_sms / s->nkv > 0 ? s->num_sms / s->nkv : 1;
+  s->nq_max = s->G * 8;
+  pp_status r;
+  s->L.resize(s->nl);
+  for (int l = 0; l < s->nl; ++l) {
+    LayerDev& Ld = s->L[l];
+    if ((r = dalloc(s, &Ld.wqkv, (size_t)s->qkv_rows * s->Hp * 2))) return r;
+    if ((r = dalloc(s, &Ld.wo, (size_t)s->o_rows * s->Qp * 2))) return r;
+    if ((r = dalloc(s, &Ld.wgu, (size_t)s->gu_rows * s->Hp * 2))) return r;
+    if ((r = dalloc(s, &Ld.wd, (size_t)s->d_rows * s->Ip * 2))) return r;
+    if ((r = dalloc(s, &Ld.norm[N_ATTN], (size_t)s->H * 4))) return r;
+    if ((r = dalloc(s, &Ld.norm[N_QN], (size_t)s->hd * 4))) return r;
+    if ((r = dalloc(s, &Ld.norm[N_KN], (size_t)s->hd * 4))) return r;
+    if ((r = dalloc(s, &Ld.norm[N_FFN], (size_t)s->H * 4))) return r;
+    if ((r = dalloc(s, &Ld.kc, (size_t)s->KV * desc->capacity * 4))) return r;
+    if ((r = dalloc(s, &Ld.vc, (size_t)s->KV * desc->capacity * 4))) return r;
+    if ((r = make_wmap(s, &Ld.tm_qkv, Ld.wqkv, s->Hp, s->qkv_rows))) return r;
+    if ((r = make_wmap(s, &Ld.tm_o, Ld.wo, s->Qp, s->o_rows))) return r;
+    if ((r = make_wmap(s, &Ld.tm_gu, Ld.wgu, s->Hp, s->gu_rows))) return r;
+    if ((r = make_wmap(s, &Ld.tm_d, Ld.wd, s->Ip, s->d_rows))) return r;
+  }
+  if (s->first || s->last) {
+    if ((r = dalloc(s, &s->embed, (size_t)s->Vp * s->Hp * 2))) return r;
+    if ((r = make_wmap(s, &s->tm_embed, s->embed, s->Hp, s->Vp))) return r;
+  }
+  if (s->last && (r = dalloc(s, &s->final_norm, (size_t)s->H * 4))) return r;
+  // RoPE table, src/qwen/model.rs:397-402 / tiny.rs:29-30: angle = pos * theta^(-2i/d).
+  {
+    const int half = s->hd / 2;
+    std::vector<float2> tab((size_t)desc->capacity * half);
+    for (uint32_t p = 0; p < desc->capacity; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double ang = (double)p * pow((double)c.rope_theta, -2.0 * i / (double)s->hd);
+        tab[(size_t)p * half + i] = make_float2((float)cos(ang), (float)sin(ang));
+      }
+    if ((r = dalloc(s, &s->rope, tab.size() * sizeof(float2)))) return r;
+    CK(cudaMemcpyAsync(s->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                       s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+  }
+  if ((r = dalloc(s, &s->x, (size_t)kMaxRows * s->Hp * 4))) return r;
+  if ((r = dalloc(s, &s->qbuf, (size_t)kMaxRows * s->Q * 4))) return r;
+  if ((r = dalloc(s, &s->attn, (size_t)kMaxRows * s->Qp * 4))) return r;
+  if ((r = dalloc(s, &s->act, (size_t)kMaxRows * s->Ip * 4))) return r;
+  if (s->last && (r = dalloc(s, &s->logits, (size_t)kMaxRows * s->V * 4))) return r;
+  if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 2) * 4))) return r;
+  if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * 8 * 4))) return r;
+  {
+    int64_t max_tiles = s->Vp / kTileRows;
+    const int64_t cand[4] = {s->qkv_rows, s->o_rows, s->gu_rows, s->d_rows};
+    for (int64_t v : cand) max_tiles = v / kTileRows > max_tiles ? v / kTileRows : max_tiles;
+    if ((r = dalloc(s, &s->tile_cnt, (size_t)max_tiles * 4))) return r;
+  }
+  if ((r = dalloc(s, &s->recs, (size_t)s->max_grid * 8 * sizeof(ArgRec)))) return r;
+  if ((r = dalloc(s, &s->done, 64))) return r;
+  if ((r = dalloc(s, &s->d_desc, sizeof(StepDesc)))) return r;
+  if ((r = dalloc(s, &s->d_res, sizeof(StepResult)))) return r;
+  CK(cudaMallocHost(&s->h_desc, sizeof(StepDesc)));
+  CK(cudaMallocHost(&s->h_res, sizeof(StepResult)));
+  CK(cudaMallocHost(&s->h_stage, (size_t)kMaxRows * s->H * 4));
+  memset(s->h_desc, 0, sizeof(StepDesc));
+  for (int v = 0; v < kVariants; ++v) {
+    const uint32_t w = (uint32_t)width_of(v);
+    if ((r = make_map(s, &s->tm_x_attn[v], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s->attn, s->Qp, kMaxRows,
+                      4, kChunkK, w, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return r;
+    if ((r = make_map(s, &s->tm_x_act[v], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s->act, s->Ip, kMaxRows,
+                      4, kChunkK, w, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return r;
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_create(const pp_shard_desc* desc, pp_shard** out) {
+  pp_shard* s = nullptr;
+  if (!desc || !out) return fail(nullptr, PP_E_INVALID, "null argument");
+  *out = nullptr;
+  const pp_config& c = desc->cfg;
+  // src/qwen/model.rs:206-217
+  if (!(desc->layer_begin < desc->layer_end && desc->layer_end <= c.layers))
+    return fail(nullptr, PP_E_INVALID, "invalid shard layer range");
+  if (!(desc->capacity > 0 && desc->capacity <= 0x7fffffffu && desc->chunk <= desc->capacity))
+    return fail(nullptr, PP_E_INVALID, "invalid cache/chunk capacity");
+  if (c.n_kv_heads == 0 || c.n_heads % c.n_kv_heads || c.head_dim % 4 || c.head_dim > 128 ||
+      128 % c.head_dim || c.hidden == 0 || c.intermediate == 0 || c.vocab_size == 0)
+    return fail(nullptr, PP_E_UNSUPPORTED, "unsupported geometry");
+  if ((c.n_heads / c.n_kv_heads) * 8 > 32)
+    return fail(nullptr, PP_E_UNSUPPORTED, "more than 4 query heads per KV head");
+  if (desc->chunk > 8) return fail(nullptr, PP_E_UNSUPPORTED, "chunks above 8 rows are not built");
+  if (!encode_fn()) return fail(nullptr, PP_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  s = new pp_shard();
+  int prev = 0;
+  cudaGetDevice(&prev);
+  pp_status r = create_impl(desc, s);
+  if (r) {
+    g_create_error = s->err;
+    pp_shard_destroy(s);
+    cudaSetDevice(prev);
+    return r;
+  }
+  *out = s;
+  return PP_OK;
+}
+
+int32_t pp_shard_missing(const pp_shard* s, char* buf, size_t len) {
+  int n = 0;
+  std::string names;
+  auto miss = [&](const std::string& nm) {
+    ++n;
+    names += nm + ";";
+  };
+  if ((s->first || s->last) && !s->embed_set) miss("model.embed_tokens.weight");
+  if (s->last && !s->final_norm_set) miss("model.norm.weight");
+  for (int l = 0; l < s->nl; ++l) {
+    const int gl = (int)s->d.layer_begin + l;
+    for (int m = 0; m < M_COUNT; ++m)
+      if (!s->L[l].mat_set[m]) miss("model.layers." + std::to_string(gl) + "." + kMatNames[m] + ".weight");
+    for (int m = 0; m < N_COUNT; ++m)
+      if (!s->L[l].norm_set[m]) miss("model.layers." + std::to_string(gl) + "." + kNormNames[m] + ".weight");
+  }
+  if (buf && len) {
+    size_t k = names.size() < len - 1 ? names.size() : len - 1;
+    memcpy(buf, names.data(), k);
+    buf[k] = 0;
+  }
+  return n;
+}
+
+// Resolve a checkpoint name to this shard's destination.
+struct Target {
+  bool mine = false;
+  bool is_norm = false;
+  uint16_t* mat = nullptr;
+  float* norm = nullptr;
+  int64_t rows = 0, cols = 0, ld = 0;
+  RowMap map{1, 0, 0};
+  bool* flag = nullptr;
+};
+
+static pp_status resolve(pp_shard* s, const char* name, Target& t) {
+  const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
+  if (!strcmp(name, "model.embed_tokens.weight")) {
+    if (!(s->first || s->last)) return PP_OK;
+    t = Target{true, false, s->embed, nullptr, s->V, H, s->Hp, RowMap{(int32_t)s->V, 0, 0}, &s->embed_set};
+    return PP_OK;
+  }
+  if (!strcmp(name, "model.norm.weight")) {
+    if (!s->last) return PP_OK;
+    t = Target{true, true, nullptr, s->final_norm, 1, H, H, RowMap{1, 0, 0}, &s->final_norm_set};
+    return PP_OK;
+  }
+  int layer = -1, off = 0;
+  if (sscanf(name, "model.layers.%d.%n", &layer, &off) != 1 || off == 0)
+    return fail(s, PP_E_INVALID, "unknown parameter %s", name);
+  if (layer < (int)s->d.layer_begin || layer >= (int)s->d.layer_end) {
+    if (layer < 0 || layer >= (int)s->d.cfg.layers)
+      return fail(s, PP_E_INVALID, "unknown parameter %s", name);
+    return PP_OK;
+  }
+  LayerDev& Ld = s->L[layer - s->d.layer_begin];
+  const char* rest = name + off;
+  for (int m = 0; m < M_COUNT; ++m) {
+    std::string full = std::string(kMatNames[m]) + ".weight";
+    if (full != rest) continue;
+    t.mine = true;
+    t.flag = &Ld.mat_set[m];
+    switch (m) {
+      case M_Q: t.mat = Ld.wqkv; t.rows = Q; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)Q, 0, 0}; break;
+      case M_K: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)KV, 0, (int32_t)Q}; break;
+      case M_V: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)KV, 0, (int32_t)(Q + KV)}; break;
+      case M_O: t.mat = Ld.wo; t.rows = H; t.cols = Q; t.ld = s->Qp; t.map = RowMap{(int32_t)H, 0, 0}; break;
+      case M_G: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.ld = s->Hp; t.map = RowMap{kTileRows / 2, kTileRows, 0}; break;
+      case M_U: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.ld = s->Hp; t.map = RowMap{kTileRows / 2, kTileRows, kTileRows / 2}; break;
+      default: t.mat = Ld.wd; t.rows = H; t.cols = I; t.ld = s->Ip; t.map = RowMap{(int32_t)H, 0, 0}; break;
+    }
+    return PP_OK;
+  }
+  for (int m = 0; m < N_COUNT; ++m) {
+    std::string full = std::string(kNormNames[m]) + ".weight";
+    if (full != rest) continue;
+    t.mine = true;
+    t.is_norm = true;
+    t.flag = &Ld.norm_set[m];
+    t.norm = Ld.norm[m];
+    t.rows = 1;
+    t.cols = (m == N_QN || m == N_KN) ? s->hd : H;
+    return PP_OK;
+  }
+  return fail(s, PP_E_INVALID, "unknown parameter %s", name);
+}
+
+pp_status pp_shard_set_tensor(pp_shard* s, const char* name, pp_dtype dtype, const void* data,
+                              uint64_t elements) {
+  if (!s || !name || !data) return fail(s, PP_E_INVALID, "null argument");
+  CK(cudaSetDevice(s->dev));
+  Target t;
+  pp_status r = resolve(s, name, t);
+  if (r || !t.mine) return r;
+  if ((int64_t)elements != t.rows * t.cols)
+    return fail(s, PP_E_INVALID, "shape mismatch for %s: %llu elements, want %lld", name,
+                (unsigned long long)elements, (long long)(t.rows * t.cols));
+  if (t.is_norm) {
+    std::vector<float> v(elements);
+    for (uint64_t i = 0; i < elements; ++i)
+      v[i] = dtype == PP_F32 ? ((const float*)data)[i]
+                             : bits_to_float((uint32_t)((const uint16_t*)data)[i] << 16);
+    CK(cudaMemcpyAsync(t.norm, v.data(), elements * 4, cudaMemcpyHostToDevice, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+  } else {
+    const size_t eb = dtype == PP_F32 ? 4 : 2;
+    void* tmp = nullptr;
+    CK(cudaMalloc(&tmp, elements * eb));
+    cudaError_t e = cudaMemcpyAsync(tmp, data, elements * eb, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) {
+      pack_matrix_kernel<<<1024, 256, 0, s->stream>>>(t.mat, tmp, dtype == PP_F32, t.rows, t.cols,
+                                                      t.ld, t.map);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "upload %s: %s", name, cudaGetErrorString(e));
+  }
+  *t.flag = true;
+  return PP_OK;
+}
+
+pp_status pp_shard_init_random(pp_shard* s, uint64_t seed, float stdv) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  CK(cudaSetDevice(s->dev));
+  std::vector<std::string> names;
+  if (s->first || s->last) names.push_back("model.embed_tokens.weight");
+  if (s->last) names.push_back("model.norm.weight");
+  for (int l = 0; l < s->nl; ++l) {
+    const std::string pre = "model.layers." + std::to_string(s->d.layer_begin + l) + ".";
+    for (int m = 0; m < M_COUNT; ++m) names.push_back(pre + kMatNames[m] + ".weight");
+    for (int m = 0; m < N_COUNT; ++m) names.push_back(pre + kNormNames[m] + ".weight");
+  }
+  const float scale = stdv * (1.0f / 65536.0f);
+  for (const std::string& nm : names) {
+    Target t;
+    pp_status r = resolve(s, nm.c_str(), t);
+    if (r) return r;
+    if (t.is_norm) {
+      fill_f32_kernel<<<64, 256, 0, s->stream>>>(t.norm, t.cols, 1.0f);
+    } else {
+      gen_matrix_kernel<<<2048, 256, 0, s->stream>>>(t.mat, t.rows, t.cols, t.ld, t.map,
+                                                     tensor_key(seed, nm.c_str()), scale);
+    }
+    CK(cudaGetLastError());
+    *t.flag = true;
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_load_safetensors(pp_shard* s, const char* path) {
+  if (!s || !path) return fail(s, PP_E_INVALID, "null argument");
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(s, PP_E_INVALID, "cannot open %s", path);
+  struct stat sb;
+  fstat(fd, &sb);
+  const size_t size = (size_t)sb.st_size;
+  void* mp = size ? mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+  close(fd);
+  if (mp == MAP_FAILED) return fail(s, PP_E_INVALID, "cannot map %s", path);
+  const uint8_t* base = (const uint8_t*)mp;
+  pp_status r = PP_OK;
+  uint64_t hlen = 0;
+  std::map<std::string, StEntry> ents;
+  if (size < 8) {
+    r = fail(s, PP_E_INVALID, "%s: not a safetensors file", path);
+  } else {
+    memcpy(&hlen, base, 8);
+    if (hlen > size - 8 || !parse_header((const char*)base + 8, hlen, ents))
+      r = fail(s, PP_E_INVALID, "%s: bad safetensors header", path);
+  }
+  const uint8_t* data = base + 8 + hlen;
+  const size_t dsize = size - 8 - (size_t)hlen;
+  for (auto it = ents.begin(); r == PP_OK && it != ents.end(); ++it) {
+    const std::string& nm = it->first;
+    const StEntry& en = it->second;
+    Target t;
+    if ((r = resolve(s, nm.c_str(), t))) {
+      if (nm.rfind("model.", 0) != 0) {  // not a model parameter (e.g. lm_head): ignore
+        r = PP_OK;
+        s->err.clear();
+      }
+      continue;
+    }
+    if (!t.mine) continue;
+    int64_t n = 1;
+    for (int64_t v : en.shape) n *= v;
+    if (en.begin < 0 || en.end < en.begin || (size_t)en.end > dsize) {
+      r = fail(s, PP_E_INVALID, "%s: bad data offsets", nm.c_str());
+      break;
+    }
+    const uint8_t* src = data + en.begin;
+    if (en.dtype == "BF16" && (en.end - en.begin) == n * 2) {
+      r = pp_shard_set_tensor(s, nm.c_str(), PP_BF16, src, (uint64_t)n);
+    } else if (en.dtype == "F32" && (en.end - en.begin) == n * 4) {
+      r = pp_shard_set_tensor(s, nm.c_str(), PP_F32, src, (uint64_t)n);
+    } else if (en.dtype == "F16" && (en.end - en.begin) == n * 2) {
+      std::vector<float> f((size_t)n);
+      for (int64_t i = 0; i < n; ++i) {
+        uint16_t hbits;
+        memcpy(&hbits, src + 2 * i, 2);
+        const uint32_t sign = (uint32_t)(hbits >> 15) << 31, ex = (hbits >> 10) & 31, man = hbits & 1023;
+        float v;
+        if (ex == 0) v = ldexpf((float)man, -24);
+        else if (ex == 31) v = man ? NAN : INFINITY;
+        else v = ldexpf((float)(man | 1024), (int)ex - 25);
+        uint32_t u;
+        memcpy(&u, &v, 4);
+        u |= sign;
+        memcpy(&f[i], &u, 4);
+      }
+      r = pp_shard_set_tensor(s, nm.c_str(), PP_F32, f.data(), (uint64_t)n);
+    } else {
+      r = fail(s, PP_E_INVALID, "%s: unsupported dtype %s", nm.c_str(), en.dtype.c_str());
+    }
+  }
+  munmap(mp, size);
+  return r;
+}
+
+pp_status pp_shard_forward_tokens(pp_shard* s, uint32_t pos, const int32_t* tokens, uint32_t m,
+                                  float* out_hidden, pp_verify_out* verify) {
+  if (!s || !tokens) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->first) return fail(s, PP_E_INVALID, "invalid token input");
+  pp_status r = check_step(s, pos, m);
+  if (r) return r;
+  for (uint32_t i = 0; i < m; ++i)  // src/qwen/model.rs:383-389
+    if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
+      return fail(s, PP_E_INVALID, "invalid token input");
+  CK(cudaSetDevice(s->dev));
+  StepDesc& d = *s->h_desc;
+  d.pos = (int32_t)pos;
+  d.m = (int32_t)m;
+  d.n_drafts = (int32_t)m - 1;
+  d.flags = (verify && verify->logits) ? 1 : 0;
+  for (uint32_t i = 0; i < m; ++i) d.tokens[i] = tokens[i];
+  for (uint32_t i = 1; i < m; ++i) d.drafts[i - 1] = tokens[i];
+  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, s->stream));
+  return finish_host_step(s, m, out_hidden, verify);
+}
+
+pp_status pp_shard_forward_hidden(pp_shard* s, uint32_t pos, uint32_t m, const float* hidden,
+                                  const int32_t* drafts, uint32_t n_drafts, float* out_hidden,
+                                  pp_verify_out* verify) {
+  if (!s || !hidden) return fail(s, PP_E_INVALID, "null argument");
+  if (s->first) return fail(s, PP_E_INVALID, "invalid hidden input");
+  pp_status r = check_step(s, pos, m);
+  if (r) return r;
+  if (n_drafts > (uint32_t)kMaxRows || (n_drafts && !drafts))
+    return fail(s, PP_E_INVALID, "invalid drafts");
+  for (size_t i = 0; i < (size_t)m * s->H; ++i)  // src/qwen/model.rs:390-392
+    if (!std::isfinite(hidden[i])) return fail(s, PP_E_INVALID, "invalid hidden input");
+  CK(cudaSetDevice(s->dev));
+  StepDesc& d = *s->h_desc;
+  d.pos = (int32_t)pos;
+  d.m = (int32_t)m;
+  d.n_drafts = (int32_t)n_drafts;
+  d.flags = (verify && verify->logits) ? 1 : 0;
+  for (uint32_t i = 0; i < n_drafts; ++i) d.drafts[i] = drafts[i];
+  memcpy(s->h_stage, hidden, (size_t)m * s->H * 4);
+  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaMemcpy2DAsync(s->x, (size_t)s->Hp * 4, s->h_stage, (size_t)s->H * 4, (size_t)s->H * 4, m,
+                       cudaMemcpyHostToDevice, s->stream));
+  return finish_host_step(s, m, out_hidden, verify);
+}
+
+pp_status pp_shard_set_step(pp_shard* s, uint32_t pos, uint32_t m, const int32_t* tokens,
+                            const int32_t* drafts, uint32_t n_drafts, int32_t want_logits,
+                            void* stream) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  pp_status r = check_step(s, pos, m);
+  if (r) return r;
+  if (n_drafts > (uint32_t)kMaxRows || (n_drafts && !drafts) || (s->first && !tokens))
+    return fail(s, PP_E_INVALID, "invalid step");
+  CK(cudaSetDevice(s->dev));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  // The pinned header may still be in flight from the previous step.
+  CK(cudaStreamSynchronize(st));
+  StepDesc& d = *s->h_desc;
+  d.pos = (int32_t)pos;
+  d.m = (int32_t)m;
+  d.n_drafts = (int32_t)n_drafts;
+  d.flags = want_logits ? 1 : 0;
+  for (uint32_t i = 0; i < m && tokens; ++i) d.tokens[i] = tokens[i];
+  for (uint32_t i = 0; i < n_drafts; ++i) d.drafts[i] = drafts[i];
+  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, st));
+  return PP_OK;
+}
+
+pp_status pp_shard_step_device(pp_shard* s, uint32_t max_rows, void* stream) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (max_rows == 0 || max_rows > 8) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..8");
+  CK(cudaSetDevice(s->dev));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  return run_step(s, variant_of((int)max_rows), st);
+}
+
+pp_status pp_shard_buffers(pp_shard* s, void** hidden, void** header, void** result) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (hidden) *hidden = s->x;
+  if (header) *header = s->d_desc;
+  if (result) *result = s->d_res;
+  return PP_OK;
+}
+
+pp_status pp_shard_read_result(pp_shard* s, uint32_t m, pp_verify_out* verify, void* stream) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  CK(cudaSetDevice(s->dev));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  CK(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(StepResult), cudaMemcpyDeviceToHost, st));
+  if (s->last && verify && verify->logits)
+    CK(cudaMemcpyAsync(verify->logits, s->logits, (size_t)m * s->V * 4, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (verify) fill_verify(s, m, verify);
+  return status_of(s, *s->h_res);
+}
+
+pp_status pp_shard_reset(pp_shard* s) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  CK(cudaSetDevice(s->dev));
+  for (auto& Ld : s->L) {
+    CK(cudaMemsetAsync(Ld.kc, 0, (size_t)s->KV * s->d.capacity * 4, s->stream));
+    CK(cudaMemsetAsync(Ld.vc, 0, (size_t)s->KV * s->d.capacity * 4, s->stream));
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_fill_kv(pp_shard* s, uint64_t seed, uint32_t rows) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (rows > s->d.capacity) return fail(s, PP_E_INVALID, "rows exceed capacity");
+  CK(cudaSetDevice(s->dev));
+  for (int l = 0; l < s->nl; ++l) {
+    const uint64_t key = mix64h(seed * 0x9E3779B97F4A7C15ull ^ (uint64_t)(l + 1));
+    fill_kv_kernel<<<1024, 256, 0, s->stream>>>(s->L[l].kc, s->L[l].vc, rows, s->KV, s->nkv, s->hd,
+                                                s->d.capacity, key);
+    CK(cudaGetLastError());
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+uint32_t pp_shard_capacity(const pp_shard* s) { return s->d.capacity; }
+uint32_t pp_shard_chunk_size(const pp_shard* s) { return s->d.chunk; }
+void pp_shard_range(const pp_shard* s, uint32_t* b, uint32_t* e) {
+  if (b) *b = s->d.layer_begin;
+  if (e) *e = s->d.layer_end;
+}
+uint32_t pp_shard_hidden_dim(const pp_shard* s) { return (uint32_t)s->H; }
+uint32_t pp_shard_vocab_size(const pp_shard* s) { return (uint32_t)s->V; }
+uint32_t pp_shard_model_layers(const pp_shard* s) { return s->d.cfg.layers; }
+uint64_t pp_shard_device_bytes(const pp_shard* s) { return s->bytes; }
+uint32_t pp_shard_last_launches(const pp_shard* s) { return s->variant_launches[s->last_variant]; }
+
+pp_status pp_shard_set_graphs(pp_shard* s, int32_t enabled) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  s->use_graphs = enabled != 0;
+  return PP_OK;
+}
+pp_status pp_shard_set_pdl(pp_shard* s, int32_t enabled) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  s->use_pdl = enabled != 0;
+  for (auto& e : s->exec)
+    if (e) {
+      cudaGraphExecDestroy(e);
+      e = nullptr;
+    }
+  return PP_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,268 @@
+"""One contiguous range of Qwen3 layers on one B200, behind the reference's shard interface.
+
+``Shard`` mirrors ``src/qwen/shard.rs:17-133`` and the ``ShardEngine`` trait of
+``src/node.rs:55-86`` (forward_tokens / forward_hidden / reset / capacity / chunk_size /
+range / hidden_dim / vocab_size / hello) over the C ABI of ``include/potpori_b200.h``.
+The reference's forward returns the full F32 logits of the last shard and picks tokens on
+the host; here the tail also computes the greedy pick, top-2 and the accept compare on the
+device (``verify_*``), so the default path reads back only a few integers per row.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import PPError, check
+from .config import QwenConfig
+
+
+@dataclass
+class VerifyResult:
+    """What the tail returns for one chunk (``src/transport.rs`` VerifyResult + accept)."""
+    argmax: list
+    top1: list
+    top2: list
+    n_accepted: int
+    correction: int
+    nonfinite_rows: int
+    logits: Optional[np.ndarray] = field(default=None, repr=False)
+
+    @property
+    def finite(self) -> bool:
+        return self.nonfinite_rows == 0
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+class Shard:
+    """Layers ``[begin, end)`` of a Qwen3 model with its own F32 KV cache on one device."""
+
+    def __init__(self, cfg: QwenConfig, layer_range: tuple, capacity: int, chunk: int = 8,
+                 device: int = 0):
+        L = _lib.load()
+        self.cfg = cfg
+        self._range = (int(layer_range[0]), int(layer_range[1]))
+        self.first = self._range[0] == 0
+        self.last = self._range[1] == cfg.layers
+        desc = _lib.ShardDesc(
+            _lib.Config(cfg.layers, cfg.hidden, cfg.intermediate, cfg.head_dim, cfg.n_heads,
+                        cfg.n_kv_heads, cfg.vocab_size, cfg.rms_norm_eps, cfg.rope_theta),
+            self._range[0], self._range[1], capacity, chunk, device)
+        h = ctypes.c_void_p()
+        st = L.pp_shard_create(ctypes.byref(desc), ctypes.byref(h))
+        if st != _lib.PP_OK:
+            raise PPError(st, f"invalid shard configuration: {_lib.last_error(None)}")
+        self._h = h
+        self._L = L
+        self.device = device
+        self._vo = _lib.VerifyOut()
+        self._am = np.zeros(16, np.int32)
+        self._t1 = np.zeros(16, np.float32)
+        self._t2 = np.zeros(16, np.float32)
+
+    # ---- construction helpers (Shard::load_chunked, src/qwen/shard.rs:28-52) ----
+    @classmethod
+    def load_chunked(cls, cfg: QwenConfig, layer_range: tuple, first: bool, last: bool, path: str,
+                     capacity: int, search: int = 0, chunk: int = 8, device: int = 0) -> "Shard":
+        """Build the shard for ``layer_range`` and load its parameters from a prepared
+        safetensors file. ``first``/``last`` must match the range (model.rs:210-213);
+        ``search`` is accepted for signature parity (there is no kernel search here)."""
+        if first != (layer_range[0] == 0) or last != (layer_range[1] == cfg.layers):
+            raise PPError(_lib.PP_E_INVALID, "shard role does not match layer range")
+        s = cls(cfg, layer_range, capacity, chunk, device)
+        s.load_safetensors(path)
+        return s
+
+    @classmethod
+    def random(cls, cfg: QwenConfig, layer_range: tuple, capacity: int, chunk: int = 8,
+               seed: int = 0, std: float = 0.02, device: int = 0) -> "Shard":
+        s = cls(cfg, layer_range, capacity, chunk, device)
+        s.init_random(seed, std)
+        return s
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.pp_shard_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    # ---- parameters ----
+    def set_tensor(self, name: str, value: np.ndarray) -> None:
+        value = np.ascontiguousarray(value)
+        if value.dtype == np.float32:
+            dt = _lib.PP_F32
+        elif value.dtype in (np.uint16, np.int16):
+            dt = _lib.PP_BF16
+        else:
+            raise TypeError(f"{name}: float32 or bf16 bits (uint16) expected, got {value.dtype}")
+        check(self._L.pp_shard_set_tensor(self._h, name.encode(), dt, value.ctypes.data, value.size),
+              self._h, f"set_tensor {name}")
+
+    def load(self, tensors: dict) -> None:
+        for name, value in tensors.items():
+            self.set_tensor(name, value)
+
+    def load_safetensors(self, path: str) -> None:
+        check(self._L.pp_shard_load_safetensors(self._h, str(path).encode()), self._h,
+              f"load {path}")
+
+    def init_random(self, seed: int, std: float = 0.02) -> None:
+        check(self._L.pp_shard_init_random(self._h, seed, std), self._h, "init_random")
+
+    def missing(self) -> list:
+        buf = ctypes.create_string_buffer(1 << 16)
+        self._L.pp_shard_missing(self._h, buf, len(buf))
+        return [s for s in buf.value.decode().split(";") if s]
+
+    def fill_kv(self, seed: int, rows: int) -> None:
+        check(self._L.pp_shard_fill_kv(self._h, seed, rows), self._h, "fill_kv")
+
+    # ---- ShardEngine ----
+    def range(self) -> tuple:
+        return self._range
+
+    def model_layers(self) -> int:
+        return self.cfg.layers
+
+    def hidden_dim(self) -> int:
+        return self.cfg.hidden
+
+    def vocab_size(self) -> int:
+        return self.cfg.vocab_size
+
+    def capacity(self) -> int:
+        return int(self._L.pp_shard_capacity(self._h))
+
+    def chunk_size(self) -> int:
+        return int(self._L.pp_shard_chunk_size(self._h))
+
+    def hello(self, next_layer: int) -> dict:
+        """SessionHello of src/qwen/shard.rs:89-105."""
+        return {"model": self.cfg.hello_model(), "next_layer": next_layer,
+                "max_seq": self.capacity(), "chunk": self.chunk_size(), "taps": []}
+
+    def reset(self) -> None:
+        check(self._L.pp_shard_reset(self._h), self._h, "reset KV")
+
+    def device_bytes(self) -> int:
+        return int(self._L.pp_shard_device_bytes(self._h))
+
+    def last_launches(self) -> int:
+        return int(self._L.pp_shard_last_launches(self._h))
+
+    def set_graphs(self, enabled: bool) -> None:
+        check(self._L.pp_shard_set_graphs(self._h, int(enabled)), self._h)
+
+    def set_pdl(self, enabled: bool) -> None:
+        check(self._L.pp_shard_set_pdl(self._h, int(enabled)), self._h)
+
+    def _verify_struct(self, want_logits: Optional[np.ndarray]):
+        vo = self._vo
+        vo.argmax = self._am.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+        vo.top1 = self._t1.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        vo.top2 = self._t2.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        vo.logits = (want_logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+                     if want_logits is not None else None)
+        return vo
+
+    def _result(self, m: int, logits) -> VerifyResult:
+        vo = self._vo
+        return VerifyResult(self._am[:m].tolist(), self._t1[:m].tolist(), self._t2[:m].tolist(),
+                            int(vo.n_accepted), int(vo.correction), int(vo.nonfinite_rows), logits)
+
+    def _run(self, pos: int, tokens, hidden, drafts, want_logits: bool):
+        cfg = self.cfg
+        if self.first:
+            tok = _i32(tokens)
+            m = tok.size
+        else:
+            hid = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32)).reshape(-1)
+            m = hid.size // cfg.hidden
+        out_h = None if self.last else np.empty((m, cfg.hidden), np.float32)
+        logits = np.empty((m, cfg.vocab_size), np.float32) if (self.last and want_logits) else None
+        vo = self._verify_struct(logits) if self.last else None
+        vp = ctypes.byref(vo) if vo is not None else None
+        hp = out_h.ctypes.data if out_h is not None else None
+        if self.first:
+            st = self._L.pp_shard_forward_tokens(
+                self._h, pos, tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), m, hp, vp)
+        else:
+            d = _i32(drafts if drafts is not None else [])
+            st = self._L.pp_shard_forward_hidden(
+                self._h, pos, m, hid.ctypes.data,
+                d.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if d.size else None, d.size, hp, vp)
+        if st not in (_lib.PP_OK, _lib.PP_E_NONFINITE):
+            check(st, self._h, f"forward(pos={pos}, m={m})")
+        if self.last:
+            return self._result(m, logits)
+        return out_h
+
+    def forward_tokens(self, pos: int, tokens: Sequence[int]) -> np.ndarray:
+        """First shard (src/node.rs:70): the residual stream ``[s, hidden]``, or the
+        ``[s, vocab]`` logits when this shard is also the last."""
+        out = self._run(pos, tokens, None, None, want_logits=True)
+        return out.logits if self.last else out
+
+    def forward_hidden(self, pos: int, s: int, hidden) -> np.ndarray:
+        """Non-first shard (src/node.rs:73): ``[s, hidden]`` in, ``[s, hidden]`` or logits out."""
+        hid = np.asarray(hidden, dtype=np.float32).reshape(s, self.cfg.hidden)
+        out = self._run(pos, None, hid, None, want_logits=True)
+        return out.logits if self.last else out
+
+    def verify_tokens(self, pos: int, tokens: Sequence[int], logits: bool = False) -> VerifyResult:
+        """First+last shard: on-device greedy pick for every row of the chunk and the accept
+        compare of drafts = tokens[1:] (src/specdecode.rs:92-98)."""
+        return self._run(pos, tokens, None, None, want_logits=logits)
+
+    def verify_hidden(self, pos: int, hidden, drafts: Sequence[int] = (),
+                      logits: bool = False) -> VerifyResult:
+        return self._run(pos, None, hidden, drafts, want_logits=logits)
+
+    # ---- device-resident stage path (in-box pipeline) ----
+    def buffers(self) -> tuple:
+        """Device pointers (hidden, header, result) of the shard's resident buffers."""
+        h, d, r = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        check(self._L.pp_shard_buffers(self._h, ctypes.byref(h), ctypes.byref(d), ctypes.byref(r)),
+              self._h)
+        return h.value, d.value, r.value
+
+    def set_step(self, pos: int, m: int, tokens=None, drafts=(), want_logits=False,
+                 stream: int = 0) -> None:
+        t = _i32(tokens) if tokens is not None else None
+        d = _i32(drafts)
+        check(self._L.pp_shard_set_step(
+            self._h, pos, m, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if t is not None else None,
+            d.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if d.size else None, d.size,
+            int(want_logits), stream or None), self._h, "set_step")
+
+    def step_device(self, max_rows: int, stream: int = 0) -> None:
+        check(self._L.pp_shard_step_device(self._h, max_rows, stream or None), self._h, "step")
+
+    def read_result(self, m: int, stream: int = 0, logits: bool = False) -> VerifyResult:
+        lg = np.empty((m, self.cfg.vocab_size), np.float32) if logits else None
+        vo = self._verify_struct(lg)
+        st = self._L.pp_shard_read_result(self._h, m, ctypes.byref(vo), stream or None)
+        if st not in (_lib.PP_OK, _lib.PP_E_NONFINITE):
+            check(st, self._h, "read_result")
+        return self._result(m, lg)

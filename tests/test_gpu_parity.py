@@ -1,0 +1,202 @@
+"""Parity of the sm_100a verify pass with the oracle and the reference's golden vectors.
+
+Every test here runs the CUDA path through the C ABI (potpori_b200/libpotpori_b200.so) and
+checks it against the oracle (a CPU restatement of the reference math) or the reference's own
+fixtures. Tolerances: the reference's own bounds where it has them (2e-4 for the tiny model,
+src/qwen/tiny.rs:225; 2e-3 against transformers, src/qwen/cpu_check.rs:268-270); per-layer
+hidden states rel-L2 <= 1e-3 and token identity except where the oracle's top-2 logit gap is
+below 1e-3 for the Qwen3 geometries.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import load_fixture, rel_l2, tiny_weights
+from potpori_b200._lib import PP_E_INVALID, PP_E_NONFINITE, PPError
+from potpori_b200.config import QWEN3_0_6B, QWEN3_4B, TINY
+from potpori_b200.shard import Shard
+
+pytestmark = pytest.mark.gpu
+
+TIE_GAP = 1e-3
+
+
+def test_tiny_shards_and_rollback(gpu):
+    """src/qwen/tiny.rs:136-249 on the device: the whole model against the oracle, a 2-shard
+    cut against the whole model, and a rolled-back cache against a fresh one (2e-4)."""
+    cfg, W = TINY, tiny_weights()
+    full, head, tail = (Shard(cfg, r, 8, 2) for r in [(0, 2), (0, 1), (1, 2)])
+    for s in (full, head, tail):
+        s.load(W)
+        assert not s.missing()
+    ref = oracle.OracleShard(cfg, 0, 2, 8, 2)
+    ref.load(W)
+    rollback = None
+    for pos, toks in [(0, [1]), (1, [2, 3]), (1, [4, 5]), (3, [6])]:
+        got = full.forward_tokens(pos, toks)
+        want = ref.forward(pos, tokens=toks)
+        assert got.shape == (len(toks), cfg.vocab_size)
+        assert np.isfinite(got).all()
+        assert np.abs(got - want).max() < 2e-4
+        hidden = head.forward_tokens(pos, toks)
+        cut = tail.forward_hidden(pos, len(toks), hidden)
+        assert np.abs(cut - got).max() < 2e-4
+        if pos == 3:
+            rollback = got
+    full.reset()
+    full.forward_tokens(0, [1])
+    full.forward_tokens(1, [4, 5])
+    clean = full.forward_tokens(3, [6])
+    assert np.abs(rollback - clean).max() < 2e-4
+
+
+def test_fixture_cut_matches_transformers(gpu):
+    """src/qwen/cpu_check.rs:244-275 on the device: the 6-layer fixture cut at the tapped
+    layers into four shards reproduces transformers' logits and layer outputs (2e-3) and the
+    greedy continuation."""
+    cfg, meta, W, want_logits, want_feat = load_fixture()
+    ranges = [(0, 1), (1, 3), (3, 5), (5, 6)]
+    shards = [Shard(cfg, r, 64, 8) for r in ranges]
+    for s in shards:
+        s.load(W)
+        assert not s.missing()
+    seq = meta["sequence"]
+    logits, feats, pos = [], [], 0
+    while pos < len(seq):
+        take = 8 if len(seq) - pos >= 8 else 1
+        h = shards[0].forward_tokens(pos, seq[pos:pos + take])
+        taps = [h]
+        for s in shards[1:]:
+            h = s.forward_hidden(pos, take, h)
+            if not s.last:
+                taps.append(h)
+        logits.append(h)
+        feats.append(np.concatenate(taps, axis=1))
+        pos += take
+    logits = np.concatenate(logits)
+    feats = np.concatenate(feats)
+    assert np.abs(logits - want_logits).max() < 2e-3
+    assert np.abs(feats - want_feat).max() < 2e-3
+    assert [int(np.argmax(r)) for r in logits] == meta["next_tokens"]
+
+
+def _oracle_whole(cfg, seed, capacity, chunk):
+    o = oracle.OracleShard(cfg, 0, cfg.layers, capacity, chunk)
+    o.init_random(seed)
+    return o
+
+
+def test_qwen3_0_6b_per_layer_parity(gpu):
+    """Qwen3-0.6B (seed 0): one device shard per layer, each layer's output against the
+    oracle's (rel-L2 <= 1e-3), then the greedy picks of the last shard."""
+    cfg, seed, cap = QWEN3_0_6B, 0, 128
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, cfg.vocab_size, 41).tolist()
+    shards = [Shard.random(cfg, (l, l + 1), cap, 8, seed=seed) for l in range(cfg.layers)]
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    pos = 0
+    worst = 0.0
+    while pos < len(prompt):
+        take = 8 if len(prompt) - pos >= 8 else 1
+        toks = prompt[pos:pos + take]
+        want_logits, taps = ref.forward(pos, tokens=toks, taps=True)
+        h = shards[0].forward_tokens(pos, toks)
+        for l, s in enumerate(shards[1:], start=1):
+            worst = max(worst, rel_l2(h, taps[l - 1]))
+            assert rel_l2(h, taps[l - 1]) <= 1e-3, (pos, l)
+            if s.last:
+                res = s.verify_hidden(pos, h, drafts=toks[1:], logits=True)
+            else:
+                h = s.forward_hidden(pos, take, h)
+        assert rel_l2(res.logits, want_logits) <= 1e-3
+        for r in range(take):
+            t1, t2 = oracle.top2(want_logits[r])
+            want = oracle.argmax(want_logits[r])
+            if t1 - t2 >= TIE_GAP:
+                assert res.argmax[r] == want, (pos, r)
+            assert res.argmax[r] == int(np.argmax(res.logits[r]))
+            assert abs(res.top1[r] - float(res.logits[r].max())) == 0.0
+        pos += take
+    print(f"worst per-layer rel-L2 {worst:.3e}")
+
+
+def test_qwen3_0_6b_whole_model_verify(gpu):
+    """The production layout: all 28 layers in one shard; argmax, top-2 and the accept
+    compare against the oracle."""
+    cfg, seed, cap = QWEN3_0_6B, 0, 128
+    rng = np.random.default_rng(1)
+    toks_all = rng.integers(0, cfg.vocab_size, 24).tolist()
+    dev = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    for pos in range(0, 24, 8):
+        toks = toks_all[pos:pos + 8]
+        want = ref.forward(pos, tokens=toks)
+        res = dev.verify_tokens(pos, toks, logits=True)
+        assert rel_l2(res.logits, want) <= 1e-3
+        picks = []
+        for r in range(8):
+            t1, t2 = oracle.top2(want[r])
+            if t1 - t2 >= TIE_GAP:
+                assert res.argmax[r] == oracle.argmax(want[r])
+            picks.append(res.argmax[r])
+        # accept compare: drafts = toks[1:] against the device's own picks
+        n = 0
+        while n < 7 and toks[1 + n] == picks[n]:
+            n += 1
+        assert res.n_accepted == n and res.correction == picks[n]
+
+
+@pytest.mark.parametrize("m", [1, 4, 8])
+@pytest.mark.parametrize("kv_len", [128, 2048])
+def test_qwen3_4b_layer_with_rollback(gpu, m, kv_len):
+    """One Qwen3-4B decoder layer (seed 4) over a random warm cache: each step appends m
+    rows and rolls back a random rejected suffix; output against the oracle."""
+    cfg, seed = QWEN3_4B, 4
+    lay = (5, 6)
+    dev = Shard.random(cfg, lay, 4096, 0, seed=seed)
+    ref = oracle.OracleShard(cfg, lay[0], lay[1], 4096, 0)
+    ref.init_random(seed)
+    dev.fill_kv(7, kv_len)
+    ref.fill_kv(7, kv_len)
+    rng = np.random.default_rng(kv_len + m)
+    pos = kv_len
+    for _ in range(3):
+        hidden = rng.standard_normal((m, cfg.hidden)).astype(np.float32)
+        got = dev.forward_hidden(pos, m, hidden)
+        want = ref.forward(pos, hidden=hidden)
+        assert rel_l2(got, want) <= 1e-3
+        pos += m - int(rng.integers(0, m))  # keep a prefix, overwrite the rest next step
+
+
+def test_rejects_invalid_steps(gpu):
+    """src/qwen/model.rs:373-395: chunk size, capacity, token range, finite hidden."""
+    cfg = TINY
+    W = tiny_weights()
+    full = Shard(cfg, (0, 2), 8, 2)
+    full.load(W)
+    tail = Shard(cfg, (1, 2), 8, 2)
+    tail.load(W)
+    for pos, toks in [(0, [1, 2, 3]), (7, [1, 2]), (0, [16]), (0, [-1])]:
+        with pytest.raises(PPError) as e:
+            full.forward_tokens(pos, toks)
+        assert e.value.status == PP_E_INVALID
+    bad = np.zeros((1, cfg.hidden), np.float32)
+    bad[0, 3] = np.nan
+    with pytest.raises(PPError) as e:
+        tail.forward_hidden(0, 1, bad)
+    assert e.value.status == PP_E_INVALID
+    # the shard still works after the rejections
+    assert np.isfinite(full.forward_tokens(0, [1])).all()
+
+
+def test_nonfinite_logits_are_flagged(gpu):
+    """A NaN weight reaches the logits: the tail reports the row as non-finite
+    (src/engine.rs:14-17, src/node.rs:266-272) instead of a token."""
+    cfg = TINY
+    W = tiny_weights()
+    W["model.norm.weight"] = np.full(cfg.hidden, np.nan, np.float32)
+    full = Shard(cfg, (0, 2), 8, 2)
+    full.load(W)
+    res = full.verify_tokens(0, [1, 2])
+    assert res.nonfinite_rows == 0b11
+    assert res.argmax == [-1, -1]
