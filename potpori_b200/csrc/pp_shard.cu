@@ -113,7 +113,7 @@ struct pp_shard {
   int64_t Hp, Qp, Ip, Vp;
   int64_t qkv_rows, o_rows, gu_rows, d_rows;
   int first, last, nl;
-  int dev = 0, num_sms = 148;
+  int dev = 0, num_sms = 148, smem_optin = 0;
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
   uint64_t bytes = 0;
@@ -205,23 +205,31 @@ pp_status make_wmap(pp_shard* s, CUtensorMap* map, uint16_t* base, int64_t cols,
 
 // ---- kernel table ---------------------------------------------------------------------------
 template <int MT, int XM>
-int gemv_stages(int64_t kp) {
+int gemv_stages(int64_t kp, size_t budget) {
   using Lay = GemvSmem<MT, XM>;
-  const size_t budget = 227 * 1024;
   int ns = 12;
   while (ns > 2 && Lay::total(ns, (int)kp) > budget) --ns;
   return ns;
+}
+
+// Dynamic shared memory a kernel may use: the opt-in limit minus its static shared memory.
+template <typename K>
+size_t dyn_smem_limit(pp_shard* s, K kern) {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+  return (size_t)s->smem_optin > fa.sharedSizeBytes ? (size_t)s->smem_optin - fa.sharedSizeBytes : 0;
 }
 
 template <int MT, int XM, int EPI>
 pp_status launch_gemv(pp_shard* s, cudaStream_t st, const CUtensorMap& wmap, const CUtensorMap& xmap,
                       GemvArgs a) {
   using Lay = GemvSmem<MT, XM>;
-  a.nstages = gemv_stages<MT, XM>(a.kp);
-  const size_t smem = Lay::total(a.nstages, a.kp);
-  if (smem > 227 * 1024)
-    return fail(s, PP_E_UNSUPPORTED, "GEMV with K=%d needs %zu bytes of shared memory", a.k, smem);
   auto kern = gemv_kernel<MT, XM, EPI>;
+  const size_t budget = dyn_smem_limit(s, kern);
+  a.nstages = gemv_stages<MT, XM>(a.kp, budget);
+  const size_t smem = Lay::total(a.nstages, a.kp);
+  if (smem > budget)
+    return fail(s, PP_E_UNSUPPORTED, "GEMV with K=%d needs %zu bytes of shared memory", a.k, smem);
   const int64_t T = (int64_t)a.tiles * a.kchunks;
   const int grid = (int)(T < s->max_grid ? T : s->max_grid);
   cudaLaunchConfig_t cfg = {};
@@ -428,19 +436,23 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   return PP_OK;
 }
 
+template <typename K>
+pp_status set_max_smem(pp_shard* s, K kern) {
+  const size_t lim = dyn_smem_limit(s, kern);
+  if (!lim) return fail(s, PP_E_CUDA, "cudaFuncGetAttributes failed");
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lim));
+  return PP_OK;
+}
+
 template <int MT>
 pp_status set_attrs_mt(pp_shard* s) {
-  const int big = 227 * 1024;
-  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_QKV>,
-                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_STREAM, EPI_RESADD>,
-                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_SWIGLU>,
-                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-  CK(cudaFuncSetAttribute(gemv_kernel<MT, X_RESIDENT_NORM, EPI_ARGMAX>,
-                          cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-  CK(cudaFuncSetAttribute(attn_split_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)attn_smem_bytes(kMaxHeadDim)));
+  pp_status r;
+  if ((r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_QKV>)) ||
+      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_RESADD>)) ||
+      (r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_SWIGLU>)) ||
+      (r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_ARGMAX>)) ||
+      (r = set_max_smem(s, attn_split_kernel<MT>)))
+    return r;
   return PP_OK;
 }
 
@@ -717,6 +729,7 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   s->dev = desc->cuda_device;
   CK(cudaSetDevice(s->dev));
   CK(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->dev));
+  CK(cudaDeviceGetAttribute(&s->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, s->dev));
   s->max_grid = s->num_sms;
   CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   pp_status r0 = set_attrs(s);
