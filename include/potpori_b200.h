@@ -103,9 +103,11 @@ pp_status pp_shard_forward_hidden(pp_shard* shard, uint32_t pos, uint32_t m, con
  * of which a peer copy or NCCL receive may fill; no host synchronisation. stream: a
  * cudaStream_t (NULL = the shard's stream). max_rows selects the compiled chunk width. */
 pp_status pp_shard_step_device(pp_shard* shard, uint32_t max_rows, void* stream);
-/* Host-side enqueue of the step header (pos, m, drafts) for pp_shard_step_device. */
+/* Host-side enqueue of the step header (pos, m, tokens, drafts) for pp_shard_step_device.
+ * flags: bit 0 = also write the full logits (last shard); the other bits travel with the
+ * header unchanged (pipeline stages use them to mark a timed window). */
 pp_status pp_shard_set_step(pp_shard* shard, uint32_t pos, uint32_t m, const int32_t* tokens,
-                            const int32_t* drafts, uint32_t n_drafts, int32_t want_logits,
+                            const int32_t* drafts, uint32_t n_drafts, int32_t flags,
                             void* stream);
 /* Device pointers of the shard's resident buffers: hidden [max_rows][hidden] F32 (input of
  * a non-first shard, output of a non-last one), the step header (pp_step_header layout, 144
@@ -113,6 +115,16 @@ pp_status pp_shard_set_step(pp_shard* shard, uint32_t pos, uint32_t m, const int
 pp_status pp_shard_buffers(pp_shard* shard, void** hidden, void** header, void** result);
 /* Read the device step result after a device step (synchronises the stream). */
 pp_status pp_shard_read_result(pp_shard* shard, uint32_t m, pp_verify_out* verify, void* stream);
+
+/* In-box stage handoff (replaces the hidden-state frame of src/node.rs:476-489 and
+ * src/transport.rs:425-489): enqueue on `to`'s stream a copy of `from`'s output rows
+ * [m][hidden] into `to`'s input buffer, ordered after the work already enqueued on `from`
+ * (a peer copy over NVLink when the devices differ). No host synchronisation. */
+pp_status pp_shard_handoff(pp_shard* from, pp_shard* to, uint32_t m);
+/* Enqueue the device-to-host copy of the step result into result slot `slot` (0..63). */
+pp_status pp_shard_result_enqueue(pp_shard* shard, uint32_t slot);
+/* Wait for result slot `slot` and fill `verify` (m rows); the status of that step. */
+pp_status pp_shard_result_wait(pp_shard* shard, uint32_t slot, uint32_t m, pp_verify_out* verify);
 
 /* ShardEngine::reset (src/qwen/runtime/cuda.rs:181-189): KV cache back to zeros. */
 pp_status pp_shard_reset(pp_shard* shard);
@@ -129,6 +141,27 @@ uint32_t pp_shard_vocab_size(const pp_shard* shard);
 uint32_t pp_shard_model_layers(const pp_shard* shard);
 /* Bytes of device memory the handle holds. */
 uint64_t pp_shard_device_bytes(const pp_shard* shard);
+
+/* Kernel kinds reported by pp_shard_profile_kernels. */
+typedef enum pp_kernel_kind {
+  PP_K_BEGIN = 0,        /* step header check */
+  PP_K_EMBED = 1,        /* embedding gather (first shard) */
+  PP_K_QKV = 2,          /* input norm + QKV + QK-norm + RoPE + KV write */
+  PP_K_ATTN = 3,         /* split-KV attention */
+  PP_K_ATTN_COMBINE = 4, /* merge of the splits */
+  PP_K_O = 5,            /* O projection + residual */
+  PP_K_GATE_UP = 6,      /* post-attention norm + gate/up + SwiGLU */
+  PP_K_DOWN = 7,         /* down projection + residual */
+  PP_K_HEAD = 8          /* final norm + vocab projection + argmax/top-2/accept */
+} pp_kernel_kind;
+
+/* Time every kernel of one step: the step is captured into a graph with an event after each
+ * kernel (which also serialises them) and replayed `iters` times; ms[k] is the mean duration
+ * of the k-th kernel and kinds[k] its pp_kernel_kind. *count = kernels per step. */
+pp_status pp_shard_profile_kernels(pp_shard* shard, uint32_t max_rows, uint32_t iters, float* ms,
+                                   int32_t* kinds, uint32_t cap, uint32_t* count);
+/* The shard's own CUDA stream (a cudaStream_t). */
+void* pp_shard_stream(const pp_shard* shard);
 
 /* Kernel launches of the last forward (for the benchmark's launch count). */
 uint32_t pp_shard_last_launches(const pp_shard* shard);

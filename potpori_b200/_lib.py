@@ -25,11 +25,16 @@ EXPORTS = [
     "pp_shard_create", "pp_shard_destroy", "pp_shard_set_tensor", "pp_shard_load_safetensors",
     "pp_shard_init_random", "pp_shard_missing", "pp_shard_forward_tokens",
     "pp_shard_forward_hidden", "pp_shard_step_device", "pp_shard_set_step", "pp_shard_buffers",
-    "pp_shard_read_result", "pp_shard_reset", "pp_shard_fill_kv", "pp_shard_capacity",
+    "pp_shard_read_result", "pp_shard_handoff", "pp_shard_result_enqueue",
+    "pp_shard_result_wait", "pp_shard_reset", "pp_shard_fill_kv", "pp_shard_capacity",
     "pp_shard_chunk_size", "pp_shard_range", "pp_shard_hidden_dim", "pp_shard_vocab_size",
     "pp_shard_model_layers", "pp_shard_device_bytes", "pp_shard_last_launches",
-    "pp_shard_set_graphs", "pp_shard_set_pdl", "pp_last_error", "pp_version",
+    "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
+    "pp_last_error", "pp_version",
 ]
+
+KERNEL_KINDS = ["begin", "embed", "qkv", "attn", "attn_combine", "o_proj", "gate_up", "down",
+                "head"]
 
 
 class PPError(RuntimeError):
@@ -95,6 +100,9 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_step": (I32, [P, U32, U32, pI32, pI32, U32, I32, P]),
         "pp_shard_buffers": (I32, [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)]),
         "pp_shard_read_result": (I32, [P, U32, ctypes.POINTER(VerifyOut), P]),
+        "pp_shard_handoff": (I32, [P, P, U32]),
+        "pp_shard_result_enqueue": (I32, [P, U32]),
+        "pp_shard_result_wait": (I32, [P, U32, U32, ctypes.POINTER(VerifyOut)]),
         "pp_shard_reset": (I32, [P]),
         "pp_shard_fill_kv": (I32, [P, U64, U32]),
         "pp_shard_capacity": (U32, [P]),
@@ -105,6 +113,9 @@ def load() -> ctypes.CDLL:
         "pp_shard_model_layers": (U32, [P]),
         "pp_shard_device_bytes": (U64, [P]),
         "pp_shard_last_launches": (U32, [P]),
+        "pp_shard_profile_kernels": (I32, [P, U32, U32, ctypes.POINTER(F), pI32, U32,
+                                           ctypes.POINTER(U32)]),
+        "pp_shard_stream": (P, [P]),
         "pp_shard_set_graphs": (I32, [P, I32]),
         "pp_shard_set_pdl": (I32, [P, I32]),
         "pp_last_error": (SZ, [P, ctypes.c_char_p, SZ]),

@@ -1,0 +1,86 @@
+"""In-box chains of shards: the reference's head/middle/tail chain (src/node.rs:372-633) with
+the QUIC hop replaced by device-to-device copies.
+
+``LocalChain`` runs every stage in this process (stages may sit on different GPUs; the
+hidden rows move with a peer copy over NVLink, ordered by events, and nothing waits on the
+host until a result is polled). It implements the ``PipelinedChain`` contract of
+src/specpipe.rs:29-43 (submit / poll in FIFO order) and the ``TargetChain`` contract of
+src/engine.rs:55-65 (prefill / verify).
+"""
+from __future__ import annotations
+
+from collections import deque
+from typing import List, Sequence
+
+from .config import is_eos
+from .shard import Shard
+from .target import NonFiniteLogits
+
+RING = 64
+
+
+class LocalChain:
+    def __init__(self, stages: Sequence[Shard]):
+        assert stages and stages[0].first and stages[-1].last
+        for a, b in zip(stages, stages[1:]):
+            assert a.range()[1] == b.range()[0], "stages must be contiguous"
+        self.stages = list(stages)
+        self.chunk = stages[0].chunk_size() or 8
+        self.inflight: deque = deque()
+        self.slot = 0
+        self.submitted = 0
+
+    # ---- PipelinedChain ----
+    def capacity(self) -> int:
+        return min(s.capacity() for s in self.stages)
+
+    def submit(self, start_pos: int, cur: int, drafts: List[int]) -> None:
+        if len(self.inflight) >= RING:
+            raise RuntimeError("too many chunks in flight")
+        tokens = [cur] + list(drafts)
+        m = len(tokens)
+        width = max(self.chunk, m)
+        first, last = self.stages[0], self.stages[-1]
+        first.set_step(start_pos, m, tokens=tokens, drafts=drafts if first.last else ())
+        first.step_device(width)
+        for prev, st in zip(self.stages, self.stages[1:]):
+            st.handoff_from(prev, m)
+            st.set_step(start_pos, m, drafts=drafts if st.last else ())
+            st.step_device(width)
+        last.result_enqueue(self.slot)
+        self.inflight.append((self.slot, m))
+        self.slot = (self.slot + 1) % RING
+        self.submitted += 1
+
+    def poll(self) -> List[int]:
+        slot, m = self.inflight.popleft()
+        r = self.stages[-1].result_wait(slot, m)
+        if not r.finite:
+            raise NonFiniteLogits("the shard produced missing or non-finite logits")
+        return r.argmax
+
+    def prefill(self, prompt: List[int]) -> int:
+        pos = 0
+        while pos < len(prompt):
+            take = self.chunk if len(prompt) - pos >= self.chunk else 1
+            piece = prompt[pos:pos + take]
+            self.submit(pos, piece[0], piece[1:])
+            pos += take
+            while len(self.inflight) > RING // 2:
+                self.poll()
+        last = 0
+        while self.inflight:
+            last = self.poll()[-1]
+        return last
+
+    # ---- TargetChain ----
+    def verify(self, start_pos: int, cur: int, drafts: List[int]) -> List[int]:
+        self.submit(start_pos, cur, drafts)
+        return self.poll()
+
+    def is_eos(self, token: int) -> bool:
+        return is_eos(token)
+
+    def reset(self) -> None:
+        for s in self.stages:
+            s.reset()

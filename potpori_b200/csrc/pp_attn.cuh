@@ -20,7 +20,7 @@ struct AttnArgs {
   const float* kcache;  // [n_kv][capacity][head_dim]
   const float* vcache;
   float* part;          // [n_kv][splits][nq_max][head_dim + 2]
-  float* out;           // [MT][q_dim]
+  uint8_t* out_split;   // attention output rows, split BF16 layout (input of the O GEMV)
   int32_t n_heads, n_kv, head_dim, capacity, splits, q_dim, nq_max;
   float scale;  // sqrt(head_dim); scores are divided by it as in tiny.rs:90
   const StepDesc* desc;
@@ -37,10 +37,12 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Shared memory (floats): qs[32][hdp] | K[2][32][hdp] | V[2][32][hdp] | ps[32][32] | st[3][32]
+constexpr int kAttnStages = 3;  // K/V tiles in flight per CTA (cp.async groups)
+
+// Shared memory (floats): qs[32][hdp] | K[S][32][hdp] | V[S][32][hdp] | ps[32][32] | st[3][32]
 __host__ __device__ inline size_t attn_smem_bytes(int hd) {
   const int hdp = hd + 4;
-  return (size_t)(32 * hdp + 4 * kAttnTile * hdp + 32 * kAttnTile + 3 * 32) * 4;
+  return (size_t)(32 * hdp + 2 * kAttnStages * kAttnTile * hdp + 32 * kAttnTile + 3 * 32) * 4;
 }
 
 template <int MT>
@@ -49,8 +51,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
   const int hd = a.head_dim, hdp = hd + 4;
   float* qs = sm;
   float* ks = qs + 32 * hdp;
-  float* vs = ks + 2 * kAttnTile * hdp;
-  float* ps = vs + 2 * kAttnTile * hdp;
+  float* vs = ks + kAttnStages * kAttnTile * hdp;
+  float* ps = vs + kAttnStages * kAttnTile * hdp;
   float* st_m = ps + 32 * kAttnTile;
   float* st_l = st_m + 32;
 
@@ -108,15 +110,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = 0.f;
 
-  if (t0 < t1) load_tile(0, t0);
+  // kAttnStages - 1 tiles in flight ahead of the one being computed; every iteration
+  // commits exactly one (possibly empty) group so the wait count stays uniform.
+#pragma unroll
+  for (int i = 0; i < kAttnStages - 1; ++i) {
+    if (t0 + i < t1)
+      load_tile(i, t0 + i);
+    else
+      cp_async_commit();
+  }
   for (int tile = t0; tile < t1; ++tile) {
-    const int buf = (tile - t0) & 1;
-    if (tile + 1 < t1) {
-      load_tile(buf ^ 1, tile + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    const int buf = (tile - t0) % kAttnStages;
+    const int nxt = tile + kAttnStages - 1;
+    if (nxt < t1)
+      load_tile((nxt - t0) % kAttnStages, nxt);
+    else
+      cp_async_commit();
+    cp_async_wait<kAttnStages - 1>();
     __syncthreads();
     const float* kt = ks + buf * kAttnTile * hdp;
     const float* vt = vs + buf * kAttnTile * hdp;
@@ -186,8 +196,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         }
       }
     }
-    __syncthreads();  // the buffer is refilled next iteration
+    __syncthreads();  // this buffer is refilled kAttnStages - 1 iterations later
   }
+  cp_async_wait<0>();
 
   __syncthreads();
   // Partial of this split: running max, running sum, unnormalised output.
@@ -224,20 +235,40 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
   const int hd = a.head_dim;
   const size_t stride = (size_t)a.nq_max * (hd + 2);
   const float* base = a.part + ((size_t)h * a.splits * a.nq_max + qi) * (hd + 2);
-  float mx = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, base[s * stride]);
-  float l = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float ms = base[s * stride];
-    if (ms != -INFINITY) l += base[s * stride + 1] * expf(ms - mx);
+  // Per-split (max, sum) pairs are read once into shared memory with independent loads.
+  __shared__ float sm_m[256], sm_w[256];
+  __shared__ float red_l;
+  const int S = a.splits;
+  for (int s = threadIdx.x; s < S; s += blockDim.x) {
+    sm_m[s] = __ldcg(base + s * stride);
+    sm_w[s] = __ldcg(base + s * stride + 1);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mx = -INFINITY;
+    for (int s = 0; s < S; ++s) mx = fmaxf(mx, sm_m[s]);
+    float l = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float f = (sm_m[s] == -INFINITY) ? 0.f : expf(sm_m[s] - mx);
+      l += sm_w[s] * f;
+      sm_w[s] = f;  // now the scale of split s
+    }
+    red_l = l;
+  }
+  __syncthreads();
+  const float inv_l = 1.0f / red_l;
   for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
     float o = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = base[s * stride];
-      if (ms != -INFINITY) o += base[s * stride + 2 + dd] * expf(ms - mx);
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float pv[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        pv[q] = (s0 + q < S && sm_w[s0 + q] != 0.f) ? __ldcg(base + (s0 + q) * stride + 2 + dd) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (s0 + q < S) o += pv[q] * sm_w[s0 + q];
     }
-    a.out[(size_t)r * a.q_dim + hq * hd + dd] = o / l;
+    store_split<MT>(a.out_split, r, hq * hd + dd, o * inv_l);
   }
 }
 

@@ -134,6 +134,61 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Rows of the split activation block: the MMA's N dimension (8, or 16 for 16-row chunks).
+template <int MT>
+struct SplitRows {
+  static constexpr int R = MT <= 8 ? 8 : 16;
+  static constexpr int kBlock = 2 * R * 128;  // bytes per 64-column chunk: [hi|lo][R][128 B]
+};
+
+// Byte offset of element (row m, column k) of a split activation matrix: for each 64-column
+// chunk a block [hi, lo][R rows][64 BF16], the 16-byte unit u of row m stored at u ^ (m & 7)
+// (bank-conflict-free ldmatrix). hi = bf16(v), lo = bf16(v - hi): hi + lo carries v to about
+// 2^-17 relative, and the BF16 products of the MMA are exact in its F32 accumulator.
+template <int MT>
+__host__ __device__ __forceinline__ size_t split_offset(int m, int k, int hl) {
+  constexpr int R = SplitRows<MT>::R;
+  const int c = k >> 6, kk = k & 63;
+  return (size_t)c * SplitRows<MT>::kBlock + (size_t)(hl * R + m) * 128 +
+         ((((kk >> 3) ^ (m & 7))) << 4) + ((kk & 7) << 1);
+}
+
+__device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+  hi = f32_to_bf16_rne(v);
+  lo = f32_to_bf16_rne(v - __uint_as_float((uint32_t)hi << 16));
+}
+
+template <int MT>
+__device__ __forceinline__ void store_split(uint8_t* base, int m, int k, float v) {
+  uint16_t hi, lo;
+  split_bf16(v, hi, lo);
+  *(uint16_t*)(base + split_offset<MT>(m, k, 0)) = hi;
+  *(uint16_t*)(base + split_offset<MT>(m, k, 1)) = lo;
+}
+
+// ---- weight layout ------------------------------------------------------------------------
+// Matrices are stored as the shared-memory image of the GEMV's pipeline stages: for tile t
+// (128 output rows) and K chunk c (64 columns), one contiguous 16 KB block of 128 rows x
+// 128 bytes in which the 16-byte unit u of row r sits at position u ^ (r & 7) (the 128-byte
+// swizzle, so the consumers' row reads are bank-conflict free). Blocks are ordered tile-major,
+// which is the stream-K iteration order: every CTA streams one contiguous range of bytes.
+// Element offset of (row n, column k) with kchunks 64-column chunks per row:
+__host__ __device__ __forceinline__ int64_t tiled_offset(int64_t n, int64_t k, int64_t kchunks) {
+  const int64_t t = n >> 7, r = n & 127, c = k >> 6, kk = k & 63;
+  return (((t * kchunks + c) * 128 + r) << 6) + ((((kk >> 3) ^ (r & 7))) << 3) + (kk & 7);
+}
+
+// One contiguous global -> shared copy on the bulk-copy (TMA) engine, completing on `bar`.
+// 16-byte aligned addresses, size a multiple of 16. Destination is this CTA's own memory.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---- TMA (tiled, no multicast) ------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {

@@ -9,15 +9,17 @@
 //    space is cut into one contiguous, equal range per CTA, so all 148 SMs get the same
 //    number of weight bytes whatever N and K are. A tile split between CTAs is finished
 //    by the last contributor, which sums the partial results in K order (deterministic).
-//  * One producer warp streams [128 x 64] BF16 weight boxes (16 KB, 128-byte swizzle) into
-//    a ring of shared-memory stages with TMA (no multicast) and mbarriers; it starts before
-//    the previous kernel has finished (programmatic dependent launch), since weights do not
-//    depend on it.
-//  * Eight consumer warps: lane = (row r4 in 0..3, 16-byte K slice kq in 0..7); each lane
-//    owns 4 rows x 8 K values per stage and multiplies them into M rows with packed FFMA2
-//    (even/odd K lanes), then an 8-lane shuffle reduction.
+//  * One producer warp streams [128 x 64] BF16 weight blocks (16 KB, stored pre-swizzled in
+//    HBM in stream order) into a ring of shared-memory stages with 1-D bulk copies (TMA
+//    engine, no multicast) and mbarriers; it starts before the previous kernel has finished
+//    (programmatic dependent launch), since weights do not depend on it.
+//  * Eight consumer warps, 16 weight rows each, on the tensor cores: the activation is
+//    carried as two BF16 parts (x = hi + lo, about 2^-17 relative), so D += W.hi + W.lo with
+//    m16n8k16 MMAs into F32 accumulators reproduces the F32 products of BF16 weights (the
+//    CUDA-core FFMA roof is about the HBM roof at M = 8, which this sidesteps).
 //  * x is either resident in shared memory for the whole K (the input RMSNorm is applied
-//    while staging it, src/qwen/tiny.rs:20-23) or streamed next to the weights with TMA.
+//    while staging it, src/qwen/tiny.rs:20-23) or streamed next to the weights as split
+//    blocks that the producing kernel wrote in the MMA's operand layout.
 //  * Fused epilogues: QK-RMSNorm + RoPE + KV write (QKV), residual add (O, down), SwiGLU
 //    (gate/up interleaved in 64-row blocks), and argmax/top-2/accept for the vocab head.
 #pragma once
@@ -36,6 +38,9 @@ struct ArgRec {
 };
 
 struct GemvArgs {
+  const uint16_t* w;       // tiled weights (tiled_offset layout)
+  const uint8_t* xsplit;   // streamed activations, split BF16 blocks (split_offset layout)
+  uint8_t* out_split;      // SwiGLU output in the same split layout (input of the down GEMV)
   int32_t n_out;     // valid output columns (after the SwiGLU pairing: intermediate)
   int32_t n_packed;  // rows of the packed weight matrix
   int32_t k;         // valid K
@@ -73,11 +78,12 @@ struct GemvArgs {
 template <int MT, int XM>
 struct GemvSmem {
   static constexpr int kWBytes = kTileRows * kChunkK * 2;  // 16 KB per stage
-  static constexpr int kXBytes = (XM == X_STREAM) ? MT * kChunkK * 4 : 0;
+  static constexpr int kXBytes = (XM == X_STREAM) ? SplitRows<MT>::kBlock : 0;
   static __host__ __device__ size_t x_off(int ns) { return (size_t)ns * kWBytes; }
   static __host__ __device__ size_t xs_off(int ns) { return x_off(ns) + (size_t)ns * kXBytes; }
   static __host__ __device__ size_t tile_off(int ns, int kp) {
-    return xs_off(ns) + (XM == X_RESIDENT_NORM ? (size_t)MT * kp * 4 : 0);
+    return xs_off(ns) +
+           (XM == X_RESIDENT_NORM ? (size_t)(kp / kChunkK) * SplitRows<MT>::kBlock : 0);
   }
   static __host__ __device__ size_t bar_off(int ns, int kp) {
     return tile_off(ns, kp) + (size_t)kTileRows * MT * 4;
@@ -102,22 +108,39 @@ __device__ __forceinline__ void argrec_merge(float& b1, int32_t& i1, float& s1, 
   }
 }
 
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// D[16 x 8] += A[16 x 16] . B[16 x 8], BF16 inputs, F32 accumulate.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 template <int MT, int XM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1)
-    gemv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
   using L = GemvSmem<MT, XM>;
+  constexpr int R = SplitRows<MT>::R;
+  constexpr int NB = R / 8;  // 8-row MMA column blocks
+  constexpr int XB = SplitRows<MT>::kBlock;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int ns = a.nstages;
   uint8_t* wst = smem;
   uint8_t* xst = smem + L::x_off(ns);
-  float* xs = (float*)(smem + L::xs_off(ns));
+  uint8_t* xs = smem + L::xs_off(ns);
   float* tile_out = (float*)(smem + L::tile_off(ns, a.kp));
   uint64_t* full = (uint64_t*)(smem + L::bar_off(ns, a.kp));
   uint64_t* empty = full + ns;
   int32_t* misc = (int32_t*)(smem + L::misc_off(ns, a.kp));
-  // misc: [0] fixup flag, [1] status bits, [2..] argmax running state (4 x MT words)
+  // misc: [0] fixup flag, [1] status bits, [8..] argmax running state (4 x MT words)
   float* st_best = (float*)(misc + 8);
   int32_t* st_idx = misc + 8 + MT;
   float* st_second = (float*)(misc + 8 + 2 * MT);
@@ -152,34 +175,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   // ------------------------------------------------------------------ producer warp
   if (warp == kConsumerWarps) {
     if (lane == 0) {
-      tma_prefetch_desc(&wmap);
-      if (XM == X_STREAM) tma_prefetch_desc(&xmap);
       const int64_t n_it = i1 - i0;
       const int pre = (int)(n_it < ns ? n_it : ns);
       const uint32_t bytes = L::kWBytes + L::kXBytes;
-      for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
-        const int64_t it = i0 + i;
+      auto wsrc = [&](int64_t it) {
         const int t = (int)(it / a.kchunks), c = (int)(it % a.kchunks);
+        return a.w + ((size_t)t * a.kchunks + c) * (kTileRows * kChunkK);
+      };
+      for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
         mbar_arrive_expect_tx(&full[i], bytes);
-        tma_load_2d(wst + (size_t)i * L::kWBytes, &wmap, &full[i], c * kChunkK, t * kTileRows);
+        bulk_load(wst + (size_t)i * L::kWBytes, wsrc(i0 + i), L::kWBytes, &full[i]);
       }
       pdl_wait();
       if (XM == X_STREAM)
         for (int i = 0; i < pre; ++i) {
           const int c = (int)((i0 + i) % a.kchunks);
-          tma_load_2d(xst + (size_t)i * L::kXBytes, &xmap, &full[i], c * kChunkK, 0);
+          bulk_load(xst + (size_t)i * XB, a.xsplit + (size_t)c * XB, XB, &full[i]);
         }
       int64_t issued = pre;
       for (int64_t i = pre; i < n_it; ++i) {
         const int s = (int)(i % ns);
         const uint32_t use = (uint32_t)(i / ns);
         if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
-        const int64_t it = i0 + i;
-        const int t = (int)(it / a.kchunks), c = (int)(it % a.kchunks);
         mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d(wst + (size_t)s * L::kWBytes, &wmap, &full[s], c * kChunkK, t * kTileRows);
-        if (XM == X_STREAM)
-          tma_load_2d(xst + (size_t)s * L::kXBytes, &xmap, &full[s], c * kChunkK, 0);
+        bulk_load(wst + (size_t)s * L::kWBytes, wsrc(i0 + i), L::kWBytes, &full[s]);
+        if (XM == X_STREAM) {
+          const int c = (int)((i0 + i) % a.kchunks);
+          bulk_load(xst + (size_t)s * XB, a.xsplit + (size_t)c * XB, XB, &full[s]);
+        }
         issued = i + 1;
       }
       if (issued < n_it) {
@@ -196,25 +219,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   pdl_wait();
   const StepDesc& d = *a.desc;
   const int mv = d.m;  // rows that matter; the launch guarantees 1 <= m <= MT
-  const int r4 = lane >> 3, kq = lane & 7;
 
   if (XM == X_RESIDENT_NORM) {
-    // RMSNorm (tiny.rs:20-23): x / sqrt(mean(x^2) + eps) * w, staged as [chunk][m][h][kq][4]
-    // so that the lanes of a warp read 128 contiguous bytes per load.
+    // RMSNorm (tiny.rs:20-23): x * (1 / sqrt(mean(x^2) + eps)) * w, staged for the whole K
+    // as split BF16 blocks (hi, lo) in the MMA's B-operand layout.
     __shared__ float red[kConsumerWarps][MT];
-    __shared__ float rms_s[MT];
+    __shared__ float inv_s[MT];
+    const int k4 = a.k >> 2;
     float ss[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) ss[m] = 0.f;
     int bad = 0;
-    for (int k = tid; k < a.k; k += kConsumerWarps * 32) {
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
-        if (m < mv) {
-          const float v = a.x[(size_t)m * a.ldx + k];
-          bad |= !isfinite(v);
-          ss[m] += v * v;
+    for (int m = 0; m < MT; ++m) {
+      ss[m] = 0.f;
+      if (m < mv) {
+        const float4* xr = (const float4*)(a.x + (size_t)m * a.ldx);
+        for (int q = tid; q < k4; q += kConsumerWarps * 32) {
+          const float4 v = xr[q];
+          bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+          ss[m] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
+      }
     }
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
@@ -226,21 +250,52 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     if (tid < MT) {
       float t = 0.f;
       for (int w = 0; w < kConsumerWarps; ++w) t += red[w][tid];
-      rms_s[tid] = sqrtf(t / (float)a.k + a.eps);
+      inv_s[tid] = 1.0f / sqrtf(t / (float)a.k + a.eps);
     }
     consumer_sync();
-    for (int e = tid; e < MT * a.kp; e += kConsumerWarps * 32) {
-      const int m = e / a.kp, k = e - m * a.kp;
-      float v = 0.f;
-      if (m < mv && k < a.k) v = a.x[(size_t)m * a.ldx + k] / rms_s[m] * a.norm_w[k];
-      const int c = k >> 6, kl = k & 63;
-      const int kqq = kl >> 3, h = (kl >> 2) & 1, e4 = kl & 3;
-      xs[((size_t)(c * MT + m) * 64) + (h * 8 + kqq) * 4 + e4] = v;
+    // One thread per (chunk, row, 16-byte unit): 8 columns -> 8 hi + 8 lo BF16.
+    const int units = a.kchunks * R * 8;
+    for (int e = tid; e < units; e += kConsumerWarps * 32) {
+      const int u = e & 7, m = (e >> 3) % R, c = (e >> 3) / R;
+      const int k0 = c * 64 + u * 8;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      if (m < mv) {
+        const float inv = inv_s[m];
+        const float* xr = a.x + (size_t)m * a.ldx;
+        if (k0 + 8 <= a.k) {
+          const float4 x0 = *(const float4*)(xr + k0), x1 = *(const float4*)(xr + k0 + 4);
+          const float4 w0 = *(const float4*)(a.norm_w + k0), w1 = *(const float4*)(a.norm_w + k0 + 4);
+          v[0] = x0.x * inv * w0.x; v[1] = x0.y * inv * w0.y; v[2] = x0.z * inv * w0.z;
+          v[3] = x0.w * inv * w0.w; v[4] = x1.x * inv * w1.x; v[5] = x1.y * inv * w1.y;
+          v[6] = x1.z * inv * w1.z; v[7] = x1.w * inv * w1.w;
+        } else {
+          for (int j = 0; j < 8; ++j)
+            if (k0 + j < a.k) v[j] = xr[k0 + j] * inv * a.norm_w[k0 + j];
+        }
+      }
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint16_t h0, l0, h1, l1;
+        split_bf16(v[2 * j], h0, l0);
+        split_bf16(v[2 * j + 1], h1, l1);
+        hw[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+      }
+      uint8_t* blk = xs + (size_t)c * XB + (size_t)m * 128 + ((u ^ (m & 7)) << 4);
+      *(uint4*)blk = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *(uint4*)(blk + R * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     consumer_sync();
     if (tid == 0 && misc[1]) atomicOr(&a.res->status, misc[1]);
   }
 
+  // Lane roles for ldmatrix: A (weights) matrix mat = lane >> 3 covers rows (mat & 1) * 8 and
+  // K half (mat >> 1); B (activations) matrix mat covers K step (mat >> 1), half (mat & 1).
+  const int mat = lane >> 3, l7 = lane & 7;
+  const int arow = warp * 16 + l7 + (mat & 1) * 8;
   int64_t it = i0;
   int local = 0;  // iterations consumed so far by this CTA
   bool ok = true;
@@ -248,11 +303,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     const int t = (int)(it / a.kchunks);
     const int64_t tile_begin = (int64_t)t * a.kchunks, tile_end = tile_begin + a.kchunks;
     const int64_t seg_begin = it, seg_end = i1 < tile_end ? i1 : tile_end;
-    float2 acc[4][MT];
+    float acc[NB][4];
 #pragma unroll
-    for (int g = 0; g < 4; ++g)
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int m = 0; m < MT; ++m) acc[g][m] = make_float2(0.f, 0.f);
+      for (int q = 0; q < 4; ++q) acc[nb][q] = 0.f;
 
     for (; it < seg_end; ++it, ++local) {
       const int s = local % ns;
@@ -262,58 +317,50 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       }
       const int c = (int)(it - tile_begin);
       const uint8_t* wb = wst + (size_t)s * L::kWBytes;
-      uint4 wv[4];
+      const uint8_t* xb = (XM == X_STREAM) ? xst + (size_t)s * XB : xs + (size_t)c * XB;
+      uint32_t af[4][4];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int rr = warp * 16 + g * 4 + r4;
-        wv[g] = *(const uint4*)(wb + rr * 128 + ((kq ^ (rr & 7)) << 4));
+      for (int st = 0; st < 4; ++st) {
+        const int u = 2 * st + (mat >> 1);
+        ldmatrix_x4(af[st], wb + arow * 128 + ((u ^ (arow & 7)) << 4));
       }
-      float4 xa[MT], xb[MT];
-      if (XM == X_STREAM) {
-        const float* xb_s = (const float*)(xst + (size_t)s * L::kXBytes);
+      uint32_t bh[NB][2][4], bl[NB][2][4];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          xa[m] = *(const float4*)(xb_s + m * 64 + kq * 8);
-          xb[m] = *(const float4*)(xb_s + m * 64 + kq * 8 + 4);
-        }
-      } else {
-        const float* base = xs + (size_t)c * MT * 64;
+      for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          xa[m] = *(const float4*)(base + m * 64 + kq * 4);
-          xb[m] = *(const float4*)(base + m * 64 + 32 + kq * 4);
+        for (int p = 0; p < 2; ++p) {
+          const int u = 2 * (2 * p + (mat >> 1)) + (mat & 1);
+          const uint8_t* row = xb + (size_t)(nb * 8 + l7) * 128 + ((u ^ l7) << 4);
+          ldmatrix_x4(bh[nb][p], row);
+          ldmatrix_x4(bl[nb][p], row + R * 128);
         }
-      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const float2 w01 = make_float2(bf16lo(wv[g].x), bf16hi(wv[g].x));
-        const float2 w23 = make_float2(bf16lo(wv[g].y), bf16hi(wv[g].y));
-        const float2 w45 = make_float2(bf16lo(wv[g].z), bf16hi(wv[g].z));
-        const float2 w67 = make_float2(bf16lo(wv[g].w), bf16hi(wv[g].w));
+      for (int st = 0; st < 4; ++st)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          ffma2(acc[g][m], w01, make_float2(xa[m].x, xa[m].y));
-          ffma2(acc[g][m], w23, make_float2(xa[m].z, xa[m].w));
-          ffma2(acc[g][m], w45, make_float2(xb[m].x, xb[m].y));
-          ffma2(acc[g][m], w67, make_float2(xb[m].z, xb[m].w));
+        for (int nb = 0; nb < NB; ++nb) {
+          const int p = st >> 1, q = (st & 1) * 2;
+          mma_bf16(acc[nb], af[st], bh[nb][p][q], bh[nb][p][q + 1]);
+          mma_bf16(acc[nb], af[st], bl[nb][p][q], bl[nb][p][q + 1]);
         }
-      }
     }
     if (!ok) break;
 
-    // Sum even/odd lanes and the eight K slices of each row.
+    {  // accumulator fragments -> tile_out[row][m]
+      const int g = lane >> 2, tq = lane & 3;
+      const int r0 = warp * 16 + g;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int rr = warp * 16 + g * 4 + r4;
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float v = acc[g][m].x + acc[g][m].y;
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if ((m & 7) == kq) tile_out[rr * MT + m] = v;
+      for (int nb = 0; nb < NB; ++nb) {
+        const int m0 = nb * 8 + 2 * tq;
+        if (m0 < MT) {
+          tile_out[r0 * MT + m0] = acc[nb][0];
+          tile_out[(r0 + 8) * MT + m0] = acc[nb][2];
+        }
+        if (m0 + 1 < MT) {
+          tile_out[r0 * MT + m0 + 1] = acc[nb][1];
+          tile_out[(r0 + 8) * MT + m0 + 1] = acc[nb][3];
+        }
       }
     }
     consumer_sync();
@@ -334,11 +381,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       consumer_sync();
       if (!misc[0]) continue;
       __threadfence();
+      // Sum the contributors' partials in K order; loads are issued in groups of 8
+      // independent reads so the fixup costs about one L2 round trip per group.
+      const int nbk = (int)(b_hi - b_lo + 1);
       for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
         float v = 0.f;
-        for (int64_t b = b_lo; b <= b_hi; ++b) {
-          const int bslot = (sk_start(b, T, G) / a.kchunks == t) ? 0 : 1;
-          v += __ldcg(a.partials + ((size_t)b * 2 + bslot) * kTileRows * MT + e);
+        for (int b0 = 0; b0 < nbk; b0 += 8) {
+          float pv[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int64_t b = b_lo + b0 + q;
+            pv[q] = 0.f;
+            if (b0 + q < nbk) {
+              const int bslot = (sk_start(b, T, G) / a.kchunks == t) ? 0 : 1;
+              pv[q] = __ldcg(a.partials + ((size_t)b * 2 + bslot) * kTileRows * MT + e);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (b0 + q < nbk) v += pv[q];
         }
         tile_out[e] = v;
       }
@@ -366,7 +427,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const int n = t * half + r;
         if (m < mv && n < a.n_out) {
           const float g = tile_out[r * MT + m], u = tile_out[(r + half) * MT + m];
-          a.out[(size_t)m * a.ldo + n] = g / (1.0f + expf(-g)) * u;  // tiny.rs:111-115
+          store_split<MT>(a.out_split, m, n, g / (1.0f + expf(-g)) * u);  // tiny.rs:111-115
         }
       }
     } else if (EPI == EPI_QKV) {

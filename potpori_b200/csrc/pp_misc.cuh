@@ -7,9 +7,10 @@ namespace pp {
 
 // Embedding rows of the chunk's tokens, BF16 decoded to F32 (src/qwen/model.rs:239-241).
 // Grid (MT); a row past m is left alone.
-__global__ void embed_kernel(const uint16_t* __restrict__ table, int32_t hidden, int32_t vocab,
-                             float* __restrict__ x, int32_t ldx, const StepDesc* desc,
-                             StepResult* res, int32_t capacity, int32_t max_rows) {
+__global__ void embed_kernel(const uint16_t* __restrict__ table, int32_t hidden, int32_t kchunks,
+                             int32_t vocab, float* __restrict__ x, int32_t ldx,
+                             const StepDesc* desc, StepResult* res, int32_t capacity,
+                             int32_t max_rows) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(desc, capacity, max_rows)) return;
   pdl_wait();
@@ -20,9 +21,8 @@ __global__ void embed_kernel(const uint16_t* __restrict__ table, int32_t hidden,
     if (threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
     return;
   }
-  const uint16_t* row = table + (size_t)tok * hidden;
   for (int k = threadIdx.x; k < hidden; k += blockDim.x)
-    x[(size_t)r * ldx + k] = __uint_as_float((uint32_t)row[k] << 16);
+    x[(size_t)r * ldx + k] = __uint_as_float((uint32_t)table[tiled_offset(tok, k, kchunks)] << 16);
 }
 
 // ---- seeded generator (bit-identical to the oracle's or_gen_bf16) -------------------------
@@ -52,27 +52,27 @@ struct RowMap {
   }
 };
 
-// Fill a [rows][cols] logical matrix from the generator into the packed layout (row stride ld).
-__global__ void gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int64_t ld,
+// Fill a [rows][cols] logical matrix from the generator into the tiled layout.
+__global__ void gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int64_t kchunks,
                                   RowMap map, uint64_t key, float scale) {
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i - r * cols;
-    dst[map(r) * ld + c] = gen_bf16(key, i, scale);
+    dst[tiled_offset(map(r), c, kchunks)] = gen_bf16(key, i, scale);
   }
 }
 
 // Copy an uploaded [rows][cols] matrix (BF16 bits, or F32 rounded to BF16 as the reference's
 // loader does, src/qwen/hf.rs:248-253) into the packed layout.
 __global__ void pack_matrix_kernel(uint16_t* dst, const void* src, int32_t src_f32, int64_t rows,
-                                   int64_t cols, int64_t ld, RowMap map) {
+                                   int64_t cols, int64_t kchunks, RowMap map) {
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i - r * cols;
     const uint16_t v = src_f32 ? f32_to_bf16_rne(((const float*)src)[i]) : ((const uint16_t*)src)[i];
-    dst[map(r) * ld + c] = v;
+    dst[tiled_offset(map(r), c, kchunks)] = v;
   }
 }
 

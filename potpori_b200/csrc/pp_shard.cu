@@ -96,14 +96,13 @@ struct LayerDev {
   float* norm[N_COUNT] = {};
   float* kc = nullptr;  // [n_kv][capacity][hd]
   float* vc = nullptr;
-  CUtensorMap tm_qkv, tm_o, tm_gu, tm_d;
   bool mat_set[M_COUNT] = {};
   bool norm_set[N_COUNT] = {};
 };
 
 constexpr int kVariants = 4;  // chunk widths 1, 2, 4, 8
+constexpr int kRing = 64;     // in-flight headers / results per shard
 inline int variant_of(int m) { return m <= 1 ? 0 : m <= 2 ? 1 : m <= 4 ? 2 : 3; }
-inline int width_of(int v) { return 1 << v; }
 
 }  // namespace
 
@@ -120,13 +119,12 @@ struct pp_shard {
   std::vector<LayerDev> L;
   uint16_t* embed = nullptr;  // [Vp][Hp]
   float* final_norm = nullptr;
-  CUtensorMap tm_embed;
   bool embed_set = false, final_norm_set = false;
   float2* rope = nullptr;
   float* x = nullptr;      // [kMaxRows][Hp]
   float* qbuf = nullptr;   // [kMaxRows][Q]
-  float* attn = nullptr;   // [kMaxRows][Qp]
-  float* act = nullptr;    // [kMaxRows][Ip]
+  uint8_t* attn_split = nullptr;  // attention output, split BF16 blocks (Qp / 64 x 4 KB)
+  uint8_t* act_split = nullptr;   // SwiGLU output, split BF16 blocks (Ip / 64 x 4 KB)
   float* logits = nullptr; // [kMaxRows][V]
   float* apart = nullptr;
   float* gpart = nullptr;
@@ -135,15 +133,21 @@ struct pp_shard {
   uint32_t* done = nullptr;
   StepDesc* d_desc = nullptr;
   StepResult* d_res = nullptr;
-  StepDesc* h_desc = nullptr;
-  StepResult* h_res = nullptr;
+  StepDesc* h_desc = nullptr;      // pinned ring of kRing headers
+  StepResult* h_res = nullptr;     // pinned: result of the host-synchronous path
+  StepResult* h_slots = nullptr;   // pinned ring of kRing results (asynchronous path)
+  cudaEvent_t desc_ev[kRing] = {};
+  cudaEvent_t slot_ev[kRing] = {};
+  cudaEvent_t handoff_ev = nullptr, handoff_done_ev = nullptr;
+  uint32_t desc_next = 0;
   float* h_stage = nullptr;  // pinned [kMaxRows][H]
-  CUtensorMap tm_x_attn[kVariants], tm_x_act[kVariants];
   int splits = 1, nq_max = 1;
   int max_grid = 148;
   bool use_graphs = true, use_pdl = true;
   cudaGraphExec_t exec[kVariants] = {};
   uint32_t launches = 0;                 // kernels of the step being enqueued
+  std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
+  std::vector<int>* prof_kinds = nullptr;
   uint32_t variant_launches[kVariants] = {};
   int last_variant = 0;
   std::string err;
@@ -183,27 +187,20 @@ pp_status dalloc(pp_shard* s, T** p, size_t bytes) {
   return PP_OK;
 }
 
-pp_status make_map(pp_shard* s, CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t cols,
-                   uint64_t rows, uint32_t elem_bytes, uint32_t box_cols, uint32_t box_rows,
-                   CUtensorMapSwizzle swz) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return fail(s, PP_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * elem_bytes};
-  cuuint32_t box[2] = {box_cols, box_rows};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = enc(map, dt, 2, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(s, PP_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+// ---- kernel table ---------------------------------------------------------------------------
+pp_status after_launch(pp_shard* s, cudaStream_t st, int kind) {
+  ++s->launches;
+  if (s->prof_events) {
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    // External: a real event record node in the captured graph (timing works on replay).
+    CK(cudaEventRecordWithFlags(e, st, cudaEventRecordExternal));
+    s->prof_events->push_back(e);
+    s->prof_kinds->push_back(kind);
+  }
   return PP_OK;
 }
 
-pp_status make_wmap(pp_shard* s, CUtensorMap* map, uint16_t* base, int64_t cols, int64_t rows) {
-  return make_map(s, map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, cols, rows, 2, kChunkK,
-                  kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
-}
-
-// ---- kernel table ---------------------------------------------------------------------------
 template <int MT, int XM>
 int gemv_stages(int64_t kp, size_t budget) {
   using Lay = GemvSmem<MT, XM>;
@@ -221,8 +218,8 @@ size_t dyn_smem_limit(pp_shard* s, K kern) {
 }
 
 template <int MT, int XM, int EPI>
-pp_status launch_gemv(pp_shard* s, cudaStream_t st, const CUtensorMap& wmap, const CUtensorMap& xmap,
-                      GemvArgs a) {
+pp_status launch_gemv(pp_shard* s, cudaStream_t st, const uint16_t* w, GemvArgs a) {
+  a.w = w;
   using Lay = GemvSmem<MT, XM>;
   auto kern = gemv_kernel<MT, XM, EPI>;
   const size_t budget = dyn_smem_limit(s, kern);
@@ -242,14 +239,17 @@ pp_status launch_gemv(pp_shard* s, cudaStream_t st, const CUtensorMap& wmap, con
   attr[0].val.programmaticStreamSerializationAllowed = s->use_pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CK(cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a));
-  ++s->launches;
-  return PP_OK;
+  CK(cudaLaunchKernelEx(&cfg, kern, a));
+  return after_launch(s, st, EPI == EPI_QKV      ? PP_K_QKV
+                             : EPI == EPI_SWIGLU ? PP_K_GATE_UP
+                             : EPI == EPI_ARGMAX ? PP_K_HEAD
+                             : a.k == s->Q       ? PP_K_O
+                                                 : PP_K_DOWN);
 }
 
 template <typename... KArgs, typename... Args>
-pp_status launch_plain(pp_shard* s, cudaStream_t st, bool pdl, dim3 grid, dim3 block, size_t smem,
-                       void (*kern)(KArgs...), Args... args) {
+pp_status launch_plain(pp_shard* s, cudaStream_t st, int kind, bool pdl, dim3 grid, dim3 block,
+                       size_t smem, void (*kern)(KArgs...), Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -261,8 +261,7 @@ pp_status launch_plain(pp_shard* s, cudaStream_t st, bool pdl, dim3 grid, dim3 b
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   CK(cudaLaunchKernelEx(&cfg, kern, args...));
-  ++s->launches;
-  return PP_OK;
+  return after_launch(s, st, kind);
 }
 
 }  // namespace
@@ -299,16 +298,15 @@ template <int MT>
 pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   s->launches = 0;
   pp_status r;
-  if ((r = launch_plain(s, st, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
+  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
                         (int32_t)s->d.capacity, (int32_t)MT, (int32_t)s->V, (int32_t)s->first)))
     return r;
   if (s->first)
-    if ((r = launch_plain(s, st, true, dim3(MT), dim3(256), 0, embed_kernel, (const uint16_t*)s->embed,
-                          (int32_t)s->Hp, (int32_t)s->V, s->x, (int32_t)s->Hp,
+    if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(MT), dim3(256), 0, embed_kernel, (const uint16_t*)s->embed,
+                          (int32_t)s->H, (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x, (int32_t)s->Hp,
                           (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity,
                           (int32_t)MT)))
       return r;
-  const int vi = variant_of(MT);
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
     GemvArgs a = {};
@@ -342,14 +340,14 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     q.rope = s->rope;
     q.kcache = Ld.kc;
     q.vcache = Ld.vc;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_QKV>(s, st, Ld.tm_qkv, Ld.tm_qkv, q))) return r;
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_QKV>(s, st, Ld.wqkv, q))) return r;
     // Attention.
     AttnArgs at = {};
     at.q = s->qbuf;
     at.kcache = Ld.kc;
     at.vcache = Ld.vc;
     at.part = s->apart;
-    at.out = s->attn;
+    at.out_split = s->attn_split;
     at.n_heads = s->nh;
     at.n_kv = s->nkv;
     at.head_dim = s->hd;
@@ -365,11 +363,12 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     {
       // Split kernel reads q with stride Q; combine writes attn with stride Qp.
       const size_t smem = attn_smem_bytes(s->hd);
-      if ((r = launch_plain(s, st, true, dim3(s->nkv, s->splits), dim3(kAttnThreads), smem,
-                            attn_split_kernel<MT>, atq)))
+      if ((r = launch_plain(s, st, PP_K_ATTN, true, dim3(s->nkv, s->splits), dim3(kAttnThreads),
+                            smem, attn_split_kernel<MT>, atq)))
         return r;
       const int tb = s->hd < 32 ? 32 : s->hd;
-      if ((r = launch_plain(s, st, true, dim3(s->nh, MT), dim3(tb), 0, attn_combine_kernel<MT>, at)))
+      if ((r = launch_plain(s, st, PP_K_ATTN_COMBINE, true, dim3(s->nh, MT), dim3(tb), 0,
+                            attn_combine_kernel<MT>, at)))
         return r;
     }
     // O projection + residual.
@@ -380,9 +379,10 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     o.kp = (int32_t)s->Qp;
     o.tiles = (int32_t)(s->o_rows / kTileRows);
     o.kchunks = (int32_t)(s->Qp / kChunkK);
+    o.xsplit = s->attn_split;
     o.out = s->x;
     o.ldo = (int32_t)s->Hp;
-    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.tm_o, s->tm_x_attn[vi], o))) return r;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wo, o))) return r;
     // gate/up with the post-attention norm and SwiGLU.
     GemvArgs g = a;
     g.n_out = s->I;
@@ -394,9 +394,8 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     g.x = s->x;
     g.ldx = (int32_t)s->Hp;
     g.norm_w = Ld.norm[N_FFN];
-    g.out = s->act;
-    g.ldo = (int32_t)s->Ip;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_SWIGLU>(s, st, Ld.tm_gu, Ld.tm_gu, g))) return r;
+    g.out_split = s->act_split;
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_SWIGLU>(s, st, Ld.wgu, g))) return r;
     // down + residual.
     GemvArgs dn = a;
     dn.n_out = s->H;
@@ -405,9 +404,10 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     dn.kp = (int32_t)s->Ip;
     dn.tiles = (int32_t)(s->d_rows / kTileRows);
     dn.kchunks = (int32_t)(s->Ip / kChunkK);
+    dn.xsplit = s->act_split;
     dn.out = s->x;
     dn.ldo = (int32_t)s->Hp;
-    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.tm_d, s->tm_x_act[vi], dn))) return r;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wd, dn))) return r;
   }
   if (s->last) {
     GemvArgs h = {};
@@ -430,7 +430,7 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     h.norm_w = s->final_norm;
     h.check_input = (!s->first && s->nl == 0) ? 1 : 0;
     h.logits = s->logits;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_ARGMAX>(s, st, s->tm_embed, s->tm_embed, h)))
+    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_ARGMAX>(s, st, s->embed, h)))
       return r;
   }
   return PP_OK;
@@ -520,6 +520,20 @@ void fill_verify(pp_shard* s, uint32_t m, pp_verify_out* v) {
   v->n_accepted = r.n_accepted;
   v->correction = r.correction;
   v->nonfinite_rows = r.nonfinite_rows;
+}
+
+// Next pinned header slot; waits (host) until its previous upload has been consumed.
+StepDesc* next_desc(pp_shard* s, int* slot) {
+  const int i = (int)(s->desc_next++ % kRing);
+  cudaEventSynchronize(s->desc_ev[i]);
+  *slot = i;
+  return &s->h_desc[i];
+}
+
+pp_status upload_desc(pp_shard* s, int slot, cudaStream_t st) {
+  CK(cudaMemcpyAsync(s->d_desc, &s->h_desc[slot], sizeof(StepDesc), cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(s->desc_ev[slot], st));
+  return PP_OK;
 }
 
 pp_status check_step(pp_shard* s, uint32_t pos, uint32_t m) {
@@ -697,6 +711,13 @@ void pp_shard_destroy(pp_shard* s) {
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_desc) cudaFreeHost(s->h_desc);
   if (s->h_res) cudaFreeHost(s->h_res);
+  if (s->h_slots) cudaFreeHost(s->h_slots);
+  for (int i = 0; i < kRing; ++i) {
+    if (s->desc_ev[i]) cudaEventDestroy(s->desc_ev[i]);
+    if (s->slot_ev[i]) cudaEventDestroy(s->slot_ev[i]);
+  }
+  if (s->handoff_ev) cudaEventDestroy(s->handoff_ev);
+  if (s->handoff_done_ev) cudaEventDestroy(s->handoff_done_ev);
   if (s->h_stage) cudaFreeHost(s->h_stage);
   if (s->stream) cudaStreamDestroy(s->stream);
   cudaSetDevice(prev);
@@ -735,6 +756,7 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   pp_status r0 = set_attrs(s);
   if (r0) return r0;
   s->splits = s->num_sms / s->nkv > 0 ? s->num_sms / s->nkv : 1;
+  if (s->splits > 256) s->splits = 256;  // the combine kernel holds up to 256 splits
   s->nq_max = s->G * 8;
   pp_status r;
   s->L.resize(s->nl);
@@ -750,14 +772,9 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
     if ((r = dalloc(s, &Ld.norm[N_FFN], (size_t)s->H * 4))) return r;
     if ((r = dalloc(s, &Ld.kc, (size_t)s->KV * desc->capacity * 4))) return r;
     if ((r = dalloc(s, &Ld.vc, (size_t)s->KV * desc->capacity * 4))) return r;
-    if ((r = make_wmap(s, &Ld.tm_qkv, Ld.wqkv, s->Hp, s->qkv_rows))) return r;
-    if ((r = make_wmap(s, &Ld.tm_o, Ld.wo, s->Qp, s->o_rows))) return r;
-    if ((r = make_wmap(s, &Ld.tm_gu, Ld.wgu, s->Hp, s->gu_rows))) return r;
-    if ((r = make_wmap(s, &Ld.tm_d, Ld.wd, s->Ip, s->d_rows))) return r;
   }
   if (s->first || s->last) {
     if ((r = dalloc(s, &s->embed, (size_t)s->Vp * s->Hp * 2))) return r;
-    if ((r = make_wmap(s, &s->tm_embed, s->embed, s->Hp, s->Vp))) return r;
   }
   if (s->last && (r = dalloc(s, &s->final_norm, (size_t)s->H * 4))) return r;
   // RoPE table, src/qwen/model.rs:397-402 / tiny.rs:29-30: angle = pos * theta^(-2i/d).
@@ -776,8 +793,8 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   }
   if ((r = dalloc(s, &s->x, (size_t)kMaxRows * s->Hp * 4))) return r;
   if ((r = dalloc(s, &s->qbuf, (size_t)kMaxRows * s->Q * 4))) return r;
-  if ((r = dalloc(s, &s->attn, (size_t)kMaxRows * s->Qp * 4))) return r;
-  if ((r = dalloc(s, &s->act, (size_t)kMaxRows * s->Ip * 4))) return r;
+  if ((r = dalloc(s, &s->attn_split, (size_t)(s->Qp / kChunkK) * SplitRows<16>::kBlock))) return r;
+  if ((r = dalloc(s, &s->act_split, (size_t)(s->Ip / kChunkK) * SplitRows<16>::kBlock))) return r;
   if (s->last && (r = dalloc(s, &s->logits, (size_t)kMaxRows * s->V * 4))) return r;
   if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 2) * 4))) return r;
   if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * 8 * 4))) return r;
@@ -791,19 +808,17 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   if ((r = dalloc(s, &s->done, 64))) return r;
   if ((r = dalloc(s, &s->d_desc, sizeof(StepDesc)))) return r;
   if ((r = dalloc(s, &s->d_res, sizeof(StepResult)))) return r;
-  CK(cudaMallocHost(&s->h_desc, sizeof(StepDesc)));
+  CK(cudaMallocHost(&s->h_desc, sizeof(StepDesc) * kRing));
   CK(cudaMallocHost(&s->h_res, sizeof(StepResult)));
-  CK(cudaMallocHost(&s->h_stage, (size_t)kMaxRows * s->H * 4));
-  memset(s->h_desc, 0, sizeof(StepDesc));
-  for (int v = 0; v < kVariants; ++v) {
-    const uint32_t w = (uint32_t)width_of(v);
-    if ((r = make_map(s, &s->tm_x_attn[v], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s->attn, s->Qp, kMaxRows,
-                      4, kChunkK, w, CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return r;
-    if ((r = make_map(s, &s->tm_x_act[v], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s->act, s->Ip, kMaxRows,
-                      4, kChunkK, w, CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return r;
+  CK(cudaMallocHost(&s->h_slots, sizeof(StepResult) * kRing));
+  for (int i = 0; i < kRing; ++i) {
+    CK(cudaEventCreateWithFlags(&s->desc_ev[i], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&s->slot_ev[i], cudaEventDisableTiming));
   }
+  CK(cudaEventCreateWithFlags(&s->handoff_ev, cudaEventDisableTiming));
+  CK(cudaEventCreateWithFlags(&s->handoff_done_ev, cudaEventDisableTiming));
+  CK(cudaMallocHost(&s->h_stage, (size_t)kMaxRows * s->H * 4));
+  memset(s->h_desc, 0, sizeof(StepDesc) * kRing);
   CK(cudaStreamSynchronize(s->stream));
   return PP_OK;
 }
@@ -819,6 +834,7 @@ pp_status pp_shard_create(const pp_shard_desc* desc, pp_shard** out) {
   if (!(desc->capacity > 0 && desc->capacity <= 0x7fffffffu && desc->chunk <= desc->capacity))
     return fail(nullptr, PP_E_INVALID, "invalid cache/chunk capacity");
   if (c.n_kv_heads == 0 || c.n_heads % c.n_kv_heads || c.head_dim % 4 || c.head_dim > 128 ||
+      c.hidden % 4 || c.intermediate % 4 ||
       128 % c.head_dim || c.hidden == 0 || c.intermediate == 0 || c.vocab_size == 0)
     return fail(nullptr, PP_E_UNSUPPORTED, "unsupported geometry");
   if ((c.n_heads / c.n_kv_heads) * 8 > 32)
@@ -869,7 +885,7 @@ struct Target {
   bool is_norm = false;
   uint16_t* mat = nullptr;
   float* norm = nullptr;
-  int64_t rows = 0, cols = 0, ld = 0;
+  int64_t rows = 0, cols = 0, kchunks = 0;
   RowMap map{1, 0, 0};
   bool* flag = nullptr;
 };
@@ -878,7 +894,7 @@ static pp_status resolve(pp_shard* s, const char* name, Target& t) {
   const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
   if (!strcmp(name, "model.embed_tokens.weight")) {
     if (!(s->first || s->last)) return PP_OK;
-    t = Target{true, false, s->embed, nullptr, s->V, H, s->Hp, RowMap{(int32_t)s->V, 0, 0}, &s->embed_set};
+    t = Target{true, false, s->embed, nullptr, s->V, H, s->Hp / kChunkK, RowMap{(int32_t)s->V, 0, 0}, &s->embed_set};
     return PP_OK;
   }
   if (!strcmp(name, "model.norm.weight")) {
@@ -902,13 +918,13 @@ static pp_status resolve(pp_shard* s, const char* name, Target& t) {
     t.mine = true;
     t.flag = &Ld.mat_set[m];
     switch (m) {
-      case M_Q: t.mat = Ld.wqkv; t.rows = Q; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)Q, 0, 0}; break;
-      case M_K: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)KV, 0, (int32_t)Q}; break;
-      case M_V: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.ld = s->Hp; t.map = RowMap{(int32_t)KV, 0, (int32_t)(Q + KV)}; break;
-      case M_O: t.mat = Ld.wo; t.rows = H; t.cols = Q; t.ld = s->Qp; t.map = RowMap{(int32_t)H, 0, 0}; break;
-      case M_G: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.ld = s->Hp; t.map = RowMap{kTileRows / 2, kTileRows, 0}; break;
-      case M_U: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.ld = s->Hp; t.map = RowMap{kTileRows / 2, kTileRows, kTileRows / 2}; break;
-      default: t.mat = Ld.wd; t.rows = H; t.cols = I; t.ld = s->Ip; t.map = RowMap{(int32_t)H, 0, 0}; break;
+      case M_Q: t.mat = Ld.wqkv; t.rows = Q; t.cols = H; t.kchunks = s->Hp / kChunkK; t.map = RowMap{(int32_t)Q, 0, 0}; break;
+      case M_K: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.kchunks = s->Hp / kChunkK; t.map = RowMap{(int32_t)KV, 0, (int32_t)Q}; break;
+      case M_V: t.mat = Ld.wqkv; t.rows = KV; t.cols = H; t.kchunks = s->Hp / kChunkK; t.map = RowMap{(int32_t)KV, 0, (int32_t)(Q + KV)}; break;
+      case M_O: t.mat = Ld.wo; t.rows = H; t.cols = Q; t.kchunks = s->Qp / kChunkK; t.map = RowMap{(int32_t)H, 0, 0}; break;
+      case M_G: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.kchunks = s->Hp / kChunkK; t.map = RowMap{kTileRows / 2, kTileRows, 0}; break;
+      case M_U: t.mat = Ld.wgu; t.rows = I; t.cols = H; t.kchunks = s->Hp / kChunkK; t.map = RowMap{kTileRows / 2, kTileRows, kTileRows / 2}; break;
+      default: t.mat = Ld.wd; t.rows = H; t.cols = I; t.kchunks = s->Ip / kChunkK; t.map = RowMap{(int32_t)H, 0, 0}; break;
     }
     return PP_OK;
   }
@@ -950,7 +966,7 @@ pp_status pp_shard_set_tensor(pp_shard* s, const char* name, pp_dtype dtype, con
     cudaError_t e = cudaMemcpyAsync(tmp, data, elements * eb, cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) {
       pack_matrix_kernel<<<1024, 256, 0, s->stream>>>(t.mat, tmp, dtype == PP_F32, t.rows, t.cols,
-                                                      t.ld, t.map);
+                                                      t.kchunks, t.map);
       e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
@@ -980,7 +996,7 @@ pp_status pp_shard_init_random(pp_shard* s, uint64_t seed, float stdv) {
     if (t.is_norm) {
       fill_f32_kernel<<<64, 256, 0, s->stream>>>(t.norm, t.cols, 1.0f);
     } else {
-      gen_matrix_kernel<<<2048, 256, 0, s->stream>>>(t.mat, t.rows, t.cols, t.ld, t.map,
+      gen_matrix_kernel<<<2048, 256, 0, s->stream>>>(t.mat, t.rows, t.cols, t.kchunks, t.map,
                                                      tensor_key(seed, nm.c_str()), scale);
     }
     CK(cudaGetLastError());
@@ -1070,14 +1086,15 @@ pp_status pp_shard_forward_tokens(pp_shard* s, uint32_t pos, const int32_t* toke
     if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
       return fail(s, PP_E_INVALID, "invalid token input");
   CK(cudaSetDevice(s->dev));
-  StepDesc& d = *s->h_desc;
+  int slot;
+  StepDesc& d = *next_desc(s, &slot);
   d.pos = (int32_t)pos;
   d.m = (int32_t)m;
   d.n_drafts = (int32_t)m - 1;
   d.flags = (verify && verify->logits) ? 1 : 0;
   for (uint32_t i = 0; i < m; ++i) d.tokens[i] = tokens[i];
   for (uint32_t i = 1; i < m; ++i) d.drafts[i - 1] = tokens[i];
-  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, s->stream));
+  if ((r = upload_desc(s, slot, s->stream))) return r;
   return finish_host_step(s, m, out_hidden, verify);
 }
 
@@ -1093,40 +1110,43 @@ pp_status pp_shard_forward_hidden(pp_shard* s, uint32_t pos, uint32_t m, const f
   for (size_t i = 0; i < (size_t)m * s->H; ++i)  // src/qwen/model.rs:390-392
     if (!std::isfinite(hidden[i])) return fail(s, PP_E_INVALID, "invalid hidden input");
   CK(cudaSetDevice(s->dev));
-  StepDesc& d = *s->h_desc;
+  int slot;
+  StepDesc& d = *next_desc(s, &slot);
   d.pos = (int32_t)pos;
   d.m = (int32_t)m;
   d.n_drafts = (int32_t)n_drafts;
   d.flags = (verify && verify->logits) ? 1 : 0;
   for (uint32_t i = 0; i < n_drafts; ++i) d.drafts[i] = drafts[i];
   memcpy(s->h_stage, hidden, (size_t)m * s->H * 4);
-  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, s->stream));
+  if ((r = upload_desc(s, slot, s->stream))) return r;
   CK(cudaMemcpy2DAsync(s->x, (size_t)s->Hp * 4, s->h_stage, (size_t)s->H * 4, (size_t)s->H * 4, m,
                        cudaMemcpyHostToDevice, s->stream));
   return finish_host_step(s, m, out_hidden, verify);
 }
 
 pp_status pp_shard_set_step(pp_shard* s, uint32_t pos, uint32_t m, const int32_t* tokens,
-                            const int32_t* drafts, uint32_t n_drafts, int32_t want_logits,
+                            const int32_t* drafts, uint32_t n_drafts, int32_t flags,
                             void* stream) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
   pp_status r = check_step(s, pos, m);
   if (r) return r;
   if (n_drafts > (uint32_t)kMaxRows || (n_drafts && !drafts) || (s->first && !tokens))
     return fail(s, PP_E_INVALID, "invalid step");
+  if (s->first)
+    for (uint32_t i = 0; i < m; ++i)
+      if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
+        return fail(s, PP_E_INVALID, "invalid token input");
   CK(cudaSetDevice(s->dev));
   cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
-  // The pinned header may still be in flight from the previous step.
-  CK(cudaStreamSynchronize(st));
-  StepDesc& d = *s->h_desc;
+  int slot;
+  StepDesc& d = *next_desc(s, &slot);
   d.pos = (int32_t)pos;
   d.m = (int32_t)m;
   d.n_drafts = (int32_t)n_drafts;
-  d.flags = want_logits ? 1 : 0;
+  d.flags = flags;
   for (uint32_t i = 0; i < m && tokens; ++i) d.tokens[i] = tokens[i];
   for (uint32_t i = 0; i < n_drafts; ++i) d.drafts[i] = drafts[i];
-  CK(cudaMemcpyAsync(s->d_desc, s->h_desc, sizeof(StepDesc), cudaMemcpyHostToDevice, st));
-  return PP_OK;
+  return upload_desc(s, slot, st);
 }
 
 pp_status pp_shard_step_device(pp_shard* s, uint32_t max_rows, void* stream) {
@@ -1180,6 +1200,116 @@ pp_status pp_shard_fill_kv(pp_shard* s, uint64_t seed, uint32_t rows) {
   }
   CK(cudaStreamSynchronize(s->stream));
   return PP_OK;
+}
+
+pp_status pp_shard_profile_kernels(pp_shard* s, uint32_t max_rows, uint32_t iters, float* ms,
+                                   int32_t* kinds, uint32_t cap, uint32_t* count) {
+  if (!s || !ms || !kinds || !count || iters == 0) return fail(s, PP_E_INVALID, "null argument");
+  if (max_rows == 0 || max_rows > 8) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..8");
+  if (pp_shard_missing(s, nullptr, 0)) return fail(s, PP_E_MISSING, "parameters missing");
+  CK(cudaSetDevice(s->dev));
+  // Capture the step with an event record after every kernel, then replay the graph: the
+  // per-kernel times carry no host launch overhead (the events do serialise the kernels).
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kd;
+  cudaEvent_t start;
+  CK(cudaEventCreate(&start));
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = cudaEventRecordWithFlags(start, s->stream, cudaEventRecordExternal);
+  s->prof_events = &ev;
+  s->prof_kinds = &kd;
+  pp_status r = e == cudaSuccess ? enqueue_variant(s, variant_of((int)max_rows), s->stream)
+                                 : fail(s, PP_E_CUDA, "profile: %s", cudaGetErrorString(e));
+  s->prof_events = nullptr;
+  s->prof_kinds = nullptr;
+  e = cudaStreamEndCapture(s->stream, &g);
+  if (r == PP_OK && e != cudaSuccess) r = fail(s, PP_E_CUDA, "profile capture: %s", cudaGetErrorString(e));
+  if (r == PP_OK) {
+    e = cudaGraphInstantiate(&ge, g, 0);
+    if (e != cudaSuccess) r = fail(s, PP_E_CUDA, "profile instantiate: %s", cudaGetErrorString(e));
+  }
+  std::vector<double> acc(ev.size(), 0.0);
+  for (uint32_t it = 0; r == PP_OK && it <= iters; ++it) {
+    e = cudaGraphLaunch(ge, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) {
+      r = fail(s, PP_E_CUDA, "profile: %s", cudaGetErrorString(e));
+      break;
+    }
+    if (it == 0) continue;  // warm-up replay
+    cudaEvent_t prev = start;
+    for (size_t k = 0; k < ev.size(); ++k) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, prev, ev[k]);
+      acc[k] += t;
+      prev = ev[k];
+    }
+  }
+  if (ge) cudaGraphExecDestroy(ge);
+  if (g) cudaGraphDestroy(g);
+  cudaEventDestroy(start);
+  for (cudaEvent_t x : ev) cudaEventDestroy(x);
+  if (r) return r;
+  *count = (uint32_t)acc.size();
+  for (size_t k = 0; k < acc.size() && k < cap; ++k) {
+    ms[k] = (float)(acc[k] / iters);
+    kinds[k] = kd[k];
+  }
+  return PP_OK;
+}
+
+void* pp_shard_stream(const pp_shard* s) { return s ? (void*)s->stream : nullptr; }
+
+pp_status pp_shard_handoff(pp_shard* from, pp_shard* to, uint32_t m) {
+  pp_shard* s = to;
+  if (!from || !to) return fail(to, PP_E_INVALID, "null shard");
+  if (from->last || to->first || from->H != to->H || from->d.layer_end != to->d.layer_begin)
+    return fail(to, PP_E_INVALID, "shards are not adjacent stages");
+  if (m == 0 || m > (uint32_t)kMaxRows) return fail(to, PP_E_INVALID, "bad row count");
+  CK(cudaSetDevice(from->dev));
+  CK(cudaEventRecord(from->handoff_ev, from->stream));
+  CK(cudaSetDevice(to->dev));
+  CK(cudaStreamWaitEvent(to->stream, from->handoff_ev, 0));
+  const size_t bytes = (size_t)m * to->Hp * 4;
+  if (from->dev == to->dev)
+    CK(cudaMemcpyAsync(to->x, from->x, bytes, cudaMemcpyDeviceToDevice, to->stream));
+  else
+    CK(cudaMemcpyPeerAsync(to->x, to->dev, from->x, from->dev, bytes, to->stream));
+  // `from` may not overwrite its output rows before they have been copied out.
+  CK(cudaEventRecord(to->handoff_done_ev, to->stream));
+  CK(cudaSetDevice(from->dev));
+  CK(cudaStreamWaitEvent(from->stream, to->handoff_done_ev, 0));
+  return PP_OK;
+}
+
+pp_status pp_shard_result_enqueue(pp_shard* s, uint32_t slot) {
+  if (!s || slot >= (uint32_t)kRing) return fail(s, PP_E_INVALID, "bad result slot");
+  CK(cudaSetDevice(s->dev));
+  CK(cudaMemcpyAsync(&s->h_slots[slot], s->d_res, sizeof(StepResult), cudaMemcpyDeviceToHost,
+                     s->stream));
+  CK(cudaEventRecord(s->slot_ev[slot], s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_result_wait(pp_shard* s, uint32_t slot, uint32_t m, pp_verify_out* verify) {
+  if (!s || slot >= (uint32_t)kRing || m == 0 || m > (uint32_t)kMaxRows)
+    return fail(s, PP_E_INVALID, "bad result slot");
+  CK(cudaSetDevice(s->dev));
+  CK(cudaEventSynchronize(s->slot_ev[slot]));
+  const StepResult& r = s->h_slots[slot];
+  if (verify) {
+    for (uint32_t i = 0; i < m; ++i) {
+      if (verify->argmax) verify->argmax[i] = r.argmax[i];
+      if (verify->top1) verify->top1[i] = r.top1[i];
+      if (verify->top2) verify->top2[i] = r.top2[i];
+    }
+    verify->n_accepted = r.n_accepted;
+    verify->correction = r.correction;
+    verify->nonfinite_rows = r.nonfinite_rows;
+  }
+  return status_of(s, r);
 }
 
 uint32_t pp_shard_capacity(const pp_shard* s) { return s->d.capacity; }

@@ -171,6 +171,21 @@ class Shard:
     def last_launches(self) -> int:
         return int(self._L.pp_shard_last_launches(self._h))
 
+    def stream(self) -> int:
+        """The shard's own CUDA stream handle (cudaStream_t as an int)."""
+        return int(self._L.pp_shard_stream(self._h) or 0)
+
+    def profile_kernels(self, max_rows: int, iters: int = 5) -> list:
+        """Mean duration of every kernel of one step launched in isolation:
+        [(kind, ms), ...] in launch order."""
+        cap = 4096
+        ms = (ctypes.c_float * cap)()
+        kinds = (ctypes.c_int32 * cap)()
+        n = ctypes.c_uint32()
+        check(self._L.pp_shard_profile_kernels(self._h, max_rows, iters, ms, kinds, cap,
+                                               ctypes.byref(n)), self._h, "profile")
+        return [(_lib.KERNEL_KINDS[kinds[i]], float(ms[i])) for i in range(min(n.value, cap))]
+
     def set_graphs(self, enabled: bool) -> None:
         check(self._L.pp_shard_set_graphs(self._h, int(enabled)), self._h)
 
@@ -248,16 +263,33 @@ class Shard:
         return h.value, d.value, r.value
 
     def set_step(self, pos: int, m: int, tokens=None, drafts=(), want_logits=False,
-                 stream: int = 0) -> None:
+                 stream: int = 0, flags: int = 0) -> None:
+        """Enqueue the step header. flags bit 0 (or want_logits) also writes the logits; other
+        bits travel with the header to the next stages."""
         t = _i32(tokens) if tokens is not None else None
         d = _i32(drafts)
         check(self._L.pp_shard_set_step(
             self._h, pos, m, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if t is not None else None,
             d.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) if d.size else None, d.size,
-            int(want_logits), stream or None), self._h, "set_step")
+            int(flags) | int(bool(want_logits)), stream or None), self._h, "set_step")
 
     def step_device(self, max_rows: int, stream: int = 0) -> None:
         check(self._L.pp_shard_step_device(self._h, max_rows, stream or None), self._h, "step")
+
+    def handoff_from(self, prev: "Shard", m: int) -> None:
+        """Enqueue the copy of ``prev``'s output rows into this shard's input (peer copy over
+        NVLink across devices), ordered after ``prev``'s enqueued work."""
+        check(self._L.pp_shard_handoff(prev._h, self._h, m), self._h, "handoff")
+
+    def result_enqueue(self, slot: int) -> None:
+        check(self._L.pp_shard_result_enqueue(self._h, slot), self._h, "result_enqueue")
+
+    def result_wait(self, slot: int, m: int) -> VerifyResult:
+        vo = self._verify_struct(None)
+        st = self._L.pp_shard_result_wait(self._h, slot, m, ctypes.byref(vo))
+        if st not in (_lib.PP_OK, _lib.PP_E_NONFINITE):
+            check(st, self._h, "result_wait")
+        return self._result(m, None)
 
     def read_result(self, m: int, stream: int = 0, logits: bool = False) -> VerifyResult:
         lg = np.empty((m, self.cfg.vocab_size), np.float32) if logits else None

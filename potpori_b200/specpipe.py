@@ -6,6 +6,9 @@ wrong prefix: their results are drained and discarded, and drafting restarts fro
 committed prefix. There is no rollback call: every shard writes its KV at absolute
 positions and attends only below the chunk it runs, so a re-submission overwrites the stale
 tail.
+
+``PipelinedDriver`` is the same loop cut into steps (one FILL + one READ per step) so a
+benchmark can time a fixed number of them; ``run_spec_decode_pipelined`` runs it to the end.
 """
 from __future__ import annotations
 
@@ -33,76 +36,103 @@ class ChainError(RuntimeError):
     pass
 
 
-def run_spec_decode_pipelined(draft, chain, prompt: List[int], cfg: SpecConfig,
-                              depth: int) -> Tuple[List[int], SpecStats]:
-    assert cfg.gamma > 0, "gamma must be positive"
-    if cfg.max_new == 0:
-        return [], SpecStats()
-    capacity = min(chain.capacity(), draft.capacity())
-    assert prompt and len(prompt) < capacity, "prompt must leave room in the KV cache"
-    max_new = min(cfg.max_new, capacity - len(prompt))
-    gamma = cfg.gamma
-    depth = max(depth, 1)
-    prompt_len = len(prompt)
+class PipelinedDriver:
+    def __init__(self, draft, chain, prompt: List[int], cfg: SpecConfig, depth: int):
+        assert cfg.gamma > 0, "gamma must be positive"
+        self.draft, self.chain, self.cfg = draft, chain, cfg
+        self.prompt = list(prompt)
+        self.capacity = min(chain.capacity(), draft.capacity())
+        assert self.prompt and len(self.prompt) < self.capacity, \
+            "prompt must leave room in the KV cache"
+        self.max_new = min(cfg.max_new, self.capacity - len(self.prompt))
+        self.gamma = cfg.gamma
+        self.depth = max(depth, 1)
+        self.out: List[int] = []
+        self.traversals = 0
+        self.finished = cfg.max_new == 0
+        self.started = False
 
-    cur0 = chain.prefill(prompt)
-    out: List[int] = []
-    done = chain.is_eos(cur0)
-    if not done:
-        out.append(cur0)
-    done = done or len(out) >= max_new
-    dprefix = list(prompt) + [cur0]
-    send_pos = prompt_len
-    inflight: deque = deque()
-    discard = 0
-    traversals = 0
-    while True:
-        # FILL (src/specpipe.rs:89-121)
-        while len(inflight) < depth and not done and discard == 0:
-            cur = dprefix[-1]
+    def start(self) -> None:
+        """Prefill the prompt (src/specpipe.rs:68-81)."""
+        self.started = True
+        if self.finished:
+            return
+        cur0 = self.chain.prefill(self.prompt)
+        self.done = self.chain.is_eos(cur0)
+        if not self.done:
+            self.out.append(cur0)
+        self.done = self.done or len(self.out) >= self.max_new
+        self.dprefix = self.prompt + [cur0]
+        self.send_pos = len(self.prompt)
+        self.inflight: deque = deque()
+        self.discard = 0
+
+    def step(self) -> bool:
+        """One FILL + one READ (src/specpipe.rs:87-183). False once generation has ended."""
+        if not self.started:
+            self.start()
+        if self.finished:
+            return False
+        chain, gamma = self.chain, self.gamma
+        while len(self.inflight) < self.depth and not self.done and self.discard == 0:
+            cur = self.dprefix[-1]
             if chain.is_eos(cur):
                 break
-            remaining = max(capacity - send_pos, 0)
+            remaining = max(self.capacity - self.send_pos, 0)
             if remaining == 0:
                 break
             single = remaining <= gamma
-            if single and inflight:
+            if single and self.inflight:
                 break
-            ds = [] if single else draft.draft(dprefix, gamma)
+            ds = [] if single else self.draft.draft(self.dprefix, gamma)
             assert single or len(ds) == gamma, "draft returned the wrong token count"
-            chain.submit(send_pos, cur, ds)
-            dprefix.extend(ds)
-            inflight.append(ds)
-            send_pos += gamma
+            chain.submit(self.send_pos, cur, ds)
+            self.dprefix.extend(ds)
+            self.inflight.append(ds)
+            self.send_pos += gamma
             if single:
                 break
-        if not inflight:
-            break
-        # READ (src/specpipe.rs:126-183)
+        if not self.inflight:
+            self.finished = True
+            return False
         r = chain.poll()
-        ds = inflight.popleft()
+        ds = self.inflight.popleft()
         if len(r) != len(ds) + 1:
             raise ChainError(f"chain returned {len(r)} tokens for a {len(ds) + 1}-token chunk")
-        traversals += 1
-        if discard > 0:
-            discard -= 1
-            continue
+        self.traversals += 1
+        if self.discard > 0:
+            self.discard -= 1
+            return True
         n = accept(ds, r)
         diverged = (not ds) or n != len(ds)
         committed = ds[:n] + [r[n]] if diverged else list(ds)
         for t in committed:
             if chain.is_eos(t):
-                done = True
+                self.done = True
                 break
-            out.append(t)
-            if len(out) >= max_new:
-                done = True
+            self.out.append(t)
+            if len(self.out) >= self.max_new:
+                self.done = True
                 break
-        if done:
-            discard = len(inflight)
+        if self.done:
+            self.discard = len(self.inflight)
         elif diverged:
-            discard = len(inflight)
-            keep = prompt_len + len(out) - 1
-            dprefix = list(prompt) + out
-            send_pos = keep
-    return out, SpecStats(len(out), traversals)
+            self.discard = len(self.inflight)
+            keep = len(self.prompt) + len(self.out) - 1
+            self.dprefix = self.prompt + self.out
+            self.send_pos = keep
+        return True
+
+    def stats(self) -> SpecStats:
+        return SpecStats(len(self.out), self.traversals)
+
+
+def run_spec_decode_pipelined(draft, chain, prompt: List[int], cfg: SpecConfig,
+                              depth: int) -> Tuple[List[int], SpecStats]:
+    d = PipelinedDriver(draft, chain, prompt, cfg, depth)
+    if cfg.max_new == 0:
+        return [], SpecStats()
+    d.start()
+    while d.step():
+        pass
+    return d.out, d.stats()
