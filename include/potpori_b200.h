@@ -170,6 +170,25 @@ uint32_t pp_shard_last_launches(const pp_shard* shard);
 pp_status pp_shard_set_graphs(pp_shard* shard, int32_t enabled);
 pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
 
+/* Allocation-free RMSNorm + skinny GEMV (no counterpart in the reference; an addition for
+ * callers that cannot allocate device memory: code running inside a host framework or memory
+ * pool that owns every allocation, or a context where cudaMalloc/cudaFree and their implicit
+ * synchronisation are not allowed). With every pointer a device pointer:
+ *   y[i][j] = sum_c W[j][c] * (x[i][c] / sqrt(mean_c x[i][c]^2 + eps) * norm_w[c])
+ * for i < m <= 8 rows, j < n, c < k (k a multiple of 8). x is [m][k] F32, y is [m][n] F32,
+ * norm_w is [k] F32, and W is BF16 in the tiled layout the shards use: element (j, c) at
+ *   ((((j/128)*kc + c/64)*128 + j%128) * 64) + ((((c%64)/8) ^ (j%8)) * 8) + c%8
+ * with kc = ceil(k/64), the buffer holding ceil(n/128)*kc blocks of 128x64, padding zero.
+ * The call allocates nothing: its split-K scratch is a static device array of about 1.2 MB
+ * (partial sums for 148 CTAs and counters for n <= 8192*128 rows) that every GPU loading the
+ * library holds until exit; it rejects larger sizes with PP_E_INVALID. The first call on a
+ * device looks the array up with that device current and should come before any stream
+ * capture. Every call shares the array and clears the counters it needs: calls that overlap
+ * on the GPU (two streams at once) race on it. stream: a cudaStream_t (NULL = default). */
+pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x, const float* norm_w,
+                              float eps, uint32_t n, uint32_t k, uint32_t m, float* y,
+                              void* stream);
+
 /* Message of the last error on the handle (or of the last failed create when NULL). */
 size_t pp_last_error(const pp_shard* shard, char* buf, size_t len);
 /* Library version string. */

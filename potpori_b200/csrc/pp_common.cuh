@@ -8,6 +8,9 @@
 
 namespace pp {
 
+// Host: message of the last failure of an entry point without a handle (pp_last_error(NULL)).
+void set_global_error(const char* msg);
+
 // ---- limits and layout constants -------------------------------------------------------
 constexpr int kMaxRows = 16;        // largest chunk (rows of the activation) a launch takes
 constexpr int kTileRows = 128;      // GEMV output rows per tile (= one head of 128 for QKV)

@@ -71,8 +71,9 @@ struct GemvArgs {
   uint32_t* tile_cnt;   // [tiles], zero between launches
   ArgRec* recs;         // [grid][MT]
   uint32_t* done_cnt;   // zero between launches
-  const StepDesc* desc;
-  StepResult* res;
+  const StepDesc* desc;  // step header; NULL for a standalone GEMV (m_rows gives the rows)
+  StepResult* res;       // step result / status; may be NULL for a standalone GEMV
+  int32_t m_rows;
 };
 
 template <int MT, int XM>
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   float* st_second = (float*)(misc + 8 + 2 * MT);
   int32_t* st_nonf = misc + 8 + 3 * MT;
 
-  if (bad_step(a.desc, a.capacity, MT)) return;
+  if (a.desc ? bad_step(a.desc, a.capacity, MT) : (a.m_rows < 1 || a.m_rows > MT)) return;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int64_t T = (int64_t)a.tiles * a.kchunks;
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         issued = i + 1;
       }
       if (issued < n_it) {
-        atomicOr(&a.res->status, ST_TIMEOUT);
+        if (a.res) atomicOr(&a.res->status, ST_TIMEOUT);
         // Let the copies already issued land before the CTA's shared memory goes away.
         for (int64_t j = (issued > ns ? issued - ns : 0); j < issued; ++j)
           mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);
@@ -217,8 +218,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 
   // ------------------------------------------------------------------ consumer warps
   pdl_wait();
-  const StepDesc& d = *a.desc;
-  const int mv = d.m;  // rows that matter; the launch guarantees 1 <= m <= MT
+  const int mv = a.desc ? a.desc->m : a.m_rows;  // rows that matter: 1 <= mv <= MT
 
   if (XM == X_RESIDENT_NORM) {
     // RMSNorm (tiny.rs:20-23): x * (1 / sqrt(mean(x^2) + eps)) * w, staged for the whole K
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       *(uint4*)(blk + R * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     consumer_sync();
-    if (tid == 0 && misc[1]) atomicOr(&a.res->status, misc[1]);
+    if (tid == 0 && misc[1] && a.res) atomicOr(&a.res->status, misc[1]);
   }
 
   // Lane roles for ldmatrix: A (weights) matrix mat = lane >> 3 covers rows (mat & 1) * 8 and
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       for (int p = warp; p < heads * mv; p += kConsumerWarps) {
         const int hl = p / mv, m = p - hl * mv;
         const int n0 = t * kTileRows + hl * hd;
-        const int pos = d.pos + m;
+        const int pos = a.desc->pos + m;
         const float* v = tile_out + (size_t)(hl * hd) * MT + m;  // v[i * MT]
         if (n0 < a.q_dim + a.kv_dim) {
           const bool isq = n0 < a.q_dim;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         float b = -INFINITY, s2 = -INFINITY;
         int32_t bi = 0x7fffffff;
         int nf = 0;
-        const bool dump = d.flags & 1;
+        const bool dump = a.desc->flags & 1;
         for (int r = lane; r < kTileRows; r += 32) {
           const int n = t * kTileRows + r;
           if (n >= a.n_out) break;
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   }
 
   if (!ok) {
-    if (tid == 0) atomicOr(&a.res->status, ST_TIMEOUT);
+    if (tid == 0 && a.res) atomicOr(&a.res->status, ST_TIMEOUT);
     return;
   }
 
@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     consumer_sync();
     if (tid == 0) {
       int n = 0;
-      while (n < d.n_drafts && n < mv && d.drafts[n] == a.res->argmax[n]) ++n;
+      while (n < a.desc->n_drafts && n < mv && a.desc->drafts[n] == a.res->argmax[n]) ++n;
       if (n >= mv) n = mv - 1;
       a.res->n_accepted = n;
       a.res->correction = a.res->argmax[n];

@@ -685,6 +685,11 @@ bool parse_header(const char* p, size_t n, std::map<std::string, StEntry>& out) 
 
 }  // namespace
 
+namespace pp {
+// Message for pp_last_error(NULL, ...) from entry points that have no handle.
+void set_global_error(const char* msg) { g_create_error = msg; }
+}  // namespace pp
+
 // =========================================================================== C ABI
 extern "C" {
 
