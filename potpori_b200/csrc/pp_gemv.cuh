@@ -74,6 +74,16 @@ struct GemvArgs {
   const StepDesc* desc;  // step header; NULL for a standalone GEMV (m_rows gives the rows)
   StepResult* res;       // step result / status; may be NULL for a standalone GEMV
   int32_t m_rows;
+  // Streamed normalised input: the operand is split(x * w_norm) and the sums of squares of
+  // x come as per-tile partials [ss_tiles][kMaxRows]; the accumulator is scaled by
+  // 1 / sqrt(mean(x^2) + eps) (NULL ss_in: no scaling).
+  const float* ss_in;
+  int32_t ss_tiles;
+  // Residual-add epilogue extras: also write split(x_new * wnext) for the next norm's GEMV
+  // and this tile's per-row sum of squares of x_new (NULL: not needed).
+  uint8_t* xw_out;
+  const float* wnext;
+  float* ss_out;
 };
 
 template <int MT, int XM>
@@ -93,9 +103,13 @@ struct GemvSmem {
   static __host__ __device__ size_t total(int ns, int kp) { return misc_off(ns, kp) + 512 + 1024; }
 };
 
-__device__ __forceinline__ int64_t sk_start(int64_t b, int64_t T, int64_t G) { return b * T / G; }
-__device__ __forceinline__ int64_t sk_owner(int64_t i, int64_t T, int64_t G) {
-  return ((i + 1) * G + T - 1) / T - 1;
+// Stream-K ranges in 32-bit arithmetic (T * G < 2^32: T <= 2^23 iterations, G <= 256 CTAs).
+constexpr int kMaxFixup = 256;  // contributors of one split tile are at most G
+__device__ __forceinline__ int sk_start(uint32_t b, uint32_t T, uint32_t G) {
+  return (int)(b * T / G);
+}
+__device__ __forceinline__ int sk_owner(uint32_t i, uint32_t T, uint32_t G) {
+  return (int)(((i + 1) * G + T - 1) / T) - 1;
 }
 
 __device__ __forceinline__ void argrec_merge(float& b1, int32_t& i1, float& s1, float b2,
@@ -150,9 +164,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   if (a.desc ? bad_step(a.desc, a.capacity, MT) : (a.m_rows < 1 || a.m_rows > MT)) return;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int64_t T = (int64_t)a.tiles * a.kchunks;
-  const int64_t G = gridDim.x;
-  const int64_t i0 = sk_start(blockIdx.x, T, G), i1 = sk_start(blockIdx.x + 1, T, G);
+  const uint32_t T = (uint32_t)a.tiles * (uint32_t)a.kchunks;
+  const uint32_t G = gridDim.x;
+  const int i0 = sk_start(blockIdx.x, T, G), i1 = sk_start(blockIdx.x + 1, T, G);
   const int first_tile = (int)(i0 / a.kchunks);
 
   if (tid == 0) {
@@ -176,40 +190,51 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   // ------------------------------------------------------------------ producer warp
   if (warp == kConsumerWarps) {
     if (lane == 0) {
-      const int64_t n_it = i1 - i0;
-      const int pre = (int)(n_it < ns ? n_it : ns);
+      const int n_it = i1 - i0;
+      const int pre = n_it < ns ? n_it : ns;
       const uint32_t bytes = L::kWBytes + L::kXBytes;
-      auto wsrc = [&](int64_t it) {
-        const int t = (int)(it / a.kchunks), c = (int)(it % a.kchunks);
-        return a.w + ((size_t)t * a.kchunks + c) * (kTileRows * kChunkK);
+      const int kc = a.kchunks;
+      // (tile, chunk) of the next weight block, advanced without divisions.
+      int wt = i0 / kc, wc = i0 - (i0 / kc) * kc;
+      auto next_w = [&]() {
+        const uint16_t* src = a.w + ((size_t)wt * kc + wc) * (kTileRows * kChunkK);
+        if (++wc == kc) {
+          wc = 0;
+          ++wt;
+        }
+        return src;
+      };
+      int xc = wc;  // chunk of the next activation block
+      auto next_x = [&]() {
+        const uint8_t* src = a.xsplit + (size_t)xc * XB;
+        if (++xc == kc) xc = 0;
+        return src;
       };
       for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
         mbar_arrive_expect_tx(&full[i], bytes);
-        bulk_load(wst + (size_t)i * L::kWBytes, wsrc(i0 + i), L::kWBytes, &full[i]);
+        bulk_load(wst + (size_t)i * L::kWBytes, next_w(), L::kWBytes, &full[i]);
       }
       pdl_wait();
       if (XM == X_STREAM)
-        for (int i = 0; i < pre; ++i) {
-          const int c = (int)((i0 + i) % a.kchunks);
-          bulk_load(xst + (size_t)i * XB, a.xsplit + (size_t)c * XB, XB, &full[i]);
-        }
-      int64_t issued = pre;
-      for (int64_t i = pre; i < n_it; ++i) {
-        const int s = (int)(i % ns);
-        const uint32_t use = (uint32_t)(i / ns);
+        for (int i = 0; i < pre; ++i) bulk_load(xst + (size_t)i * XB, next_x(), XB, &full[i]);
+      int issued = pre;
+      int s = pre % ns;
+      uint32_t use = pre / ns;
+      for (int i = pre; i < n_it; ++i) {
         if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
         mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_load(wst + (size_t)s * L::kWBytes, wsrc(i0 + i), L::kWBytes, &full[s]);
-        if (XM == X_STREAM) {
-          const int c = (int)((i0 + i) % a.kchunks);
-          bulk_load(xst + (size_t)s * XB, a.xsplit + (size_t)c * XB, XB, &full[s]);
-        }
+        bulk_load(wst + (size_t)s * L::kWBytes, next_w(), L::kWBytes, &full[s]);
+        if (XM == X_STREAM) bulk_load(xst + (size_t)s * XB, next_x(), XB, &full[s]);
         issued = i + 1;
+        if (++s == ns) {
+          s = 0;
+          ++use;
+        }
       }
       if (issued < n_it) {
         if (a.res) atomicOr(&a.res->status, ST_TIMEOUT);
         // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int64_t j = (issued > ns ? issued - ns : 0); j < issued; ++j)
+        for (int j = (issued > ns ? issued - ns : 0); j < issued; ++j)
           mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);
       }
     }
@@ -219,6 +244,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   // ------------------------------------------------------------------ consumer warps
   pdl_wait();
   const int mv = a.desc ? a.desc->m : a.m_rows;  // rows that matter: 1 <= mv <= MT
+  __shared__ float scale_s[MT];
+  if (tid < MT) {
+    float sc = 1.0f;
+    if (a.ss_in && tid < mv) {
+      float t = 0.f;
+      for (int q = 0; q < a.ss_tiles; ++q) t += __ldcg(a.ss_in + q * kMaxRows + tid);
+      sc = 1.0f / sqrtf(t / (float)a.k + a.eps);  // RMSNorm, tiny.rs:20-23
+    }
+    scale_s[tid] = sc;
+  }
+  consumer_sync();
 
   if (XM == X_RESIDENT_NORM) {
     // RMSNorm (tiny.rs:20-23): x * (1 / sqrt(mean(x^2) + eps)) * w, staged for the whole K
@@ -296,26 +332,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   // K half (mat >> 1); B (activations) matrix mat covers K step (mat >> 1), half (mat & 1).
   const int mat = lane >> 3, l7 = lane & 7;
   const int arow = warp * 16 + l7 + (mat & 1) * 8;
-  int64_t it = i0;
-  int local = 0;  // iterations consumed so far by this CTA
+  int it = i0;
+  int cs = 0;           // ring stage of the next iteration
+  uint32_t cphase = 0;  // its parity
   bool ok = true;
+  int t = i0 / a.kchunks;
   while (it < i1 && ok) {
-    const int t = (int)(it / a.kchunks);
-    const int64_t tile_begin = (int64_t)t * a.kchunks, tile_end = tile_begin + a.kchunks;
-    const int64_t seg_begin = it, seg_end = i1 < tile_end ? i1 : tile_end;
-    float acc[NB][4];
+    const int tile_begin = t * a.kchunks, tile_end = tile_begin + a.kchunks;
+    const int seg_begin = it, seg_end = i1 < tile_end ? i1 : tile_end;
+    // Four independent accumulator chains per column block (hi/lo x even/odd K step), so
+    // consecutive MMAs never wait on each other; summed at the end of the segment.
+    float acc[NB][4][4];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[nb][q] = 0.f;
+      for (int ch = 0; ch < 4; ++ch)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[nb][ch][q] = 0.f;
 
-    for (; it < seg_end; ++it, ++local) {
-      const int s = local % ns;
-      if (!mbar_wait(&full[s], (uint32_t)(local / ns) & 1)) {
+    for (; it < seg_end; ++it) {
+      const int s = cs;
+      if (!mbar_wait(&full[s], cphase)) {
         ok = false;
         break;
       }
-      const int c = (int)(it - tile_begin);
+      if (++cs == ns) {
+        cs = 0;
+        cphase ^= 1u;
+      }
+      const int c = it - tile_begin;
       const uint8_t* wb = wst + (size_t)s * L::kWBytes;
       const uint8_t* xb = (XM == X_STREAM) ? xst + (size_t)s * XB : xs + (size_t)c * XB;
       uint32_t af[4][4];
@@ -340,26 +385,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       for (int st = 0; st < 4; ++st)
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) {
-          const int p = st >> 1, q = (st & 1) * 2;
-          mma_bf16(acc[nb], af[st], bh[nb][p][q], bh[nb][p][q + 1]);
-          mma_bf16(acc[nb], af[st], bl[nb][p][q], bl[nb][p][q + 1]);
+          const int p = st >> 1, q = (st & 1) * 2, ch = (st & 1) * 2;
+          mma_bf16(acc[nb][ch], af[st], bh[nb][p][q], bh[nb][p][q + 1]);
+          mma_bf16(acc[nb][ch + 1], af[st], bl[nb][p][q], bl[nb][p][q + 1]);
         }
     }
     if (!ok) break;
 
-    {  // accumulator fragments -> tile_out[row][m]
+    {  // accumulator fragments (x the RMSNorm scale of their row) -> tile_out[row][m]
       const int g = lane >> 2, tq = lane & 3;
       const int r0 = warp * 16 + g;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          v[q] = (acc[nb][0][q] + acc[nb][2][q]) + (acc[nb][1][q] + acc[nb][3][q]);
         const int m0 = nb * 8 + 2 * tq;
         if (m0 < MT) {
-          tile_out[r0 * MT + m0] = acc[nb][0];
-          tile_out[(r0 + 8) * MT + m0] = acc[nb][2];
+          tile_out[r0 * MT + m0] = v[0] * scale_s[m0];
+          tile_out[(r0 + 8) * MT + m0] = v[2] * scale_s[m0];
         }
         if (m0 + 1 < MT) {
-          tile_out[r0 * MT + m0 + 1] = acc[nb][1];
-          tile_out[(r0 + 8) * MT + m0 + 1] = acc[nb][3];
+          tile_out[r0 * MT + m0 + 1] = v[1] * scale_s[m0 + 1];
+          tile_out[(r0 + 8) * MT + m0 + 1] = v[3] * scale_s[m0 + 1];
         }
       }
     }
@@ -373,30 +422,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) mine[e] = tile_out[e];
       __threadfence();
       consumer_sync();
-      const int64_t b_lo = sk_owner(tile_begin, T, G), b_hi = sk_owner(tile_end - 1, T, G);
+      const int b_lo = sk_owner(tile_begin, T, G), b_hi = sk_owner(tile_end - 1, T, G);
+      const int nbk = b_hi - b_lo + 1;
       if (tid == 0) {
         const uint32_t old = atomicAdd(&a.tile_cnt[t], 1u);
         misc[0] = (old == (uint32_t)(b_hi - b_lo));
       }
+      // Where each contributor's partial of this tile sits (its first or its last slot).
+      __shared__ int fix_off[kMaxFixup];
+      for (int q = tid; q < nbk && q < kMaxFixup; q += kConsumerWarps * 32) {
+        const int b = b_lo + q;
+        const int bslot = (sk_start(b, T, G) / a.kchunks == t) ? 0 : 1;
+        fix_off[q] = (b * 2 + bslot) * kTileRows * MT;
+      }
       consumer_sync();
-      if (!misc[0]) continue;
+      if (!misc[0]) {
+        ++t;
+        continue;
+      }
       __threadfence();
       // Sum the contributors' partials in K order; loads are issued in groups of 8
       // independent reads so the fixup costs about one L2 round trip per group.
-      const int nbk = (int)(b_hi - b_lo + 1);
       for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
         float v = 0.f;
         for (int b0 = 0; b0 < nbk; b0 += 8) {
           float pv[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int64_t b = b_lo + b0 + q;
-            pv[q] = 0.f;
-            if (b0 + q < nbk) {
-              const int bslot = (sk_start(b, T, G) / a.kchunks == t) ? 0 : 1;
-              pv[q] = __ldcg(a.partials + ((size_t)b * 2 + bslot) * kTileRows * MT + e);
-            }
-          }
+          for (int q = 0; q < 8; ++q)
+            pv[q] = (b0 + q < nbk) ? __ldcg(a.partials + fix_off[b0 + q] + e) : 0.f;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             if (b0 + q < nbk) v += pv[q];
@@ -409,15 +462,40 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 
     // ---------------------------------------------------------------- epilogues
     if (EPI == EPI_STORE || EPI == EPI_RESADD) {
+      // Residual add (src/qwen/model.rs:318-331). With xw_out, also the next RMSNorm's
+      // operand split(x_new * w) and this tile's per-row sum of squares of x_new, so the
+      // next GEMV streams its input instead of normalising it in a prologue.
+      const bool extras = EPI == EPI_RESADD && a.xw_out != nullptr;
+      __shared__ float ssr[MT][kTileRows / 32];
       for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
         const int m = e / kTileRows, r = e - m * kTileRows;
         const int n = t * kTileRows + r;
+        float sq = 0.f;
         if (m < mv && n < a.n_out) {
           float* o = a.out + (size_t)m * a.ldo + n;
-          if (EPI == EPI_RESADD)
-            *o += tile_out[r * MT + m];
-          else
+          if (EPI == EPI_RESADD) {
+            const float xn = *o + tile_out[r * MT + m];
+            *o = xn;
+            if (extras) {
+              store_split<MT>(a.xw_out, m, n, xn * a.wnext[n]);
+              sq = xn * xn;
+            }
+          } else {
             *o = tile_out[r * MT + m];
+          }
+        }
+        if (extras) {  // a warp covers 32 consecutive rows of one column m
+          sq = warp_sum(sq);
+          if (lane == 0) ssr[m][r >> 5] = sq;
+        }
+      }
+      if (extras) {
+        consumer_sync();
+        if (tid < MT) {
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < kTileRows / 32; ++q) v += ssr[tid][q];
+          a.ss_out[t * kMaxRows + tid] = v;
         }
       }
     } else if (EPI == EPI_SWIGLU) {
@@ -500,6 +578,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       }
     }
     consumer_sync();  // tile_out is reused by the next tile
+    ++t;
   }
 
   if (!ok) {
@@ -532,7 +611,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       float b = -INFINITY, s2 = -INFINITY;
       int32_t bi = 0x7fffffff;
       int nf = 0;
-      for (int64_t g = lane; g < G; g += 32) {
+      for (uint32_t g = lane; g < G; g += 32) {
         const ArgRec* rp = a.recs + (size_t)g * MT + m;
         const float rb = __ldcg(&rp->best), rs = __ldcg(&rp->second);
         const int32_t ri = __ldcg(&rp->idx), rn = __ldcg(&rp->nonfinite);

@@ -1,28 +1,69 @@
-// Small kernels around the verify pass: the embedding gather of the first shard, the seeded
-// weight generator, packing uploaded parameters into the shard's HBM layout, and fills.
+// Small kernels around the verify pass: the shard's input kernel (embedding gather or hidden
+// check, and the first GEMV's normalised operand), the seeded weight generator, packing uploaded parameters into the shard's HBM layout, and fills.
 #pragma once
 #include "pp_common.cuh"
 
 namespace pp {
 
-// Embedding rows of the chunk's tokens, BF16 decoded to F32 (src/qwen/model.rs:239-241).
-// Grid (MT); a row past m is left alone.
-__global__ void embed_kernel(const uint16_t* __restrict__ table, int32_t hidden, int32_t kchunks,
-                             int32_t vocab, float* __restrict__ x, int32_t ldx,
-                             const StepDesc* desc, StepResult* res, int32_t capacity,
-                             int32_t max_rows) {
+// The shard's input rows and the operand of its first GEMV. On the first shard x is the
+// embedding rows of the chunk's tokens, BF16 decoded to F32 (src/qwen/model.rs:239-241);
+// otherwise x is the hidden state received from the previous shard, checked finite
+// (src/qwen/model.rs:384-386). For the GEMV after it (QKV, or the vocab head of a shard with
+// no layers) this writes split(x * norm_w) in the split activation layout and each row's sum
+// of squares of x into slot 0 of the per-tile partials [ss_tiles][kMaxRows] (other slots 0);
+// the GEMV scales its accumulator by 1 / sqrt(mean(x^2) + eps), the RMSNorm of
+// src/qwen/tiny.rs:20-23. Grid (MT), one block of 256 threads per row; rows past m are left
+// alone.
+template <int MT>
+__global__ void input_prep_kernel(const uint16_t* __restrict__ table, int32_t hidden,
+                                  int32_t kchunks, int32_t vocab, float* __restrict__ x,
+                                  int32_t ldx, const float* __restrict__ norm_w,
+                                  uint8_t* __restrict__ xw, float* __restrict__ ss,
+                                  int32_t ss_tiles, const StepDesc* desc, StepResult* res,
+                                  int32_t capacity) {
   if (threadIdx.x == 0) pdl_launch_dependents();
-  if (bad_step(desc, capacity, max_rows)) return;
+  if (bad_step(desc, capacity, MT)) return;
   pdl_wait();
   const int r = blockIdx.x;
   if (r >= desc->m) return;
-  const int tok = desc->tokens[r];
-  if (tok < 0 || tok >= vocab) {
-    if (threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
-    return;
+  int tok = 0;
+  if (table) {
+    tok = desc->tokens[r];
+    if (tok < 0 || tok >= vocab) {
+      if (threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
+      return;
+    }
   }
-  for (int k = threadIdx.x; k < hidden; k += blockDim.x)
-    x[(size_t)r * ldx + k] = __uint_as_float((uint32_t)table[tiled_offset(tok, k, kchunks)] << 16);
+  float* xr = x + (size_t)r * ldx;
+  float sq = 0.f;
+  int bad = 0;
+  for (int k = threadIdx.x; k < hidden; k += blockDim.x) {
+    float v;
+    if (table) {
+      v = __uint_as_float((uint32_t)table[tiled_offset(tok, k, kchunks)] << 16);
+      xr[k] = v;
+    } else {
+      v = xr[k];
+      bad |= !isfinite(v);
+    }
+    sq += v * v;
+    if (xw) store_split<MT>(xw, r, k, v * norm_w[k]);
+  }
+  __shared__ float red[32];
+  __shared__ int bad_s;
+  if (threadIdx.x == 0) bad_s = 0;
+  __syncthreads();
+  sq = warp_sum(sq);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  if (bad) atomicOr(&bad_s, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    ss[r] = t;
+    for (int q = 1; q < ss_tiles; ++q) ss[q * kMaxRows + r] = 0.f;
+    if (bad_s) atomicOr(&res->status, ST_NONFINITE_IN);
+  }
 }
 
 // ---- seeded generator (bit-identical to the oracle's or_gen_bf16) -------------------------

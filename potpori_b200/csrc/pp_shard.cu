@@ -125,6 +125,14 @@ struct pp_shard {
   float* qbuf = nullptr;   // [kMaxRows][Q]
   uint8_t* attn_split = nullptr;  // attention output, split BF16 blocks (Qp / 64 x 4 KB)
   uint8_t* act_split = nullptr;   // SwiGLU output, split BF16 blocks (Ip / 64 x 4 KB)
+  // Normalised GEMV operands split(x * w) (Hp / 64 x 4 KB) and the per-tile sums of squares
+  // of x [ss_tiles][kMaxRows] they are scaled with: the attention input (QKV, and the vocab
+  // head after the last layer) and the MLP input (gate/up).
+  uint8_t* xw_attn = nullptr;
+  uint8_t* xw_ffn = nullptr;
+  float* ss_attn = nullptr;
+  float* ss_ffn = nullptr;
+  int ss_tiles = 1;
   float* logits = nullptr; // [kMaxRows][V]
   float* apart = nullptr;
   float* gpart = nullptr;
@@ -301,12 +309,16 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
                         (int32_t)s->d.capacity, (int32_t)MT, (int32_t)s->V, (int32_t)s->first)))
     return r;
-  if (s->first)
-    if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(MT), dim3(256), 0, embed_kernel, (const uint16_t*)s->embed,
-                          (int32_t)s->H, (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x, (int32_t)s->Hp,
-                          (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity,
-                          (int32_t)MT)))
+  {
+    // Input rows (embedding or received hidden) and the first GEMV's operand.
+    const float* w0 = s->nl ? s->L[0].norm[N_ATTN] : s->final_norm;
+    if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(MT), dim3(256), 0, input_prep_kernel<MT>,
+                          (const uint16_t*)(s->first ? s->embed : nullptr), (int32_t)s->H,
+                          (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x, (int32_t)s->Hp, w0,
+                          w0 ? s->xw_attn : nullptr, s->ss_attn, (int32_t)s->ss_tiles,
+                          (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity)))
       return r;
+  }
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
     GemvArgs a = {};
@@ -329,10 +341,9 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     q.kp = (int32_t)s->Hp;
     q.tiles = (int32_t)(s->qkv_rows / kTileRows);
     q.kchunks = (int32_t)(s->Hp / kChunkK);
-    q.x = s->x;
-    q.ldx = (int32_t)s->Hp;
-    q.norm_w = Ld.norm[N_ATTN];
-    q.check_input = (!s->first && l == 0) ? 1 : 0;
+    q.xsplit = s->xw_attn;
+    q.ss_in = s->ss_attn;
+    q.ss_tiles = s->ss_tiles;
     q.out = s->qbuf;
     q.ldo = s->Q;
     q.qn = Ld.norm[N_QN];
@@ -340,7 +351,7 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     q.rope = s->rope;
     q.kcache = Ld.kc;
     q.vcache = Ld.vc;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_QKV>(s, st, Ld.wqkv, q))) return r;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_QKV>(s, st, Ld.wqkv, q))) return r;
     // Attention.
     AttnArgs at = {};
     at.q = s->qbuf;
@@ -382,6 +393,9 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     o.xsplit = s->attn_split;
     o.out = s->x;
     o.ldo = (int32_t)s->Hp;
+    o.xw_out = s->xw_ffn;
+    o.wnext = Ld.norm[N_FFN];
+    o.ss_out = s->ss_ffn;
     if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wo, o))) return r;
     // gate/up with the post-attention norm and SwiGLU.
     GemvArgs g = a;
@@ -391,11 +405,11 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     g.kp = (int32_t)s->Hp;
     g.tiles = (int32_t)(s->gu_rows / kTileRows);
     g.kchunks = (int32_t)(s->Hp / kChunkK);
-    g.x = s->x;
-    g.ldx = (int32_t)s->Hp;
-    g.norm_w = Ld.norm[N_FFN];
+    g.xsplit = s->xw_ffn;
+    g.ss_in = s->ss_ffn;
+    g.ss_tiles = s->ss_tiles;
     g.out_split = s->act_split;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_SWIGLU>(s, st, Ld.wgu, g))) return r;
+    if ((r = launch_gemv<MT, X_STREAM, EPI_SWIGLU>(s, st, Ld.wgu, g))) return r;
     // down + residual.
     GemvArgs dn = a;
     dn.n_out = s->H;
@@ -407,6 +421,13 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     dn.xsplit = s->act_split;
     dn.out = s->x;
     dn.ldo = (int32_t)s->Hp;
+    // The next norm's operand: the next layer's input norm, the final norm after the last
+    // layer of the model, none when the next layer lives on another shard.
+    dn.wnext = l + 1 < s->nl ? s->L[l + 1].norm[N_ATTN] : s->last ? s->final_norm : nullptr;
+    if (dn.wnext) {
+      dn.xw_out = s->xw_attn;
+      dn.ss_out = s->ss_attn;
+    }
     if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wd, dn))) return r;
   }
   if (s->last) {
@@ -425,12 +446,11 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     h.kp = (int32_t)s->Hp;
     h.tiles = (int32_t)(s->Vp / kTileRows);
     h.kchunks = (int32_t)(s->Hp / kChunkK);
-    h.x = s->x;
-    h.ldx = (int32_t)s->Hp;
-    h.norm_w = s->final_norm;
-    h.check_input = (!s->first && s->nl == 0) ? 1 : 0;
+    h.xsplit = s->xw_attn;
+    h.ss_in = s->ss_attn;
+    h.ss_tiles = s->ss_tiles;
     h.logits = s->logits;
-    if ((r = launch_gemv<MT, X_RESIDENT_NORM, EPI_ARGMAX>(s, st, s->embed, h)))
+    if ((r = launch_gemv<MT, X_STREAM, EPI_ARGMAX>(s, st, s->embed, h)))
       return r;
   }
   return PP_OK;
@@ -447,10 +467,10 @@ pp_status set_max_smem(pp_shard* s, K kern) {
 template <int MT>
 pp_status set_attrs_mt(pp_shard* s) {
   pp_status r;
-  if ((r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_QKV>)) ||
+  if ((r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_QKV>)) ||
       (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_RESADD>)) ||
-      (r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_SWIGLU>)) ||
-      (r = set_max_smem(s, gemv_kernel<MT, X_RESIDENT_NORM, EPI_ARGMAX>)) ||
+      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_SWIGLU>)) ||
+      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_ARGMAX>)) ||
       (r = set_max_smem(s, attn_split_kernel<MT>)))
     return r;
   return PP_OK;
@@ -800,6 +820,11 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   if ((r = dalloc(s, &s->qbuf, (size_t)kMaxRows * s->Q * 4))) return r;
   if ((r = dalloc(s, &s->attn_split, (size_t)(s->Qp / kChunkK) * SplitRows<16>::kBlock))) return r;
   if ((r = dalloc(s, &s->act_split, (size_t)(s->Ip / kChunkK) * SplitRows<16>::kBlock))) return r;
+  s->ss_tiles = (int)(s->o_rows / kTileRows);
+  if ((r = dalloc(s, &s->xw_attn, (size_t)(s->Hp / kChunkK) * SplitRows<16>::kBlock))) return r;
+  if ((r = dalloc(s, &s->xw_ffn, (size_t)(s->Hp / kChunkK) * SplitRows<16>::kBlock))) return r;
+  if ((r = dalloc(s, &s->ss_attn, (size_t)s->ss_tiles * kMaxRows * 4))) return r;
+  if ((r = dalloc(s, &s->ss_ffn, (size_t)s->ss_tiles * kMaxRows * 4))) return r;
   if (s->last && (r = dalloc(s, &s->logits, (size_t)kMaxRows * s->V * 4))) return r;
   if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 2) * 4))) return r;
   if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * 8 * 4))) return r;
