@@ -6,60 +6,102 @@
 // rows past pos+m-1 (a rejected speculative tail) are never read, which is the reference's
 // rollback-by-overwrite.
 //
-// Split-KV decode layout: one CTA per (KV head, key range). All G*m query vectors that share
-// the KV head (G = n_heads / n_kv_heads) are processed together so every K/V byte is read
-// once per step; K/V tiles of 32 keys are double-buffered with cp.async; softmax is online
-// (running max, rescaled sum). A second kernel merges the per-split partials.
+// Split-KV decode layout: one CTA per (KV head, key range); all G*m query vectors that share
+// the KV head (G = n_heads / n_kv_heads <= 8) are processed together so every K/V byte is
+// read once per step. A second kernel merges the per-split partials.
 #pragma once
 #include "pp_common.cuh"
 
 namespace pp {
 
 struct AttnArgs {
-  const float* q;       // [MT][q_dim], normed and rotated
-  const float* kcache;  // [n_kv][capacity][head_dim]
-  const float* vcache;
-  float* part;          // [n_kv][splits][nq_max][head_dim + 2]
-  uint8_t* out_split;   // attention output rows, split BF16 layout (input of the O GEMV)
+  const float* q;          // [MT][q_dim], normed and rotated
+  const uint8_t* kcache;   // [n_kv][capacity] rows, split BF16 (kv_offset layout)
+  const uint8_t* vcache;
+  float* part;             // [n_kv][splits][nq_max][4 + head_dim]: max, sum, -, -, out
+  uint8_t* out_split;      // attention output rows, split BF16 layout (input of the O GEMV)
   int32_t n_heads, n_kv, head_dim, capacity, splits, q_dim, nq_max;
   float scale;  // sqrt(head_dim); scores are divided by it as in tiny.rs:90
   const StepDesc* desc;
   StepResult* res;
 };
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
+constexpr int kAttnStages = 3;  // K/V tiles in flight per CTA
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void ldmatrix_x4a(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-constexpr int kAttnStages = 3;  // K/V tiles in flight per CTA (cp.async groups)
+// Shared memory of attn_split_kernel<MT, NT> (bytes, 128-aligned base):
+//   K/V tiles [stages][K, V][32 rows][row]  | queries [8*NT rows][row] (cache row format)
+//   scores S[8*NT][33] F32 | probabilities P[hi, lo][8*NT][40] BF16 (80-byte rows)
+//   running max, sum, rescale [8*NT] F32, causal limit [8*NT] int | mbarriers [stages]
+struct AttnSmem {
+  int rowb, nq8;
+  __host__ __device__ AttnSmem(int hd, int nt) : rowb(kv_row_bytes(hd)), nq8(8 * nt) {}
+  __host__ __device__ size_t q_off() const { return (size_t)kAttnStages * 2 * kAttnTile * rowb; }
+  __host__ __device__ size_t s_off() const { return q_off() + (size_t)nq8 * rowb; }
+  __host__ __device__ size_t p_off() const { return s_off() + (size_t)nq8 * 33 * 4; }
+  __host__ __device__ size_t st_off() const { return p_off() + (size_t)2 * nq8 * 80; }
+  __host__ __device__ size_t bar_off() const { return st_off() + (size_t)4 * nq8 * 4; }
+  __host__ __device__ size_t total() const { return bar_off() + 8 * kAttnStages + 128; }
+};
+__host__ inline size_t attn_smem_bytes(int hd, int nt) { return AttnSmem(hd, nt).total(); }
 
-// Shared memory (floats): qs[32][hdp] | K[S][32][hdp] | V[S][32][hdp] | ps[32][32] | st[3][32]
-__host__ __device__ inline size_t attn_smem_bytes(int hd) {
-  const int hdp = hd + 4;
-  return (size_t)(32 * hdp + 2 * kAttnStages * kAttnTile * hdp + 32 * kAttnTile + 3 * 32) * 4;
-}
-
-template <int MT>
+// One CTA (8 warps) per (KV head h, key split s); NT = ceil(G*MT / 8) query tiles of 8.
+// Per 32-key tile, on the tensor cores (m16n8k16 BF16, F32 accumulate), with every F32
+// operand carried as hi + lo BF16 and the three products hi.hi + hi.lo + lo.hi (about 2^-16
+// relative, the F32 arithmetic of the reference to within its rounding):
+//  1. S^T = K . Q^T: the 32 keys are the M dimension (two m16 tiles), the queries N; a warp
+//     takes one (key tile, query tile) unit; scaled by 1/sqrt(head_dim) and masked (split
+//     range, causal limit pos + r) into S.
+//  2. Online softmax per query (a warp per query, lane = key): running max, rescale factor,
+//     running sum; P = exp(S - max) written as hi/lo BF16.
+//  3. O^T += V^T . P^T: head dims are M (ldmatrix.trans of the V rows), queries N; a warp owns
+//     16 dims x its query tiles, accumulators rescaled first.
+// K/V tiles are contiguous 32-row blocks of the cache, fetched with one bulk copy each into a
+// kAttnStages ring (mbarrier completion, bounded waits).
+template <int MT, int NT>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];
-  const int hd = a.head_dim, hdp = hd + 4;
-  float* qs = sm;
-  float* ks = qs + 32 * hdp;
-  float* vs = ks + kAttnStages * kAttnTile * hdp;
-  float* ps = vs + kAttnStages * kAttnTile * hdp;
-  float* st_m = ps + 32 * kAttnTile;
-  float* st_l = st_m + 32;
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
+  const int hd = a.head_dim, hdk = kv_hdk(hd), mask = kv_swz_mask(hd);
+  const AttnSmem L(hd, NT);
+  const int rowb = L.rowb;
+  constexpr int NQ8 = 8 * NT;
+  uint8_t* kvs = sm;
+  uint8_t* qsm = sm + L.q_off();
+  float* S_s = (float*)(sm + L.s_off());
+  uint8_t* P_s = sm + L.p_off();
+  float* m_s = (float*)(sm + L.st_off());
+  float* l_s = m_s + NQ8;
+  float* al_s = l_s + NQ8;
+  int* lim_s = (int*)(al_s + NQ8);
+  uint64_t* bar = (uint64_t*)(sm + L.bar_off());
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, s = blockIdx.y;
   if (tid == 0) pdl_launch_dependents();
   if (bad_step(a.desc, a.capacity, MT)) return;
+  if (tid == 0) {
+    for (int i = 0; i < kAttnStages; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+  }
   pdl_wait();
   const int pos = a.desc->pos, m = a.desc->m;
   const int G = a.n_heads / a.n_kv;
@@ -69,159 +111,191 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
   const int tps = (ntiles + a.splits - 1) / a.splits;
   const int t0 = s * tps, t1 = min(ntiles, t0 + tps);
   const int kend = min(c, t1 * kAttnTile);  // this split covers keys [t0*32, kend)
+  const uint8_t* kb = a.kcache + (size_t)h * a.capacity * rowb;
+  const uint8_t* vb = a.vcache + (size_t)h * a.capacity * rowb;
+  __syncthreads();  // barrier init visible to every thread
 
-  // Query vectors of this KV head: qi = g * MT + r, head h*G + g, row r.
-  for (int e = tid; e < nq * hd; e += kAttnThreads) {
-    const int qi = e / hd, dd = e - qi * hd;
-    const int g = qi / MT, r = qi - g * MT;
-    qs[qi * hdp + dd] = (r < m) ? a.q[(size_t)r * a.q_dim + (h * G + g) * hd + dd] : 0.f;
-  }
-  if (tid < 32) {
-    st_m[tid] = -INFINITY;
-    st_l[tid] = 0.f;
-  }
-
-  const float* kbase = a.kcache + (size_t)h * a.capacity * hd;
-  const float* vbase = a.vcache + (size_t)h * a.capacity * hd;
-  const int c4 = hd / 4;
-  auto load_tile = [&](int buf, int tile) {
+  int next_issue = t0;  // thread 0: first tile not yet requested
+  auto issue = [&](int tile) {
+    const int bi = (tile - t0) % kAttnStages;
     const int j0 = tile * kAttnTile;
-    float* kd = ks + buf * kAttnTile * hdp;
-    float* vd = vs + buf * kAttnTile * hdp;
-    for (int e = tid; e < kAttnTile * c4; e += kAttnThreads) {
-      const int row = e / c4, col = (e - row * c4) * 4;
-      const int jg = j0 + row;
-      if (jg < kend) {
-        cp_async16(kd + row * hdp + col, kbase + (size_t)jg * hd + col);
-        cp_async16(vd + row * hdp + col, vbase + (size_t)jg * hd + col);
-      } else {
-        *(float4*)(kd + row * hdp + col) = make_float4(0.f, 0.f, 0.f, 0.f);
-        *(float4*)(vd + row * hdp + col) = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    cp_async_commit();
+    const uint32_t bytes = (uint32_t)min(kAttnTile, kend - j0) * rowb;
+    uint8_t* dst = kvs + (size_t)bi * 2 * kAttnTile * rowb;
+    mbar_arrive_expect_tx(&bar[bi], 2 * bytes);
+    bulk_load(dst, kb + (size_t)j0 * rowb, bytes, &bar[bi]);
+    bulk_load(dst + (size_t)kAttnTile * rowb, vb + (size_t)j0 * rowb, bytes, &bar[bi]);
   };
+  if (tid == 0)
+    for (; next_issue < t1 && next_issue < t0 + kAttnStages; ++next_issue) issue(next_issue);
 
-  const int qi = tid >> 3, kg = tid & 7;
-  const int g_q = qi / MT, r_q = qi - g_q * MT;
-  const bool qvalid = qi < nq && r_q < m;
-  const int p_q = pos + r_q;  // absolute position of this query row
-  float acc[16];
+  // Queries of this KV head (qi = g * MT + r: query head h*G + g, chunk row r) as hi/lo rows;
+  // a thread converts 16 dims with its loads issued together.
+  for (int e = tid; e < NQ8 * (hdk / 16); e += kAttnThreads) {
+    const int qi = e / (hdk / 16), d0 = (e - qi * (hdk / 16)) * 16;
+    const int g = qi / MT, r = qi - g * MT;
+    const bool valid = qi < nq && r < m;
+    const float* src = a.q + (size_t)r * a.q_dim + (h * G + g) * hd;
+    float4 v[4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-
-  // kAttnStages - 1 tiles in flight ahead of the one being computed; every iteration
-  // commits exactly one (possibly empty) group so the wait count stays uniform.
+    for (int j = 0; j < 4; ++j)
+      v[j] = (valid && d0 + 4 * j < hd) ? *(const float4*)(src + d0 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint8_t* row = qsm + (size_t)qi * rowb;
 #pragma unroll
-  for (int i = 0; i < kAttnStages - 1; ++i) {
-    if (t0 + i < t1)
-      load_tile(i, t0 + i);
-    else
-      cp_async_commit();
+    for (int j = 0; j < 4; ++j) {
+      kv_store(row, qi, d0 + 4 * j + 0, hd, v[j].x);
+      kv_store(row, qi, d0 + 4 * j + 1, hd, v[j].y);
+      kv_store(row, qi, d0 + 4 * j + 2, hd, v[j].z);
+      kv_store(row, qi, d0 + 4 * j + 3, hd, v[j].w);
+    }
   }
-  for (int tile = t0; tile < t1; ++tile) {
-    const int buf = (tile - t0) % kAttnStages;
-    const int nxt = tile + kAttnStages - 1;
-    if (nxt < t1)
-      load_tile((nxt - t0) % kAttnStages, nxt);
-    else
-      cp_async_commit();
-    cp_async_wait<kAttnStages - 1>();
-    __syncthreads();
-    const float* kt = ks + buf * kAttnTile * hdp;
-    const float* vt = vs + buf * kAttnTile * hdp;
-    // Scores: query qi against keys kg + 8i.
-    float sc[4];
-    {
-      float2 dacc[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) dacc[i] = make_float2(0.f, 0.f);
-      const float* qrow = qs + (qi < 32 ? qi : 0) * hdp;
-      for (int dd = 0; dd < hd; dd += 4) {
-        const float4 qv = *(const float4*)(qrow + dd);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 kv = *(const float4*)(kt + (kg + 8 * i) * hdp + dd);
-          ffma2(dacc[i], make_float2(qv.x, qv.y), make_float2(kv.x, kv.y));
-          ffma2(dacc[i], make_float2(qv.z, qv.w), make_float2(kv.z, kv.w));
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int jg = tile * kAttnTile + kg + 8 * i;
-        const bool vis = qvalid && jg < kend && jg <= p_q;
-        sc[i] = vis ? (dacc[i].x + dacc[i].y) / a.scale : -INFINITY;
-      }
-    }
-    float tmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-    const float m_old = (qi < 32) ? st_m[qi] : -INFINITY;
-    const float m_new = fmaxf(m_old, tmax);
-    float psum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float p = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - m_new);
-      psum += p;
-      if (qi < 32) ps[qi * kAttnTile + kg + 8 * i] = p;
-    }
-    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-    psum += __shfl_xor_sync(0xffffffffu, psum, 4);
-    const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-    __syncthreads();  // everyone has read st_m before it changes
-    if (kg == 0 && qi < 32) {
-      st_m[qi] = m_new;
-      st_l[qi] = st_l[qi] * alpha + psum;
-    }
-    // P.V: dims {4*kg + 32*i + e}.
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] *= alpha;
-    if (qi < nq) {
-      const float* prow = ps + qi * kAttnTile;
-      for (int j = 0; j < kAttnTile; ++j) {
-        const float p = prow[j];
-        const float* vr = vt + j * hdp;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int dd = 4 * kg + 32 * i;
-          if (dd < hd) {
-            const float4 vv = *(const float4*)(vr + dd);
-            acc[4 * i + 0] += p * vv.x;
-            acc[4 * i + 1] += p * vv.y;
-            acc[4 * i + 2] += p * vv.z;
-            acc[4 * i + 3] += p * vv.w;
-          }
-        }
-      }
-    }
-    __syncthreads();  // this buffer is refilled kAttnStages - 1 iterations later
+  for (int q = tid; q < NQ8; q += kAttnThreads) {
+    const int r = q % MT;
+    lim_s[q] = (q < nq && r < m) ? pos + r : -1;
+    m_s[q] = -INFINITY;
+    l_s[q] = 0.f;
   }
-  cp_async_wait<0>();
-
   __syncthreads();
-  // Partial of this split: running max, running sum, unnormalised output.
-  if (qi < nq) {
-    float* dst = a.part + (((size_t)h * a.splits + s) * a.nq_max + qi) * (hd + 2);
-    if (kg == 0) {
-      dst[0] = st_m[qi];
-      dst[1] = st_l[qi];
-    }
+
+  const float inv_scale = 1.0f / a.scale;
+  const int mtd_n = hdk / 16;  // 16-dim tiles of the output
+  const int g4 = lane >> 2, t4 = lane & 3, mat = lane >> 3, l7 = lane & 7;
+  float o[NT][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int dd = 4 * kg + 32 * i;
-      if (dd < hd) {
-        dst[2 + dd + 0] = acc[4 * i + 0];
-        dst[2 + dd + 1] = acc[4 * i + 1];
-        dst[2 + dd + 2] = acc[4 * i + 2];
-        dst[2 + dd + 3] = acc[4 * i + 3];
+  for (int i = 0; i < NT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
+
+  bool ok = true;
+  for (int tile = t0; tile < t1; ++tile) {
+    const int it = tile - t0, bi = it % kAttnStages;
+    const int j0 = tile * kAttnTile, nrows = min(kAttnTile, kend - j0);
+    const uint8_t* kt = kvs + (size_t)bi * 2 * kAttnTile * rowb;
+    const uint8_t* vt = kt + (size_t)kAttnTile * rowb;
+    // V rows past the split's keys are zeroed (P is 0 there, and 0 * stale bits must be 0).
+    for (int e = nrows * rowb / 16 + tid; e < kAttnTile * rowb / 16; e += kAttnThreads)
+      ((uint4*)vt)[e] = make_uint4(0u, 0u, 0u, 0u);
+    const bool mine = mbar_wait(&bar[bi], (uint32_t)(it / kAttnStages) & 1u);
+    if (__syncthreads_or(!mine)) {
+      ok = false;
+      break;
+    }
+
+    // ---- 1. S^T = K . Q^T
+    for (int u = warp; u < 2 * NT; u += 8) {
+      const int mt = u & 1, nt = u >> 1;
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      const int arow = mt * 16 + l7 + (mat & 1) * 8;
+      const uint8_t* krow = kt + (size_t)arow * rowb;
+      const int brow = nt * 8 + l7;
+      const uint8_t* qrow = qsm + (size_t)brow * rowb + (mat >> 1) * 2 * hdk;
+      for (int ks = 0; ks < hdk / 16; ++ks) {
+        uint32_t khi[4], klo[4], qf[4];
+        const int ua = 2 * ks + (mat >> 1);
+        ldmatrix_x4a(khi, krow + ((ua ^ (arow & mask)) << 4));
+        ldmatrix_x4a(klo, krow + 2 * hdk + ((ua ^ (arow & mask)) << 4));
+        const int ub = 2 * ks + (mat & 1);
+        ldmatrix_x4a(qf, qrow + ((ub ^ (brow & mask)) << 4));
+        mma_bf16_16816(acc0, khi, qf[0], qf[1]);
+        mma_bf16_16816(acc1, khi, qf[2], qf[3]);
+        mma_bf16_16816(acc0, klo, qf[0], qf[1]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = mt * 16 + g4 + (e >> 1) * 8, q = nt * 8 + 2 * t4 + (e & 1);
+        const int jg = j0 + key;
+        const bool vis = jg < kend && jg <= lim_s[q];
+        S_s[q * 33 + key] = vis ? (acc0[e] + acc1[e]) * inv_scale : -INFINITY;
+      }
+    }
+    __syncthreads();
+
+    // ---- 2. online softmax, a warp per query, lane = key
+    for (int q = warp; q < NQ8; q += 8) {
+      const float sc = S_s[q * 33 + lane];
+      const float mo = m_s[q];
+      const float mn = fmaxf(mo, warp_max(sc));
+      const float alpha = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
+      const float p = (sc == -INFINITY) ? 0.f : __expf(sc - mn);
+      const float ps = warp_sum(p);
+      uint16_t ph, pl;
+      split_bf16(p, ph, pl);
+      *(uint16_t*)(P_s + (size_t)q * 80 + lane * 2) = ph;
+      *(uint16_t*)(P_s + (size_t)(NQ8 + q) * 80 + lane * 2) = pl;
+      if (lane == 0) {
+        m_s[q] = mn;
+        l_s[q] = l_s[q] * alpha + ps;
+        al_s[q] = alpha;
+      }
+    }
+    __syncthreads();
+
+    // ---- 3. O^T += V^T . P^T
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const int u = warp + 8 * i;
+      if (u >= mtd_n * NT) break;
+      const int mtd = u % mtd_n, nt = u / mtd_n;
+      const float a0 = al_s[nt * 8 + 2 * t4], a1 = al_s[nt * 8 + 2 * t4 + 1];
+      o[i][0] *= a0;
+      o[i][1] *= a1;
+      o[i][2] *= a0;
+      o[i][3] *= a1;
+      uint32_t phi[4], plo[4];
+      const uint8_t* prow = P_s + (size_t)(nt * 8 + l7) * 80 + mat * 16;
+      ldmatrix_x4a(phi, prow);
+      ldmatrix_x4a(plo, prow + (size_t)NQ8 * 80);
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const int vrow = ks * 16 + l7 + 8 * (mat >> 1);
+        const int uv = 2 * mtd + (mat & 1);
+        const uint8_t* va = vt + (size_t)vrow * rowb + ((uv ^ (vrow & mask)) << 4);
+        uint32_t vhi[4], vlo[4];
+        ldmatrix_x4_trans(vhi, va);
+        ldmatrix_x4_trans(vlo, va + 2 * hdk);
+        mma_bf16_16816(o[i], vhi, phi[2 * ks], phi[2 * ks + 1]);
+        mma_bf16_16816(o[i], vhi, plo[2 * ks], plo[2 * ks + 1]);
+        mma_bf16_16816(o[i], vlo, phi[2 * ks], phi[2 * ks + 1]);
+      }
+    }
+    __syncthreads();  // the tile's buffer, S and P are free
+    if (tid == 0 && next_issue < t1) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(next_issue++);
+    }
+  }
+
+  if (!ok) {
+    if (tid == 0) {
+      atomicOr(&a.res->status, ST_TIMEOUT);
+      // Let the copies still in flight land before the shared memory is released.
+      for (int tt = max(t0, next_issue - kAttnStages); tt < next_issue; ++tt)
+        mbar_wait(&bar[(tt - t0) % kAttnStages], (uint32_t)((tt - t0) / kAttnStages) & 1u);
+    }
+    return;
+  }
+
+  // Partial of this split: running max, running sum, unnormalised output.
+  float* pbase = a.part + ((size_t)h * a.splits + s) * a.nq_max * (hd + 4);
+  for (int q = tid; q < nq; q += kAttnThreads) {
+    pbase[(size_t)q * (hd + 4) + 0] = m_s[q];
+    pbase[(size_t)q * (hd + 4) + 1] = l_s[q];
+  }
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int u = warp + 8 * i;
+    if (u >= mtd_n * NT) break;
+    const int mtd = u % mtd_n, nt = u / mtd_n;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int dim = mtd * 16 + g4 + (e >> 1) * 8, q = nt * 8 + 2 * t4 + (e & 1);
+      if (q < nq && dim < hd) pbase[(size_t)q * (hd + 4) + 4 + dim] = o[i][e];
     }
   }
 }
 
 // Merge the splits of one (query head, row): grid (n_heads, m), one thread per dimension.
+// Every split's (max, sum) pair and output value is fetched in one batch of independent loads
+// (up to 32 splits per round trip); the merge weights are exp(max_s - max) in split order.
 template <int MT>
 __global__ void attn_combine_kernel(const AttnArgs a) {
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -233,16 +307,22 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
   const int h = hq / G, g = hq - h * G;
   const int qi = g * MT + r;
   const int hd = a.head_dim;
-  const size_t stride = (size_t)a.nq_max * (hd + 2);
-  const float* base = a.part + ((size_t)h * a.splits * a.nq_max + qi) * (hd + 2);
-  // Per-split (max, sum) pairs are read once into shared memory with independent loads.
+  const size_t stride = (size_t)a.nq_max * (hd + 4);
+  const float* base = a.part + ((size_t)h * a.splits * a.nq_max + qi) * (hd + 4);
   __shared__ float sm_m[256], sm_w[256];
   __shared__ float red_l;
   const int S = a.splits;
   for (int s = threadIdx.x; s < S; s += blockDim.x) {
-    sm_m[s] = __ldcg(base + s * stride);
-    sm_w[s] = __ldcg(base + s * stride + 1);
+    const float2 ml = __ldcg((const float2*)(base + s * stride));
+    sm_m[s] = ml.x;
+    sm_w[s] = ml.y;
   }
+  // Output values of the first 32 splits, in flight while the weights are formed.
+  const int dd = threadIdx.x;
+  float pv[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q)
+    pv[q] = (q < S && dd < hd) ? __ldcg(base + q * stride + 4 + dd) : 0.f;
   __syncthreads();
   if (threadIdx.x == 0) {
     float mx = -INFINITY;
@@ -256,20 +336,13 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     red_l = l;
   }
   __syncthreads();
-  const float inv_l = 1.0f / red_l;
-  for (int dd = threadIdx.x; dd < hd; dd += blockDim.x) {
-    float o = 0.f;
-    for (int s0 = 0; s0 < S; s0 += 8) {
-      float pv[8];
+  if (dd >= hd) return;
+  float o = 0.f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        pv[q] = (s0 + q < S && sm_w[s0 + q] != 0.f) ? __ldcg(base + (s0 + q) * stride + 2 + dd) : 0.f;
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (s0 + q < S) o += pv[q] * sm_w[s0 + q];
-    }
-    store_split<MT>(a.out_split, r, hq * hd + dd, o * inv_l);
-  }
+  for (int q = 0; q < 32; ++q)
+    if (q < S) o += pv[q] * sm_w[q];
+  for (int s = 32; s < S; ++s) o += __ldcg(base + s * stride + 4 + dd) * sm_w[s];
+  store_split<MT>(a.out_split, r, hq * hd + dd, o / red_l);
 }
 
 }  // namespace pp

@@ -19,7 +19,7 @@ constexpr int kConsumerWarps = 8;   // GEMV math warps; one more warp issues TMA
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr int kAttnTile = 32;       // keys per attention tile
 constexpr int kAttnThreads = 256;
-constexpr int kMaxHeadDim = 128;
+constexpr int kMaxHeadDim = 128;   // widest attention head the kernels take
 
 // Bounded-wait budget: every spin on an mbarrier or a counter gives up after this many
 // polls (far beyond any legitimate wait, which ends in microseconds), records ST_TIMEOUT in
@@ -102,6 +102,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
+// Counter increment that publishes this CTA's earlier global writes (release, cumulative over
+// the writes of the threads that met thread 0 at the preceding CTA barrier) and observes those
+// of the CTAs that incremented before it (acquire).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -167,6 +176,33 @@ __device__ __forceinline__ void store_split(uint8_t* base, int m, int k, float v
   split_bf16(v, hi, lo);
   *(uint16_t*)(base + split_offset<MT>(m, k, 0)) = hi;
   *(uint16_t*)(base + split_offset<MT>(m, k, 1)) = lo;
+}
+
+// ---- KV cache layout -----------------------------------------------------------------------
+// The cache holds, per layer and KV head, one row per position: the F32 key (value) vector
+// stored as two BF16 parts, hi = bf16(x) and lo = bf16(x - hi) (x = hi + lo to about 2^-17
+// relative), so the attention kernel feeds it to the tensor cores without a conversion pass.
+// Row j = [hi: hdk BF16][lo: hdk BF16], hdk = head_dim rounded up to the MMA K step (16),
+// padding zero; within each part the 16-byte unit u (dims 8u..8u+7) sits at u ^ (j & mask),
+// mask = min(hdk / 8, 8) - 1, so ldmatrix reads of 8 consecutive rows hit 8 bank groups.
+// A 32-position tile of one head is a contiguous block (one bulk copy).
+__host__ __device__ __forceinline__ int kv_hdk(int hd) { return (hd + 15) & ~15; }
+__host__ __device__ __forceinline__ int kv_row_bytes(int hd) { return 4 * kv_hdk(hd); }
+__host__ __device__ __forceinline__ int kv_swz_mask(int hd) {
+  const int u = kv_hdk(hd) >> 3;
+  return (u < 8 ? u : 8) - 1;
+}
+// Byte offset of (dim d, part 0 = hi / 1 = lo) inside row j.
+__host__ __device__ __forceinline__ int kv_offset(int j, int d, int part, int hd) {
+  return part * 2 * kv_hdk(hd) + ((((d >> 3) ^ (j & kv_swz_mask(hd)))) << 4) + ((d & 7) << 1);
+}
+
+// Writes v as the (hi, lo) parts of dim d of cache row `row` (row j of its head).
+__device__ __forceinline__ void kv_store(uint8_t* row, int j, int d, int hd, float v) {
+  uint16_t hi, lo;
+  split_bf16(v, hi, lo);
+  *(uint16_t*)(row + kv_offset(j, d, 0, hd)) = hi;
+  *(uint16_t*)(row + kv_offset(j, d, 1, hd)) = lo;
 }
 
 // ---- weight layout ------------------------------------------------------------------------

@@ -61,8 +61,8 @@ struct GemvArgs {
   const float* qn;
   const float* kn;
   const float2* rope;  // [capacity][head_dim/2] (cos, sin)
-  float* kcache;       // [n_kv][capacity][head_dim]
-  float* vcache;
+  uint8_t* kcache;     // [n_kv][capacity] rows of kv_row_bytes (split BF16, kv_offset layout)
+  uint8_t* vcache;
   int32_t q_dim, kv_dim, head_dim, capacity;
   // argmax epilogue
   float* logits;  // [M][vocab] when requested by the step flags
@@ -245,14 +245,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   pdl_wait();
   const int mv = a.desc ? a.desc->m : a.m_rows;  // rows that matter: 1 <= mv <= MT
   __shared__ float scale_s[MT];
-  if (tid < MT) {
+  // RMSNorm scale of each row (tiny.rs:20-23) from the per-tile sums of squares: warp m
+  // reads row m's partials with one load per lane and reduces them in a fixed tree.
+  for (int m = warp; m < MT; m += kConsumerWarps) {
     float sc = 1.0f;
-    if (a.ss_in && tid < mv) {
+    if (a.ss_in && m < mv) {
       float t = 0.f;
-      for (int q = 0; q < a.ss_tiles; ++q) t += __ldcg(a.ss_in + q * kMaxRows + tid);
-      sc = 1.0f / sqrtf(t / (float)a.k + a.eps);  // RMSNorm, tiny.rs:20-23
+      for (int q = lane; q < a.ss_tiles; q += 32) t += __ldcg(a.ss_in + q * kMaxRows + m);
+      t = warp_sum(t);
+      sc = 1.0f / sqrtf(t / (float)a.k + a.eps);
     }
-    scale_s[tid] = sc;
+    if (lane == 0) scale_s[m] = sc;
+  }
+  // QKV epilogue constants (q_norm, k_norm, the RoPE rows of this step's positions), staged
+  // while the first weight stages are in flight.
+  constexpr int kQkvHd = EPI == EPI_QKV ? kMaxHeadDim : 1;
+  __shared__ float qkn_s[2][kQkvHd];
+  __shared__ float2 rope_s[EPI == EPI_QKV ? MT : 1][kQkvHd / 2 > 0 ? kQkvHd / 2 : 1];
+  if (EPI == EPI_QKV) {
+    const int hd = a.head_dim, half = hd >> 1;
+    for (int e = tid; e < 2 * hd; e += kConsumerWarps * 32)
+      qkn_s[e / hd][e % hd] = e < hd ? a.qn[e] : a.kn[e - hd];
+    for (int e = tid; e < mv * half; e += kConsumerWarps * 32) {
+      const int m = e / half, i = e - m * half;
+      rope_s[m][i] = a.rope[(size_t)(a.desc->pos + m) * half + i];
+    }
   }
   consumer_sync();
 
@@ -392,6 +409,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     }
     if (!ok) break;
 
+    // Residual values of this tile, loaded now so that their latency overlaps the split-tile
+    // handshake (only the CTA that finishes the tile uses them).
+    constexpr int kPre = (kTileRows * MT + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
+    float xpre[kPre];
+    if (EPI == EPI_RESADD) {
+#pragma unroll
+      for (int j = 0; j < kPre; ++j) {
+        const int e = tid + j * kConsumerWarps * 32;
+        const int m = e / kTileRows, r = e - m * kTileRows;
+        const int n = t * kTileRows + r;
+        xpre[j] = (e < kTileRows * MT && m < mv && n < a.n_out) ? __ldcg(a.out + (size_t)m * a.ldo + n) : 0.f;
+      }
+    }
+
     {  // accumulator fragments (x the RMSNorm scale of their row) -> tile_out[row][m]
       const int g = lane >> 2, tq = lane & 3;
       const int r0 = warp * 16 + g;
@@ -419,13 +450,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       // Split tile: publish this CTA's partial; the last contributor finishes the tile.
       const int slot = (t == first_tile) ? 0 : 1;
       float* mine = a.partials + ((size_t)blockIdx.x * 2 + slot) * kTileRows * MT;
-      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) mine[e] = tile_out[e];
-      __threadfence();
+      for (int e = 4 * tid; e < kTileRows * MT; e += 4 * kConsumerWarps * 32)
+        *(float4*)(mine + e) = *(const float4*)(tile_out + e);
       consumer_sync();
       const int b_lo = sk_owner(tile_begin, T, G), b_hi = sk_owner(tile_end - 1, T, G);
       const int nbk = b_hi - b_lo + 1;
       if (tid == 0) {
-        const uint32_t old = atomicAdd(&a.tile_cnt[t], 1u);
+        const uint32_t old = atom_add_acq_rel_gpu(&a.tile_cnt[t], 1u);
         misc[0] = (old == (uint32_t)(b_hi - b_lo));
       }
       // Where each contributor's partial of this tile sits (its first or its last slot).
@@ -440,21 +471,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         ++t;
         continue;
       }
-      __threadfence();
-      // Sum the contributors' partials in K order; loads are issued in groups of 8
-      // independent reads so the fixup costs about one L2 round trip per group.
-      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
-        float v = 0.f;
-        for (int b0 = 0; b0 < nbk; b0 += 8) {
-          float pv[8];
+      // Sum the contributors' partials in K order. A thread owns 4 consecutive values and
+      // issues the float4 loads of up to 20 contributors at once, so a tile split over 20
+      // CTAs costs one L2 round trip.
+      for (int e = 4 * tid; e < kTileRows * MT; e += 4 * kConsumerWarps * 32) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int b0 = 0; b0 < nbk; b0 += 20) {
+          float4 pv[20];
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            pv[q] = (b0 + q < nbk) ? __ldcg(a.partials + fix_off[b0 + q] + e) : 0.f;
+          for (int q = 0; q < 20; ++q)
+            if (b0 + q < nbk) pv[q] = __ldcg((const float4*)(a.partials + fix_off[b0 + q] + e));
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (b0 + q < nbk) v += pv[q];
+          for (int q = 0; q < 20; ++q)
+            if (b0 + q < nbk) {
+              v.x += pv[q].x;
+              v.y += pv[q].y;
+              v.z += pv[q].z;
+              v.w += pv[q].w;
+            }
         }
-        tile_out[e] = v;
+        *(float4*)(tile_out + e) = v;
       }
       if (tid == 0) a.tile_cnt[t] = 0u;
       consumer_sync();
@@ -467,14 +503,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       // next GEMV streams its input instead of normalising it in a prologue.
       const bool extras = EPI == EPI_RESADD && a.xw_out != nullptr;
       __shared__ float ssr[MT][kTileRows / 32];
-      for (int e = tid; e < kTileRows * MT; e += kConsumerWarps * 32) {
+#pragma unroll
+      for (int j = 0; j < kPre; ++j) {
+        const int e = tid + j * kConsumerWarps * 32;
+        if (e >= kTileRows * MT) break;
         const int m = e / kTileRows, r = e - m * kTileRows;
         const int n = t * kTileRows + r;
         float sq = 0.f;
         if (m < mv && n < a.n_out) {
           float* o = a.out + (size_t)m * a.ldo + n;
           if (EPI == EPI_RESADD) {
-            const float xn = *o + tile_out[r * MT + m];
+            const float xn = xpre[j] + tile_out[r * MT + m];
             *o = xn;
             if (extras) {
               store_split<MT>(a.xw_out, m, n, xn * a.wnext[n]);
@@ -521,27 +560,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         const float* v = tile_out + (size_t)(hl * hd) * MT + m;  // v[i * MT]
         if (n0 < a.q_dim + a.kv_dim) {
           const bool isq = n0 < a.q_dim;
-          const float* w = isq ? a.qn : a.kn;
+          const float* w = qkn_s[isq ? 0 : 1];
           float ssq = 0.f;
           for (int i = lane; i < hd; i += 32) ssq += v[i * MT] * v[i * MT];
           ssq = warp_sum(ssq);
           const float rms = sqrtf(ssq / (float)hd + a.eps);
-          float* dst;
-          if (isq)
-            dst = a.out + (size_t)m * a.ldo + n0;
-          else
-            dst = a.kcache + ((size_t)((n0 - a.q_dim) / hd) * a.capacity + pos) * hd;
-          const float2* rp = a.rope + (size_t)pos * half;
-          for (int i = lane; i < half; i += 32) {
-            const float x0 = v[i * MT] / rms * w[i];
-            const float x1 = v[(i + half) * MT] / rms * w[i + half];
-            const float2 cs = rp[i];
-            dst[i] = x0 * cs.x - x1 * cs.y;
-            dst[i + half] = x1 * cs.x + x0 * cs.y;
+          const float2* rp = rope_s[m];
+          if (isq) {
+            float* dst = a.out + (size_t)m * a.ldo + n0;
+            for (int i = lane; i < half; i += 32) {
+              const float x0 = v[i * MT] / rms * w[i];
+              const float x1 = v[(i + half) * MT] / rms * w[i + half];
+              const float2 cs = rp[i];
+              dst[i] = x0 * cs.x - x1 * cs.y;
+              dst[i + half] = x1 * cs.x + x0 * cs.y;
+            }
+          } else {
+            uint8_t* row = a.kcache + ((size_t)((n0 - a.q_dim) / hd) * a.capacity + pos) * kv_row_bytes(hd);
+            for (int i = lane; i < half; i += 32) {
+              const float x0 = v[i * MT] / rms * w[i];
+              const float x1 = v[(i + half) * MT] / rms * w[i + half];
+              const float2 cs = rp[i];
+              kv_store(row, pos, i, hd, x0 * cs.x - x1 * cs.y);
+              kv_store(row, pos, i + half, hd, x1 * cs.x + x0 * cs.y);
+            }
           }
         } else if (n0 < a.q_dim + 2 * a.kv_dim) {
-          float* dst = a.vcache + ((size_t)((n0 - a.q_dim - a.kv_dim) / hd) * a.capacity + pos) * hd;
-          for (int i = lane; i < hd; i += 32) dst[i] = v[i * MT];
+          uint8_t* row = a.vcache + ((size_t)((n0 - a.q_dim - a.kv_dim) / hd) * a.capacity + pos) * kv_row_bytes(hd);
+          for (int i = lane; i < hd; i += 32) kv_store(row, pos, i, hd, v[i * MT]);
         }
       }
     } else if (EPI == EPI_ARGMAX) {
@@ -596,15 +642,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       r.nonfinite = st_nonf[tid];
       a.recs[(size_t)blockIdx.x * MT + tid] = r;
     }
-    __threadfence();
     consumer_sync();
     if (tid == 0) {
-      const uint32_t old = atomicAdd(a.done_cnt, 1u);
+      const uint32_t old = atom_add_acq_rel_gpu(a.done_cnt, 1u);
       misc[0] = (old == (uint32_t)(G - 1));
     }
     consumer_sync();
     if (!misc[0]) return;
-    __threadfence();
     // Last CTA: reduce every CTA's record, then the accept/mismatch compare of
     // src/specdecode.rs:92-98.
     for (int m = warp; m < mv; m += kConsumerWarps) {

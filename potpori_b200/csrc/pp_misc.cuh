@@ -9,61 +9,47 @@ namespace pp {
 // embedding rows of the chunk's tokens, BF16 decoded to F32 (src/qwen/model.rs:239-241);
 // otherwise x is the hidden state received from the previous shard, checked finite
 // (src/qwen/model.rs:384-386). For the GEMV after it (QKV, or the vocab head of a shard with
-// no layers) this writes split(x * norm_w) in the split activation layout and each row's sum
-// of squares of x into slot 0 of the per-tile partials [ss_tiles][kMaxRows] (other slots 0);
-// the GEMV scales its accumulator by 1 / sqrt(mean(x^2) + eps), the RMSNorm of
-// src/qwen/tiny.rs:20-23. Grid (MT), one block of 256 threads per row; rows past m are left
-// alone.
+// no layers) this writes split(x * norm_w) in the split activation layout and, per 128-column
+// tile, each row's sum of squares of x into the partials [tiles][kMaxRows]; the GEMV scales
+// its accumulator by 1 / sqrt(mean(x^2) + eps), the RMSNorm of src/qwen/tiny.rs:20-23.
+// Grid (ceil(hidden / 128), MT), one thread per column; rows past m are left alone.
 template <int MT>
-__global__ void input_prep_kernel(const uint16_t* __restrict__ table, int32_t hidden,
-                                  int32_t kchunks, int32_t vocab, float* __restrict__ x,
-                                  int32_t ldx, const float* __restrict__ norm_w,
-                                  uint8_t* __restrict__ xw, float* __restrict__ ss,
-                                  int32_t ss_tiles, const StepDesc* desc, StepResult* res,
-                                  int32_t capacity) {
+__global__ void __launch_bounds__(128) input_prep_kernel(
+    const uint16_t* __restrict__ table, int32_t hidden, int32_t kchunks, int32_t vocab,
+    float* __restrict__ x, int32_t ldx, const float* __restrict__ norm_w,
+    uint8_t* __restrict__ xw, float* __restrict__ ss, const StepDesc* desc, StepResult* res,
+    int32_t capacity) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(desc, capacity, MT)) return;
   pdl_wait();
-  const int r = blockIdx.x;
+  const int r = blockIdx.y, tile = blockIdx.x;
   if (r >= desc->m) return;
+  const int n = tile * 128 + threadIdx.x;
   int tok = 0;
   if (table) {
     tok = desc->tokens[r];
     if (tok < 0 || tok >= vocab) {
-      if (threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
+      if (tile == 0 && threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
       return;
     }
   }
-  float* xr = x + (size_t)r * ldx;
-  float sq = 0.f;
-  int bad = 0;
-  for (int k = threadIdx.x; k < hidden; k += blockDim.x) {
-    float v;
+  float v = 0.f;
+  if (n < hidden) {
+    float* xr = x + (size_t)r * ldx;
     if (table) {
-      v = __uint_as_float((uint32_t)table[tiled_offset(tok, k, kchunks)] << 16);
-      xr[k] = v;
+      v = __uint_as_float((uint32_t)table[tiled_offset(tok, n, kchunks)] << 16);
+      xr[n] = v;
     } else {
-      v = xr[k];
-      bad |= !isfinite(v);
+      v = xr[n];
+      if (!isfinite(v)) atomicOr(&res->status, ST_NONFINITE_IN);
     }
-    sq += v * v;
-    if (xw) store_split<MT>(xw, r, k, v * norm_w[k]);
+    if (xw) store_split<MT>(xw, r, n, v * norm_w[n]);
   }
-  __shared__ float red[32];
-  __shared__ int bad_s;
-  if (threadIdx.x == 0) bad_s = 0;
-  __syncthreads();
-  sq = warp_sum(sq);
+  __shared__ float red[4];
+  const float sq = warp_sum(v * v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
-  if (bad) atomicOr(&bad_s, 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-    ss[r] = t;
-    for (int q = 1; q < ss_tiles; ++q) ss[q * kMaxRows + r] = 0.f;
-    if (bad_s) atomicOr(&res->status, ST_NONFINITE_IN);
-  }
+  if (threadIdx.x == 0) ss[tile * kMaxRows + r] = (red[0] + red[1]) + (red[2] + red[3]);
 }
 
 // ---- seeded generator (bit-identical to the oracle's or_gen_bf16) -------------------------
@@ -125,17 +111,17 @@ __global__ void fill_f32_kernel(float* dst, int64_t n, float v) {
 
 // Seeded N(0,1) values (rounded through BF16) for KV rows [0, rows) of one layer: a warm
 // context for benchmarks; the oracle's or_shard_fill_kv writes the same values.
-__global__ void fill_kv_kernel(float* kc, float* vc, int64_t rows, int32_t kv_dim, int32_t n_kv,
-                               int32_t hd, int64_t capacity, uint64_t key) {
+__global__ void fill_kv_kernel(uint8_t* kc, uint8_t* vc, int64_t rows, int32_t kv_dim,
+                               int32_t n_kv, int32_t hd, int64_t capacity, uint64_t key) {
   const int64_t n = rows * kv_dim;
   const float scale = 1.0f / 65536.0f;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = i / kv_dim, col = i - row * kv_dim;
     const int64_t h = col / hd, dd = col - h * hd;
-    const size_t dst = ((size_t)h * capacity + row) * hd + dd;
-    kc[dst] = __uint_as_float((uint32_t)gen_bf16(key, 2 * i, scale) << 16);
-    vc[dst] = __uint_as_float((uint32_t)gen_bf16(key, 2 * i + 1, scale) << 16);
+    const size_t base = ((size_t)h * capacity + row) * kv_row_bytes(hd);
+    kv_store(kc + base, (int)row, (int)dd, hd, __uint_as_float((uint32_t)gen_bf16(key, 2 * i, scale) << 16));
+    kv_store(vc + base, (int)row, (int)dd, hd, __uint_as_float((uint32_t)gen_bf16(key, 2 * i + 1, scale) << 16));
   }
 }
 

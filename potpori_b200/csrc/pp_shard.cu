@@ -94,8 +94,8 @@ struct LayerDev {
   uint16_t* wgu = nullptr;   // [gu_rows][Hp]
   uint16_t* wd = nullptr;    // [d_rows][Ip]
   float* norm[N_COUNT] = {};
-  float* kc = nullptr;  // [n_kv][capacity][hd]
-  float* vc = nullptr;
+  uint8_t* kc = nullptr;  // [n_kv][capacity] rows of kv_row_bytes(hd)
+  uint8_t* vc = nullptr;
   bool mat_set[M_COUNT] = {};
   bool norm_set[N_COUNT] = {};
 };
@@ -151,6 +151,10 @@ struct pp_shard {
   float* h_stage = nullptr;  // pinned [kMaxRows][H]
   int splits = 1, nq_max = 1;
   int max_grid = 148;
+  // Weight stages per GEMV CTA (16 KB each). Fewer stages leave room on each SM for a CTA of
+  // the next kernel, which then prefetches its weights while this one finishes (PDL).
+  // PP_GEMV_STAGES overrides it (2..12).
+  int gemv_max_stages = 12;
   bool use_graphs = true, use_pdl = true;
   cudaGraphExec_t exec[kVariants] = {};
   uint32_t launches = 0;                 // kernels of the step being enqueued
@@ -210,9 +214,9 @@ pp_status after_launch(pp_shard* s, cudaStream_t st, int kind) {
 }
 
 template <int MT, int XM>
-int gemv_stages(int64_t kp, size_t budget) {
+int gemv_stages(int64_t kp, size_t budget, int max_stages) {
   using Lay = GemvSmem<MT, XM>;
-  int ns = 12;
+  int ns = max_stages;
   while (ns > 2 && Lay::total(ns, (int)kp) > budget) --ns;
   return ns;
 }
@@ -231,7 +235,7 @@ pp_status launch_gemv(pp_shard* s, cudaStream_t st, const uint16_t* w, GemvArgs 
   using Lay = GemvSmem<MT, XM>;
   auto kern = gemv_kernel<MT, XM, EPI>;
   const size_t budget = dyn_smem_limit(s, kern);
-  a.nstages = gemv_stages<MT, XM>(a.kp, budget);
+  a.nstages = gemv_stages<MT, XM>(a.kp, budget, s->gemv_max_stages);
   const size_t smem = Lay::total(a.nstages, a.kp);
   if (smem > budget)
     return fail(s, PP_E_UNSUPPORTED, "GEMV with K=%d needs %zu bytes of shared memory", a.k, smem);
@@ -312,10 +316,10 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   {
     // Input rows (embedding or received hidden) and the first GEMV's operand.
     const float* w0 = s->nl ? s->L[0].norm[N_ATTN] : s->final_norm;
-    if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(MT), dim3(256), 0, input_prep_kernel<MT>,
-                          (const uint16_t*)(s->first ? s->embed : nullptr), (int32_t)s->H,
-                          (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x, (int32_t)s->Hp, w0,
-                          w0 ? s->xw_attn : nullptr, s->ss_attn, (int32_t)s->ss_tiles,
+    if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(s->ss_tiles, MT), dim3(128), 0,
+                          input_prep_kernel<MT>, (const uint16_t*)(s->first ? s->embed : nullptr),
+                          (int32_t)s->H, (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x,
+                          (int32_t)s->Hp, w0, w0 ? s->xw_attn : nullptr, s->ss_attn,
                           (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity)))
       return r;
   }
@@ -373,10 +377,14 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     atq.q_dim = s->Q;  // the query buffer is [rows][Q]
     {
       // Split kernel reads q with stride Q; combine writes attn with stride Qp.
-      const size_t smem = attn_smem_bytes(s->hd);
-      if ((r = launch_plain(s, st, PP_K_ATTN, true, dim3(s->nkv, s->splits), dim3(kAttnThreads),
-                            smem, attn_split_kernel<MT>, atq)))
-        return r;
+      const int qpw = (s->G * MT + 7) / 8;  // query tiles of 8 (G * MT query vectors)
+      const size_t smem = attn_smem_bytes(s->hd, qpw);
+      const dim3 grid(s->nkv, s->splits), block(kAttnThreads);
+      r = qpw <= 1   ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 1>, atq)
+          : qpw <= 2 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 2>, atq)
+          : qpw <= 4 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 4>, atq)
+                     : launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 8>, atq);
+      if (r) return r;
       const int tb = s->hd < 32 ? 32 : s->hd;
       if ((r = launch_plain(s, st, PP_K_ATTN_COMBINE, true, dim3(s->nh, MT), dim3(tb), 0,
                             attn_combine_kernel<MT>, at)))
@@ -471,7 +479,10 @@ pp_status set_attrs_mt(pp_shard* s) {
       (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_RESADD>)) ||
       (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_SWIGLU>)) ||
       (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_ARGMAX>)) ||
-      (r = set_max_smem(s, attn_split_kernel<MT>)))
+      (r = set_max_smem(s, attn_split_kernel<MT, 1>)) ||
+      (r = set_max_smem(s, attn_split_kernel<MT, 2>)) ||
+      (r = set_max_smem(s, attn_split_kernel<MT, 4>)) ||
+      (r = set_max_smem(s, attn_split_kernel<MT, 8>)))
     return r;
   return PP_OK;
 }
@@ -777,6 +788,10 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   CK(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->dev));
   CK(cudaDeviceGetAttribute(&s->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, s->dev));
   s->max_grid = s->num_sms;
+  if (const char* e = getenv("PP_GEMV_STAGES")) {
+    const int v = atoi(e);
+    if (v >= 2 && v <= 12) s->gemv_max_stages = v;
+  }
   CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   pp_status r0 = set_attrs(s);
   if (r0) return r0;
@@ -795,8 +810,8 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
     if ((r = dalloc(s, &Ld.norm[N_QN], (size_t)s->hd * 4))) return r;
     if ((r = dalloc(s, &Ld.norm[N_KN], (size_t)s->hd * 4))) return r;
     if ((r = dalloc(s, &Ld.norm[N_FFN], (size_t)s->H * 4))) return r;
-    if ((r = dalloc(s, &Ld.kc, (size_t)s->KV * desc->capacity * 4))) return r;
-    if ((r = dalloc(s, &Ld.vc, (size_t)s->KV * desc->capacity * 4))) return r;
+    if ((r = dalloc(s, &Ld.kc, (size_t)s->nkv * desc->capacity * kv_row_bytes(s->hd)))) return r;
+    if ((r = dalloc(s, &Ld.vc, (size_t)s->nkv * desc->capacity * kv_row_bytes(s->hd)))) return r;
   }
   if (s->first || s->last) {
     if ((r = dalloc(s, &s->embed, (size_t)s->Vp * s->Hp * 2))) return r;
@@ -826,7 +841,7 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   if ((r = dalloc(s, &s->ss_attn, (size_t)s->ss_tiles * kMaxRows * 4))) return r;
   if ((r = dalloc(s, &s->ss_ffn, (size_t)s->ss_tiles * kMaxRows * 4))) return r;
   if (s->last && (r = dalloc(s, &s->logits, (size_t)kMaxRows * s->V * 4))) return r;
-  if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 2) * 4))) return r;
+  if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 4) * 4))) return r;
   if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * 8 * 4))) return r;
   {
     int64_t max_tiles = s->Vp / kTileRows;
@@ -867,8 +882,8 @@ pp_status pp_shard_create(const pp_shard_desc* desc, pp_shard** out) {
       c.hidden % 4 || c.intermediate % 4 ||
       128 % c.head_dim || c.hidden == 0 || c.intermediate == 0 || c.vocab_size == 0)
     return fail(nullptr, PP_E_UNSUPPORTED, "unsupported geometry");
-  if ((c.n_heads / c.n_kv_heads) * 8 > 32)
-    return fail(nullptr, PP_E_UNSUPPORTED, "more than 4 query heads per KV head");
+  if (c.n_heads / c.n_kv_heads > 8)
+    return fail(nullptr, PP_E_UNSUPPORTED, "more than 8 query heads per KV head");
   if (desc->chunk > 8) return fail(nullptr, PP_E_UNSUPPORTED, "chunks above 8 rows are not built");
   if (!encode_fn()) return fail(nullptr, PP_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
   s = new pp_shard();
@@ -1211,8 +1226,8 @@ pp_status pp_shard_reset(pp_shard* s) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
   CK(cudaSetDevice(s->dev));
   for (auto& Ld : s->L) {
-    CK(cudaMemsetAsync(Ld.kc, 0, (size_t)s->KV * s->d.capacity * 4, s->stream));
-    CK(cudaMemsetAsync(Ld.vc, 0, (size_t)s->KV * s->d.capacity * 4, s->stream));
+    CK(cudaMemsetAsync(Ld.kc, 0, (size_t)s->nkv * s->d.capacity * kv_row_bytes(s->hd), s->stream));
+    CK(cudaMemsetAsync(Ld.vc, 0, (size_t)s->nkv * s->d.capacity * kv_row_bytes(s->hd), s->stream));
   }
   CK(cudaStreamSynchronize(s->stream));
   return PP_OK;
