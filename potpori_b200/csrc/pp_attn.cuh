@@ -47,26 +47,48 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Shared memory of attn_split_kernel<MT, NT> (bytes, 128-aligned base):
+// Shared memory of one attention unit (bytes from a 128-aligned base):
 //   K/V tiles [stages][K, V][32 rows][row]  | queries [8*NT rows][row] (cache row format)
 //   scores S[8*NT][33] F32 | probabilities P[hi, lo][8*NT][40] BF16 (80-byte rows)
 //   running max, sum, rescale [8*NT] F32, causal limit [8*NT] int | mbarriers [stages]
 struct AttnSmem {
-  int rowb, nq8;
-  __host__ __device__ AttnSmem(int hd, int nt) : rowb(kv_row_bytes(hd)), nq8(8 * nt) {}
-  __host__ __device__ size_t q_off() const { return (size_t)kAttnStages * 2 * kAttnTile * rowb; }
+  int rowb, nq8, stages;
+  __host__ __device__ AttnSmem(int hd, int nt, int st)
+      : rowb(kv_row_bytes(hd)), nq8(8 * nt), stages(st) {}
+  __host__ __device__ size_t q_off() const { return (size_t)stages * 2 * kAttnTile * rowb; }
   __host__ __device__ size_t s_off() const { return q_off() + (size_t)nq8 * rowb; }
   __host__ __device__ size_t p_off() const { return s_off() + (size_t)nq8 * 33 * 4; }
   __host__ __device__ size_t st_off() const { return p_off() + (size_t)2 * nq8 * 80; }
   __host__ __device__ size_t bar_off() const { return st_off() + (size_t)4 * nq8 * 4; }
-  __host__ __device__ size_t total() const { return bar_off() + 8 * kAttnStages + 128; }
+  __host__ __device__ size_t total() const { return bar_off() + 8 * (size_t)stages; }
 };
-__host__ inline size_t attn_smem_bytes(int hd, int nt) { return AttnSmem(hd, nt).total(); }
+__host__ inline size_t attn_smem_bytes(int hd, int nt) {
+  return AttnSmem(hd, nt, kAttnStages).total() + 128;
+}
 
-// One CTA (8 warps) per (KV head h, key split s); NT = ceil(G*MT / 8) query tiles of 8.
-// Per 32-key tile, on the tensor cores (m16n8k16 BF16, F32 accumulate), with every F32
-// operand carried as hi + lo BF16 and the three products hi.hi + hi.lo + lo.hi (about 2^-16
-// relative, the F32 arithmetic of the reference to within its rounding):
+// OR of a predicate over the 256 consumer threads (named barrier 1).
+__device__ __forceinline__ bool consumer_or(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n"
+      " barrier.red.or.pred po, 1, 256, pi;\n selp.u32 %0, 1, 0, po;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void attn_init_barriers(const AttnSmem& L, uint8_t* sm) {
+  uint64_t* bar = (uint64_t*)(sm + L.bar_off());
+  for (int i = 0; i < L.stages; ++i) mbar_init(&bar[i], 1);
+  fence_barrier_init();
+}
+
+// One (KV head h, key split s) unit on the 8 consumer warps (threads 0..255), NT query tiles
+// of 8 (NT = ceil(G*MT / 8)). Per 32-key tile, on the tensor cores (m16n8k16 BF16, F32
+// accumulate), every F32 operand carried as hi + lo BF16 and the three products
+// hi.hi + hi.lo + lo.hi (about 2^-16 relative, the reference's F32 arithmetic to within its
+// rounding):
 //  1. S^T = K . Q^T: the 32 keys are the M dimension (two m16 tiles), the queries N; a warp
 //     takes one (key tile, query tile) unit; scaled by 1/sqrt(head_dim) and masked (split
 //     range, causal limit pos + r) into S.
@@ -74,15 +96,16 @@ __host__ inline size_t attn_smem_bytes(int hd, int nt) { return AttnSmem(hd, nt)
 //     running sum; P = exp(S - max) written as hi/lo BF16.
 //  3. O^T += V^T . P^T: head dims are M (ldmatrix.trans of the V rows), queries N; a warp owns
 //     16 dims x its query tiles, accumulators rescaled first.
-// K/V tiles are contiguous 32-row blocks of the cache, fetched with one bulk copy each into a
-// kAttnStages ring (mbarrier completion, bounded waits).
+// K/V tiles are contiguous 32-row blocks of the cache, fetched by thread 0 with one bulk copy
+// each into a ring of L.stages buffers (mbarrier completion, bounded waits). `uses` counts the
+// tiles this CTA has taken through the ring before (buffer and parity of the next one); it is
+// advanced on return. Writes the split's partial (max, sum, unnormalised output) and returns
+// false when a wait expired (ST_TIMEOUT set, copies in flight drained).
 template <int MT, int NT>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs a) {
-  extern __shared__ uint8_t attn_smem_raw[];
-  uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
+__device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const AttnSmem& L,
+                                          uint8_t* sm, uint32_t& uses) {
   const int hd = a.head_dim, hdk = kv_hdk(hd), mask = kv_swz_mask(hd);
-  const AttnSmem L(hd, NT);
-  const int rowb = L.rowb;
+  const int rowb = L.rowb, S = L.stages;
   constexpr int NQ8 = 8 * NT;
   uint8_t* kvs = sm;
   uint8_t* qsm = sm + L.q_off();
@@ -95,14 +118,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
   uint64_t* bar = (uint64_t*)(sm + L.bar_off());
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.x, s = blockIdx.y;
-  if (tid == 0) pdl_launch_dependents();
-  if (bad_step(a.desc, a.capacity, MT)) return;
-  if (tid == 0) {
-    for (int i = 0; i < kAttnStages; ++i) mbar_init(&bar[i], 1);
-    fence_barrier_init();
-  }
-  pdl_wait();
   const int pos = a.desc->pos, m = a.desc->m;
   const int G = a.n_heads / a.n_kv;
   const int nq = G * MT;
@@ -113,11 +128,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
   const int kend = min(c, t1 * kAttnTile);  // this split covers keys [t0*32, kend)
   const uint8_t* kb = a.kcache + (size_t)h * a.capacity * rowb;
   const uint8_t* vb = a.vcache + (size_t)h * a.capacity * rowb;
-  __syncthreads();  // barrier init visible to every thread
 
   int next_issue = t0;  // thread 0: first tile not yet requested
   auto issue = [&](int tile) {
-    const int bi = (tile - t0) % kAttnStages;
+    const uint32_t k = uses + (uint32_t)(tile - t0);
+    const int bi = (int)(k % (uint32_t)S);
     const int j0 = tile * kAttnTile;
     const uint32_t bytes = (uint32_t)min(kAttnTile, kend - j0) * rowb;
     uint8_t* dst = kvs + (size_t)bi * 2 * kAttnTile * rowb;
@@ -125,8 +140,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     bulk_load(dst, kb + (size_t)j0 * rowb, bytes, &bar[bi]);
     bulk_load(dst + (size_t)kAttnTile * rowb, vb + (size_t)j0 * rowb, bytes, &bar[bi]);
   };
-  if (tid == 0)
-    for (; next_issue < t1 && next_issue < t0 + kAttnStages; ++next_issue) issue(next_issue);
+  if (tid == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (; next_issue < t1 && next_issue < t0 + S; ++next_issue) issue(next_issue);
+  }
 
   // Queries of this KV head (qi = g * MT + r: query head h*G + g, chunk row r) as hi/lo rows;
   // a thread converts 16 dims with its loads issued together.
@@ -154,7 +171,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     m_s[q] = -INFINITY;
     l_s[q] = 0.f;
   }
-  __syncthreads();
+  consumer_sync();
 
   const float inv_scale = 1.0f / a.scale;
   const int mtd_n = hdk / 16;  // 16-dim tiles of the output
@@ -167,15 +184,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
 
   bool ok = true;
   for (int tile = t0; tile < t1; ++tile) {
-    const int it = tile - t0, bi = it % kAttnStages;
+    const uint32_t k = uses + (uint32_t)(tile - t0);
+    const int bi = (int)(k % (uint32_t)S);
     const int j0 = tile * kAttnTile, nrows = min(kAttnTile, kend - j0);
     const uint8_t* kt = kvs + (size_t)bi * 2 * kAttnTile * rowb;
     const uint8_t* vt = kt + (size_t)kAttnTile * rowb;
     // V rows past the split's keys are zeroed (P is 0 there, and 0 * stale bits must be 0).
     for (int e = nrows * rowb / 16 + tid; e < kAttnTile * rowb / 16; e += kAttnThreads)
       ((uint4*)vt)[e] = make_uint4(0u, 0u, 0u, 0u);
-    const bool mine = mbar_wait(&bar[bi], (uint32_t)(it / kAttnStages) & 1u);
-    if (__syncthreads_or(!mine)) {
+    const bool mine = mbar_wait(&bar[bi], (k / (uint32_t)S) & 1u);
+    if (consumer_or(!mine)) {
       ok = false;
       break;
     }
@@ -207,7 +225,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         S_s[q * 33 + key] = vis ? (acc0[e] + acc1[e]) * inv_scale : -INFINITY;
       }
     }
-    __syncthreads();
+    consumer_sync();
 
     // ---- 2. online softmax, a warp per query, lane = key
     for (int q = warp; q < NQ8; q += 8) {
@@ -227,7 +245,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         al_s[q] = alpha;
       }
     }
-    __syncthreads();
+    consumer_sync();
 
     // ---- 3. O^T += V^T . P^T
 #pragma unroll
@@ -257,7 +275,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         mma_bf16_16816(o[i], vlo, phi[2 * ks], phi[2 * ks + 1]);
       }
     }
-    __syncthreads();  // the tile's buffer, S and P are free
+    consumer_sync();  // the tile's buffer, S and P are free
     if (tid == 0 && next_issue < t1) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(next_issue++);
@@ -267,12 +285,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
   if (!ok) {
     if (tid == 0) {
       atomicOr(&a.res->status, ST_TIMEOUT);
-      // Let the copies still in flight land before the shared memory is released.
-      for (int tt = max(t0, next_issue - kAttnStages); tt < next_issue; ++tt)
-        mbar_wait(&bar[(tt - t0) % kAttnStages], (uint32_t)((tt - t0) / kAttnStages) & 1u);
+      // Let the copies still in flight land before the shared memory is reused or released.
+      for (int tt = max(t0, next_issue - S); tt < next_issue; ++tt) {
+        const uint32_t k = uses + (uint32_t)(tt - t0);
+        mbar_wait(&bar[k % (uint32_t)S], (k / (uint32_t)S) & 1u);
+      }
     }
-    return;
+    return false;
   }
+  uses += (uint32_t)max(0, t1 - t0);
 
   // Partial of this split: running max, running sum, unnormalised output.
   float* pbase = a.part + ((size_t)h * a.splits + s) * a.nq_max * (hd + 4);
@@ -291,40 +312,52 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
       if (q < nq && dim < hd) pbase[(size_t)q * (hd + 4) + 4 + dim] = o[i][e];
     }
   }
+  consumer_sync();  // m_s / l_s and the query rows are free for the next unit
+  return true;
 }
 
-// Merge the splits of one (query head, row): grid (n_heads, m), one thread per dimension.
-// Every split's (max, sum) pair and output value is fetched in one batch of independent loads
-// (up to 32 splits per round trip); the merge weights are exp(max_s - max) in split order.
-template <int MT>
-__global__ void attn_combine_kernel(const AttnArgs a) {
+template <int MT, int NT>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs a) {
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
+  const AttnSmem L(a.head_dim, NT, kAttnStages);
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(a.desc, a.capacity, MT)) return;
+  if (threadIdx.x == 0) attn_init_barriers(L, sm);
   pdl_wait();
-  const int hq = blockIdx.x, r = blockIdx.y;
-  if (r >= a.desc->m) return;
+  consumer_sync();  // barrier init visible to every thread
+  uint32_t uses = 0;
+  attn_unit<MT, NT>(a, blockIdx.x, blockIdx.y, L, sm, uses);
+}
+
+// Merge of the splits of one (query head hq, chunk row r) by `nthr` threads (t = 0..nthr-1,
+// nthr >= head_dim, synchronised on named barrier `bar_id`), one thread per dimension. Every
+// split's (max, sum) pair and output value is fetched in one batch of independent loads (up
+// to 32 splits per round trip); the merge weights are exp(max_s - max), summed in split
+// order. sm_m / sm_w: [splits] floats of shared memory, red_l: one float.
+template <int MT>
+__device__ __forceinline__ void combine_unit(const AttnArgs& a, int hq, int r, int t, int nthr,
+                                             int bar_id, float* sm_m, float* sm_w, float* red_l) {
   const int G = a.n_heads / a.n_kv;
   const int h = hq / G, g = hq - h * G;
   const int qi = g * MT + r;
   const int hd = a.head_dim;
   const size_t stride = (size_t)a.nq_max * (hd + 4);
   const float* base = a.part + ((size_t)h * a.splits * a.nq_max + qi) * (hd + 4);
-  __shared__ float sm_m[256], sm_w[256];
-  __shared__ float red_l;
   const int S = a.splits;
-  for (int s = threadIdx.x; s < S; s += blockDim.x) {
+  for (int s = t; s < S; s += nthr) {
     const float2 ml = __ldcg((const float2*)(base + s * stride));
     sm_m[s] = ml.x;
     sm_w[s] = ml.y;
   }
   // Output values of the first 32 splits, in flight while the weights are formed.
-  const int dd = threadIdx.x;
+  const int dd = t;
   float pv[32];
 #pragma unroll
   for (int q = 0; q < 32; ++q)
     pv[q] = (q < S && dd < hd) ? __ldcg(base + q * stride + 4 + dd) : 0.f;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  named_sync(bar_id, nthr);
+  if (t == 0) {
     float mx = -INFINITY;
     for (int s = 0; s < S; ++s) mx = fmaxf(mx, sm_m[s]);
     float l = 0.f;
@@ -333,16 +366,30 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
       l += sm_w[s] * f;
       sm_w[s] = f;  // now the scale of split s
     }
-    red_l = l;
+    *red_l = l;
   }
-  __syncthreads();
-  if (dd >= hd) return;
-  float o = 0.f;
+  named_sync(bar_id, nthr);
+  if (dd < hd) {
+    float o = 0.f;
 #pragma unroll
-  for (int q = 0; q < 32; ++q)
-    if (q < S) o += pv[q] * sm_w[q];
-  for (int s = 32; s < S; ++s) o += __ldcg(base + s * stride + 4 + dd) * sm_w[s];
-  store_split<MT>(a.out_split, r, hq * hd + dd, o / red_l);
+    for (int q = 0; q < 32; ++q)
+      if (q < S) o += pv[q] * sm_w[q];
+    for (int s = 32; s < S; ++s) o += __ldcg(base + s * stride + 4 + dd) * sm_w[s];
+    store_split<MT>(a.out_split, r, hq * hd + dd, o / *red_l);
+  }
+  named_sync(bar_id, nthr);  // sm_m / sm_w / red_l are free again
+}
+
+// Grid (n_heads, m), block max(32, head_dim) threads.
+template <int MT>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (bad_step(a.desc, a.capacity, MT)) return;
+  pdl_wait();
+  if ((int)blockIdx.y >= a.desc->m) return;
+  __shared__ float sm_m[256], sm_w[256];
+  __shared__ float red_l;
+  combine_unit<MT>(a, blockIdx.x, blockIdx.y, threadIdx.x, blockDim.x, 1, sm_m, sm_w, &red_l);
 }
 
 }  // namespace pp

@@ -139,110 +139,64 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Consumer side of the stage ring: the next stage and its parity. It persists across the
+// GEMVs that share one ring (the persistent step kernel runs many in a row).
+struct RingPos {
+  int s;
+  uint32_t phase;
+};
+
+// Shared-memory pieces of one GEMV CTA.
+struct GemvShared {
+  uint8_t* wst;     // weight stages [ns][16 KB]
+  uint8_t* xst;     // streamed activation stages [ns][split block]
+  uint8_t* xs;      // resident activation (X_RESIDENT_NORM): [kchunks][split block]
+  float* tile_out;  // [128][MT]
+  uint64_t* full;   // [ns], one arrival (producer) + transaction bytes
+  uint64_t* empty;  // [ns], one arrival per consumer warp
+  int32_t* misc;    // [0] fixup flag, [1] status bits, [8..] argmax running state (4 x MT)
+  int ns;
+};
+
+// The eight consumer warps of one GEMV over this CTA's stream-K range (CTA `bid` of `G`):
+// stages are taken from the ring at `rp` (advanced on return), the MMAs accumulate each tile
+// segment, split tiles are finished by their last contributor, and the epilogue EPI runs on
+// every finished tile. The caller has made the activation inputs visible (PDL wait or grid
+// barrier). Returns false when a bounded wait expired (ST_TIMEOUT is set).
 template <int MT, int XM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+__device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const GemvShared& sh, RingPos& rp,
+                                             uint32_t G, uint32_t bid) {
   using L = GemvSmem<MT, XM>;
   constexpr int R = SplitRows<MT>::R;
   constexpr int NB = R / 8;  // 8-row MMA column blocks
   constexpr int XB = SplitRows<MT>::kBlock;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int ns = a.nstages;
-  uint8_t* wst = smem;
-  uint8_t* xst = smem + L::x_off(ns);
-  uint8_t* xs = smem + L::xs_off(ns);
-  float* tile_out = (float*)(smem + L::tile_off(ns, a.kp));
-  uint64_t* full = (uint64_t*)(smem + L::bar_off(ns, a.kp));
-  uint64_t* empty = full + ns;
-  int32_t* misc = (int32_t*)(smem + L::misc_off(ns, a.kp));
-  // misc: [0] fixup flag, [1] status bits, [8..] argmax running state (4 x MT words)
+  const int ns = sh.ns;
+  uint8_t* wst = sh.wst;
+  uint8_t* xst = sh.xst;
+  uint8_t* xs = sh.xs;
+  float* tile_out = sh.tile_out;
+  uint64_t* full = sh.full;
+  uint64_t* empty = sh.empty;
+  int32_t* misc = sh.misc;
   float* st_best = (float*)(misc + 8);
   int32_t* st_idx = misc + 8 + MT;
   float* st_second = (float*)(misc + 8 + 2 * MT);
   int32_t* st_nonf = misc + 8 + 3 * MT;
-
-  if (a.desc ? bad_step(a.desc, a.capacity, MT) : (a.m_rows < 1 || a.m_rows > MT)) return;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const uint32_t T = (uint32_t)a.tiles * (uint32_t)a.kchunks;
-  const uint32_t G = gridDim.x;
-  const int i0 = sk_start(blockIdx.x, T, G), i1 = sk_start(blockIdx.x + 1, T, G);
+  const int i0 = sk_start(bid, T, G), i1 = sk_start(bid + 1, T, G);
   const int first_tile = (int)(i0 / a.kchunks);
-
   if (tid == 0) {
-    for (int s = 0; s < ns; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    fence_barrier_init();
     misc[0] = 0;
     misc[1] = 0;
-    pdl_launch_dependents();
   }
-  if (tid < MT) {
+  if (EPI == EPI_ARGMAX && tid < MT) {
     st_best[tid] = -INFINITY;
     st_idx[tid] = 0x7fffffff;
     st_second[tid] = -INFINITY;
     st_nonf[tid] = 0;
   }
-  __syncthreads();
-
-  // ------------------------------------------------------------------ producer warp
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      const int n_it = i1 - i0;
-      const int pre = n_it < ns ? n_it : ns;
-      const uint32_t bytes = L::kWBytes + L::kXBytes;
-      const int kc = a.kchunks;
-      // (tile, chunk) of the next weight block, advanced without divisions.
-      int wt = i0 / kc, wc = i0 - (i0 / kc) * kc;
-      auto next_w = [&]() {
-        const uint16_t* src = a.w + ((size_t)wt * kc + wc) * (kTileRows * kChunkK);
-        if (++wc == kc) {
-          wc = 0;
-          ++wt;
-        }
-        return src;
-      };
-      int xc = wc;  // chunk of the next activation block
-      auto next_x = [&]() {
-        const uint8_t* src = a.xsplit + (size_t)xc * XB;
-        if (++xc == kc) xc = 0;
-        return src;
-      };
-      for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
-        mbar_arrive_expect_tx(&full[i], bytes);
-        bulk_load(wst + (size_t)i * L::kWBytes, next_w(), L::kWBytes, &full[i]);
-      }
-      pdl_wait();
-      if (XM == X_STREAM)
-        for (int i = 0; i < pre; ++i) bulk_load(xst + (size_t)i * XB, next_x(), XB, &full[i]);
-      int issued = pre;
-      int s = pre % ns;
-      uint32_t use = pre / ns;
-      for (int i = pre; i < n_it; ++i) {
-        if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_load(wst + (size_t)s * L::kWBytes, next_w(), L::kWBytes, &full[s]);
-        if (XM == X_STREAM) bulk_load(xst + (size_t)s * XB, next_x(), XB, &full[s]);
-        issued = i + 1;
-        if (++s == ns) {
-          s = 0;
-          ++use;
-        }
-      }
-      if (issued < n_it) {
-        if (a.res) atomicOr(&a.res->status, ST_TIMEOUT);
-        // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int j = (issued > ns ? issued - ns : 0); j < issued; ++j)
-          mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------------ consumer warps
-  pdl_wait();
   const int mv = a.desc ? a.desc->m : a.m_rows;  // rows that matter: 1 <= mv <= MT
   __shared__ float scale_s[MT];
   // RMSNorm scale of each row (tiny.rs:20-23) from the per-tile sums of squares: warp m
@@ -350,8 +304,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   const int mat = lane >> 3, l7 = lane & 7;
   const int arow = warp * 16 + l7 + (mat & 1) * 8;
   int it = i0;
-  int cs = 0;           // ring stage of the next iteration
-  uint32_t cphase = 0;  // its parity
+  int cs = rp.s;             // ring stage of the next iteration
+  uint32_t cphase = rp.phase;  // its parity
   bool ok = true;
   int t = i0 / a.kchunks;
   while (it < i1 && ok) {
@@ -627,9 +581,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     ++t;
   }
 
+  rp.s = cs;
+  rp.phase = cphase;
   if (!ok) {
     if (tid == 0 && a.res) atomicOr(&a.res->status, ST_TIMEOUT);
-    return;
+    return false;
   }
 
   if (EPI == EPI_ARGMAX) {
@@ -648,7 +604,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       misc[0] = (old == (uint32_t)(G - 1));
     }
     consumer_sync();
-    if (!misc[0]) return;
+    if (!misc[0]) return true;
     // Last CTA: reduce every CTA's record, then the accept/mismatch compare of
     // src/specdecode.rs:92-98.
     for (int m = warp; m < mv; m += kConsumerWarps) {
@@ -690,6 +646,105 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       *a.done_cnt = 0u;
     }
   }
+  return true;
+}
+
+template <int MT, int XM, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+  using L = GemvSmem<MT, XM>;
+  constexpr int XB = SplitRows<MT>::kBlock;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int ns = a.nstages;
+  GemvShared sh;
+  sh.wst = smem;
+  sh.xst = smem + L::x_off(ns);
+  sh.xs = smem + L::xs_off(ns);
+  sh.tile_out = (float*)(smem + L::tile_off(ns, a.kp));
+  sh.full = (uint64_t*)(smem + L::bar_off(ns, a.kp));
+  sh.empty = sh.full + ns;
+  sh.misc = (int32_t*)(smem + L::misc_off(ns, a.kp));
+  sh.ns = ns;
+  uint8_t* wst = sh.wst;
+  uint8_t* xst = sh.xst;
+  uint64_t* full = sh.full;
+  uint64_t* empty = sh.empty;
+
+  if (a.desc ? bad_step(a.desc, a.capacity, MT) : (a.m_rows < 1 || a.m_rows > MT)) return;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const uint32_t T = (uint32_t)a.tiles * (uint32_t)a.kchunks;
+  const uint32_t G = gridDim.x;
+  const int i0 = sk_start(blockIdx.x, T, G), i1 = sk_start(blockIdx.x + 1, T, G);
+
+  if (tid == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_barrier_init();
+    pdl_launch_dependents();
+  }
+  __syncthreads();
+  // ------------------------------------------------------------------ producer warp
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      const int n_it = i1 - i0;
+      const int pre = n_it < ns ? n_it : ns;
+      const uint32_t bytes = L::kWBytes + L::kXBytes;
+      const int kc = a.kchunks;
+      // (tile, chunk) of the next weight block, advanced without divisions.
+      int wt = i0 / kc, wc = i0 - (i0 / kc) * kc;
+      auto next_w = [&]() {
+        const uint16_t* src = a.w + ((size_t)wt * kc + wc) * (kTileRows * kChunkK);
+        if (++wc == kc) {
+          wc = 0;
+          ++wt;
+        }
+        return src;
+      };
+      int xc = wc;  // chunk of the next activation block
+      auto next_x = [&]() {
+        const uint8_t* src = a.xsplit + (size_t)xc * XB;
+        if (++xc == kc) xc = 0;
+        return src;
+      };
+      for (int i = 0; i < pre; ++i) {  // weights only: safe before the previous kernel ends
+        mbar_arrive_expect_tx(&full[i], bytes);
+        bulk_load(wst + (size_t)i * L::kWBytes, next_w(), L::kWBytes, &full[i]);
+      }
+      pdl_wait();
+      if (XM == X_STREAM)
+        for (int i = 0; i < pre; ++i) bulk_load(xst + (size_t)i * XB, next_x(), XB, &full[i]);
+      int issued = pre;
+      int s = pre % ns;
+      uint32_t use = pre / ns;
+      for (int i = pre; i < n_it; ++i) {
+        if (!mbar_wait(&empty[s], (use - 1) & 1)) break;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_load(wst + (size_t)s * L::kWBytes, next_w(), L::kWBytes, &full[s]);
+        if (XM == X_STREAM) bulk_load(xst + (size_t)s * XB, next_x(), XB, &full[s]);
+        issued = i + 1;
+        if (++s == ns) {
+          s = 0;
+          ++use;
+        }
+      }
+      if (issued < n_it) {
+        if (a.res) atomicOr(&a.res->status, ST_TIMEOUT);
+        // Let the copies already issued land before the CTA's shared memory goes away.
+        for (int j = (issued > ns ? issued - ns : 0); j < issued; ++j)
+          mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);
+      }
+    }
+    return;
+  }
+
+
+  // ------------------------------------------------------------------ consumer warps
+  pdl_wait();
+  RingPos rp{0, 0u};
+  gemv_consume<MT, XM, EPI>(a, sh, rp, G, blockIdx.x);
 }
 
 }  // namespace pp

@@ -13,43 +13,61 @@ namespace pp {
 // tile, each row's sum of squares of x into the partials [tiles][kMaxRows]; the GEMV scales
 // its accumulator by 1 / sqrt(mean(x^2) + eps), the RMSNorm of src/qwen/tiny.rs:20-23.
 // Grid (ceil(hidden / 128), MT), one thread per column; rows past m are left alone.
+struct PrepArgs {
+  const uint16_t* table;  // embedding (first shard) or NULL (hidden input in x)
+  int32_t hidden, kchunks, vocab;
+  float* x;
+  int32_t ldx;
+  const float* norm_w;  // norm of the first GEMV; NULL: no operand to write
+  uint8_t* xw;
+  float* ss;
+  const StepDesc* desc;
+  StepResult* res;
+};
+
+// One (128-column tile, chunk row r) unit by 128 threads (t = 0..127, named barrier bar_id);
+// red: 4 floats of shared memory.
 template <int MT>
-__global__ void __launch_bounds__(128) input_prep_kernel(
-    const uint16_t* __restrict__ table, int32_t hidden, int32_t kchunks, int32_t vocab,
-    float* __restrict__ x, int32_t ldx, const float* __restrict__ norm_w,
-    uint8_t* __restrict__ xw, float* __restrict__ ss, const StepDesc* desc, StepResult* res,
-    int32_t capacity) {
-  if (threadIdx.x == 0) pdl_launch_dependents();
-  if (bad_step(desc, capacity, MT)) return;
-  pdl_wait();
-  const int r = blockIdx.y, tile = blockIdx.x;
-  if (r >= desc->m) return;
-  const int n = tile * 128 + threadIdx.x;
+__device__ __forceinline__ void prep_unit(const PrepArgs& p, int tile, int r, int t, int bar_id,
+                                          float* red) {
+  const int n = tile * 128 + t;
+  bool skip = false;
   int tok = 0;
-  if (table) {
-    tok = desc->tokens[r];
-    if (tok < 0 || tok >= vocab) {
-      if (tile == 0 && threadIdx.x == 0) atomicOr(&res->status, ST_BAD_STEP);
-      return;
+  if (p.table) {
+    tok = p.desc->tokens[r];
+    if (tok < 0 || tok >= p.vocab) {
+      if (tile == 0 && t == 0) atomicOr(&p.res->status, ST_BAD_STEP);
+      skip = true;  // uniform over the unit
     }
   }
   float v = 0.f;
-  if (n < hidden) {
-    float* xr = x + (size_t)r * ldx;
-    if (table) {
-      v = __uint_as_float((uint32_t)table[tiled_offset(tok, n, kchunks)] << 16);
+  if (!skip && n < p.hidden) {
+    float* xr = p.x + (size_t)r * p.ldx;
+    if (p.table) {
+      v = __uint_as_float((uint32_t)p.table[tiled_offset(tok, n, p.kchunks)] << 16);
       xr[n] = v;
     } else {
       v = xr[n];
-      if (!isfinite(v)) atomicOr(&res->status, ST_NONFINITE_IN);
+      if (!isfinite(v)) atomicOr(&p.res->status, ST_NONFINITE_IN);
     }
-    if (xw) store_split<MT>(xw, r, n, v * norm_w[n]);
+    if (p.norm_w) store_split<MT>(p.xw, r, n, v * p.norm_w[n]);
   }
-  __shared__ float red[4];
   const float sq = warp_sum(v * v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
-  __syncthreads();
-  if (threadIdx.x == 0) ss[tile * kMaxRows + r] = (red[0] + red[1]) + (red[2] + red[3]);
+  if ((t & 31) == 0) red[t >> 5] = sq;
+  named_sync(bar_id, 128);
+  if (t == 0) p.ss[tile * kMaxRows + r] = (red[0] + red[1]) + (red[2] + red[3]);
+  named_sync(bar_id, 128);  // red is free again
+}
+
+// Grid (ceil(hidden / 128), MT), 128 threads; rows past m are left alone.
+template <int MT>
+__global__ void __launch_bounds__(128) input_prep_kernel(const PrepArgs p, int32_t capacity) {
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (bad_step(p.desc, capacity, MT)) return;
+  pdl_wait();
+  if ((int)blockIdx.y >= p.desc->m) return;
+  __shared__ float red[4];
+  prep_unit<MT>(p, blockIdx.x, blockIdx.y, threadIdx.x, 1, red);
 }
 
 // ---- seeded generator (bit-identical to the oracle's or_gen_bf16) -------------------------

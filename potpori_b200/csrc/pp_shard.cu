@@ -316,11 +316,20 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   {
     // Input rows (embedding or received hidden) and the first GEMV's operand.
     const float* w0 = s->nl ? s->L[0].norm[N_ATTN] : s->final_norm;
+    PrepArgs pa = {};
+    pa.table = s->first ? s->embed : nullptr;
+    pa.hidden = s->H;
+    pa.kchunks = (int32_t)(s->Hp / kChunkK);
+    pa.vocab = s->V;
+    pa.x = s->x;
+    pa.ldx = (int32_t)s->Hp;
+    pa.norm_w = w0;
+    pa.xw = s->xw_attn;
+    pa.ss = s->ss_attn;
+    pa.desc = s->d_desc;
+    pa.res = s->d_res;
     if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(s->ss_tiles, MT), dim3(128), 0,
-                          input_prep_kernel<MT>, (const uint16_t*)(s->first ? s->embed : nullptr),
-                          (int32_t)s->H, (int32_t)(s->Hp / kChunkK), (int32_t)s->V, s->x,
-                          (int32_t)s->Hp, w0, w0 ? s->xw_attn : nullptr, s->ss_attn,
-                          (const StepDesc*)s->d_desc, s->d_res, (int32_t)s->d.capacity)))
+                          input_prep_kernel<MT>, pa, (int32_t)s->d.capacity)))
       return r;
   }
   for (int l = 0; l < s->nl; ++l) {
