@@ -151,10 +151,10 @@ struct pp_shard {
   float* h_stage = nullptr;  // pinned [kMaxRows][H]
   int splits = 1, nq_max = 1;
   int max_grid = 148;
-  // Weight stages per GEMV CTA (16 KB each). Fewer stages leave room on each SM for a CTA of
-  // the next kernel, which then prefetches its weights while this one finishes (PDL).
-  // PP_GEMV_STAGES overrides it (2..12).
-  int gemv_max_stages = 12;
+  // Weight stages per GEMV CTA (16 KB each): 6 to 8 in flight per SM already stream the
+  // vocabulary head at the measured HBM copy rate in a chain of launches; 12 is slightly
+  // slower. PP_GEMV_STAGES overrides it (2..12).
+  int gemv_max_stages = 8;
   bool use_graphs = true, use_pdl = true;
   cudaGraphExec_t exec[kVariants] = {};
   uint32_t launches = 0;                 // kernels of the step being enqueued
