@@ -14,21 +14,27 @@ Ordering is by streams only: NCCL transfers are enqueued on each shard's stream 
 torch.cuda.ExternalStream), so nothing waits on the host except the head's poll and each
 stage's look at the header it just received (to notice the end of the session).
 A header with m = 0 ends the session; flag bits mark the benchmark's timed window.
+
+The protocol (run_stage, DistChain) talks to its stage through a small I/O object:
+CudaStageIO (a Shard's device buffers and stream: the product path) or any object with the
+same methods, such as a host-memory stand-in that lets the protocol run under gloo on CPU.
 """
 from __future__ import annotations
 
+import contextlib
+import time
 from collections import deque
-from typing import List
+from typing import List, Tuple
 
 import torch
 import torch.distributed as dist
 
 from .config import is_eos
-from .shard import Shard
 from .target import NonFiniteLogits
 
 HDR_INTS = 36   # StepDesc: pos, m, n_drafts, flags, tokens[16], drafts[16]
 RES_INTS = 52   # StepResult: argmax[16], top1[16], top2[16], nonfinite_rows, n_acc, corr, status
+RES_NONFINITE, RES_STATUS = 48, 51
 RING = 64
 FLAG_WINDOW_START = 2
 FLAG_WINDOW_END = 4
@@ -45,72 +51,187 @@ def device_tensor(ptr: int, n: int, dtype, device: int) -> torch.Tensor:
     return torch.as_tensor(_DevArray(ptr, n, ts), device=torch.device("cuda", device))
 
 
-class _Bufs:
-    def __init__(self, shard: Shard, width: int):
+class CudaStageIO:
+    """A shard's resident buffers (hidden rows, step header, step result) as tensors, its
+    stream as the ordering of every transfer, and events for the timed window."""
+
+    def __init__(self, shard, width: int):
         hid, hdr, res = shard.buffers()
         dev = shard.device
+        self.shard, self.width, self.device = shard, width, dev
+        self.first, self.last = shard.first, shard.last
         self.hid = device_tensor(hid, width * shard.cfg.hidden, torch.float32, dev)
         self.hdr = device_tensor(hdr, HDR_INTS, torch.int32, dev)
         self.res = device_tensor(res, RES_INTS, torch.int32, dev)
         self.stream = torch.cuda.ExternalStream(shard.stream(), device=torch.device("cuda", dev))
+        self._host_hdr = torch.empty(HDR_INTS, dtype=torch.int32, pin_memory=True)
+        self._host_res = torch.empty(RES_INTS, dtype=torch.int32, pin_memory=True)
+        self._seen = torch.cuda.Event()
+        self._t0 = torch.cuda.Event(enable_timing=True)
+        self._t1 = torch.cuda.Event(enable_timing=True)
+
+    def ordered(self):
+        return torch.cuda.stream(self.stream)
+
+    def read_header(self) -> Tuple[int, int]:
+        """(rows, flags) of the header that just arrived (waits for it on the host)."""
+        self._host_hdr.copy_(self.hdr, non_blocking=True)
+        self._seen.record(self.stream)
+        self._seen.synchronize()
+        return int(self._host_hdr[1]), int(self._host_hdr[3])
+
+    def set_step(self, pos: int, m: int, tokens, drafts, flags: int) -> None:
+        self.shard.set_step(pos, m, tokens=tokens, drafts=drafts, flags=flags)
+
+    def step(self) -> None:
+        self.shard.step_device(self.width, stream=self.shard.stream())
+
+    def mark_start(self) -> None:
+        self._t0.record(self.stream)
+
+    def mark_end(self) -> None:
+        self._t1.record(self.stream)
+
+    def elapsed_ms(self) -> float:
+        return self._t0.elapsed_time(self._t1)
+
+    def finish(self) -> None:
+        torch.cuda.synchronize(self.device)
+
+    def result_slots(self, n: int) -> torch.Tensor:
+        return torch.zeros((n, RES_INTS), dtype=torch.int32, device=torch.device("cuda", self.device))
+
+    def fetch(self, slot_row: torch.Tensor) -> List[int]:
+        self._host_res.copy_(slot_row, non_blocking=True)
+        self.stream.synchronize()
+        return self._host_res.tolist()
+
+    def stop_header(self, flags: int) -> torch.Tensor:
+        stop = torch.zeros(HDR_INTS, dtype=torch.int32, device=torch.device("cuda", self.device))
+        stop[3] = flags
+        return stop
+
+    def drain(self) -> None:
+        self.stream.synchronize()
+
+    def capacity(self) -> int:
+        return self.shard.capacity()
+
+    def chunk_size(self) -> int:
+        return self.shard.chunk_size()
 
 
-def run_stage(shard: Shard, rank: int, world: int, width: int) -> float:
-    """Serve as stage `rank` until the session ends. Returns the device time (ms) between the
-    timed-window marks, measured with events on this stage's stream."""
-    b = _Bufs(shard, width)
-    host_hdr = torch.empty(HDR_INTS, dtype=torch.int32, pin_memory=True)
-    seen = torch.cuda.Event()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+class HostStageIO:
+    """The same interface over host tensors and a host `stage` object with `step(hdr, hid,
+    res)`: runs the protocol under gloo without a GPU (tests of the multi-process logic)."""
+
+    def __init__(self, stage, width: int, hidden: int, first: bool, last: bool,
+                 capacity: int = 4096, chunk: int = 8):
+        self.stage, self.width = stage, width
+        self.first, self.last = first, last
+        self.hid = torch.zeros(width * hidden, dtype=torch.float32)
+        self.hdr = torch.zeros(HDR_INTS, dtype=torch.int32)
+        self.res = torch.zeros(RES_INTS, dtype=torch.int32)
+        self._cap, self._chunk = capacity, chunk
+        self._t0 = self._t1 = 0.0
+
+    def ordered(self):
+        return contextlib.nullcontext()
+
+    def read_header(self) -> Tuple[int, int]:
+        return int(self.hdr[1]), int(self.hdr[3])
+
+    def set_step(self, pos: int, m: int, tokens, drafts, flags: int) -> None:
+        self.hdr.zero_()
+        self.hdr[0], self.hdr[1], self.hdr[2], self.hdr[3] = pos, m, len(drafts), flags
+        self.hdr[4:4 + m] = torch.tensor(tokens, dtype=torch.int32)
+        if drafts:
+            self.hdr[20:20 + len(drafts)] = torch.tensor(drafts, dtype=torch.int32)
+
+    def step(self) -> None:
+        self.stage.step(self.hdr, self.hid, self.res)
+
+    def mark_start(self) -> None:
+        self._t0 = time.perf_counter()
+
+    def mark_end(self) -> None:
+        self._t1 = time.perf_counter()
+
+    def elapsed_ms(self) -> float:
+        return (self._t1 - self._t0) * 1e3
+
+    def finish(self) -> None:
+        pass
+
+    def result_slots(self, n: int) -> torch.Tensor:
+        return torch.zeros((n, RES_INTS), dtype=torch.int32)
+
+    def fetch(self, slot_row: torch.Tensor) -> List[int]:
+        return slot_row.tolist()
+
+    def stop_header(self, flags: int) -> torch.Tensor:
+        stop = torch.zeros(HDR_INTS, dtype=torch.int32)
+        stop[3] = flags
+        return stop
+
+    def drain(self) -> None:
+        pass
+
+    def capacity(self) -> int:
+        return self._cap
+
+    def chunk_size(self) -> int:
+        return self._chunk
+
+
+def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
+    """Serve as stage `rank` (1 <= rank < world) until the session ends. Returns the time (ms)
+    between the timed-window marks, measured on this stage's stream (0 without both marks)."""
+    io = io or CudaStageIO(shard, width)
     started = ended = False
-    with torch.cuda.stream(b.stream):
+    with io.ordered():
         while True:
-            w1 = dist.irecv(b.hdr, rank - 1)
-            w2 = dist.irecv(b.hid, rank - 1)
+            w1 = dist.irecv(io.hdr, rank - 1)
+            w2 = dist.irecv(io.hid, rank - 1)
             w1.wait()
             w2.wait()
-            host_hdr.copy_(b.hdr, non_blocking=True)
-            seen.record(b.stream)
-            seen.synchronize()
-            m, flags = int(host_hdr[1]), int(host_hdr[3])
+            m, flags = io.read_header()
             if flags & FLAG_WINDOW_START and not started:
-                t_start.record(b.stream)
+                io.mark_start()
                 started = True
             if flags & FLAG_WINDOW_END and started and not ended:
-                t_end.record(b.stream)
+                io.mark_end()
                 ended = True
             if m > 0:
-                shard.step_device(width, stream=shard.stream())
-            if shard.last:
+                io.step()
+            if io.last:
                 if m == 0:
                     break
-                w = dist.isend(b.res, 0)
+                w = dist.isend(io.res, 0)
                 w.wait()
             else:
-                w1 = dist.isend(b.hdr, rank + 1)
-                w2 = dist.isend(b.hid, rank + 1)
+                w1 = dist.isend(io.hdr, rank + 1)
+                w2 = dist.isend(io.hid, rank + 1)
                 w1.wait()
                 w2.wait()
                 if m == 0:
                     break
-    torch.cuda.synchronize(shard.device)
-    return t_start.elapsed_time(t_end) if (started and ended) else 0.0
+    io.finish()
+    return io.elapsed_ms() if (started and ended) else 0.0
 
 
 class DistChain:
     """The head's view of the multi-process chain (PipelinedChain / TargetChain)."""
 
-    def __init__(self, stage0: Shard, world: int, width: int):
-        assert stage0.first and not stage0.last and world > 1
-        self.stage0, self.world, self.width = stage0, world, width
-        self.b = _Bufs(stage0, width)
-        dev = torch.device("cuda", stage0.device)
-        self.slots = torch.zeros((RING, RES_INTS), dtype=torch.int32, device=dev)
-        self.host = torch.empty((RING, RES_INTS), dtype=torch.int32, pin_memory=True)
+    def __init__(self, stage0, world: int, width: int, io=None):
+        self.io = io or CudaStageIO(stage0, width)
+        assert self.io.first and not self.io.last and world > 1
+        self.world, self.width = world, width
+        self.slots = self.io.result_slots(RING)
         self.inflight: deque = deque()
         self.slot = 0
-        self.capacity_ = stage0.capacity()
-        self.chunk = stage0.chunk_size() or width
+        self.capacity_ = self.io.capacity()
+        self.chunk = self.io.chunk_size() or width
         self.pending_flags = 0
         self.submitted = 0
 
@@ -124,13 +245,13 @@ class DistChain:
     def submit(self, pos: int, cur: int, drafts: List[int]) -> None:
         tokens = [cur] + list(drafts)
         m = len(tokens)
-        s0 = self.stage0
-        with torch.cuda.stream(self.b.stream):
-            s0.set_step(pos, m, tokens=tokens, drafts=drafts, flags=self.pending_flags)
+        io = self.io
+        with io.ordered():
+            io.set_step(pos, m, tokens, list(drafts), self.pending_flags)
             self.pending_flags = 0
-            s0.step_device(self.width)
-            w1 = dist.isend(self.b.hdr, 1)
-            w2 = dist.isend(self.b.hid, 1)
+            io.step()
+            w1 = dist.isend(io.hdr, 1)
+            w2 = dist.isend(io.hid, 1)
             w1.wait()
             w2.wait()
             wr = dist.irecv(self.slots[self.slot], self.world - 1)
@@ -140,18 +261,14 @@ class DistChain:
 
     def poll(self) -> List[int]:
         slot, m, wr = self.inflight.popleft()
-        with torch.cuda.stream(self.b.stream):
+        with self.io.ordered():
             wr.wait()
-            self.host[slot].copy_(self.slots[slot], non_blocking=True)
-        self.b.stream.synchronize()
-        r = self.host[slot]
-        argmax = r[:m].tolist()
-        nonfinite = int(r[48])
-        if nonfinite or int(r[51]) & 8:
+            r = self.io.fetch(self.slots[slot])
+        if r[RES_NONFINITE] or r[RES_STATUS] & 8:
             raise NonFiniteLogits("the shard produced missing or non-finite logits")
-        if int(r[51]) & 5:
-            raise RuntimeError(f"chain step failed (status {int(r[51])})")
-        return argmax
+        if r[RES_STATUS] & 5:
+            raise RuntimeError(f"chain step failed (status {r[RES_STATUS]})")
+        return r[:m]
 
     def prefill(self, prompt: List[int]) -> int:
         pos = 0
@@ -178,13 +295,12 @@ class DistChain:
         """End the session on every stage (a header with m = 0 carries any pending marks)."""
         while self.inflight:
             slot, m, wr = self.inflight.popleft()
-            with torch.cuda.stream(self.b.stream):
+            with self.io.ordered():
                 wr.wait()
-        stop = torch.zeros(HDR_INTS, dtype=torch.int32, device=self.slots.device)
-        stop[3] = self.pending_flags
-        with torch.cuda.stream(self.b.stream):
+        stop = self.io.stop_header(self.pending_flags)
+        with self.io.ordered():
             w1 = dist.isend(stop, 1)
-            w2 = dist.isend(self.b.hid, 1)
+            w2 = dist.isend(self.io.hid, 1)
             w1.wait()
             w2.wait()
-        self.b.stream.synchronize()
+        self.io.drain()

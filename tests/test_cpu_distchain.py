@@ -1,0 +1,115 @@
+"""The multi-process pipeline protocol (potpori_b200/distchain.py) on CPU: gloo ranks, host
+stand-ins for the shards (HostStageIO), no GPU.
+
+Checks what the chain of src/node.rs:242-342,466-535 must keep when its stages are separate
+processes: every chunk's header and hidden rows go rank r -> r+1 in order, the last rank's
+result comes straight back to rank 0, several chunks are in flight at once (the depth of
+src/specpipe.rs:83-127), prefill feeds the prompt in 8-row chunks and single rows, the timed
+window marks ride on the headers to every stage, a non-finite result surfaces at the head as
+NonFiniteLogits, and the stop header ends every rank.
+"""
+import multiprocessing as mp
+import os
+import socket
+
+import pytest
+import torch
+
+HIDDEN = 16
+WIDTH = 8
+
+
+class FakeStage:
+    """Stage r adds 1 to column 0 of every row; the first writes the tokens there first; the
+    last returns column 0 as the picks. So a chunk's picks are its tokens + world; token 999
+    makes the last stage report a non-finite row."""
+
+    def __init__(self, first: bool, last: bool):
+        self.first, self.last = first, last
+
+    def step(self, hdr, hid, res):
+        m = int(hdr[1])
+        h = hid.view(-1, HIDDEN)
+        toks = hdr[4:4 + m].float()
+        if self.first:
+            h[:m, 0] = toks
+        h[:m, 0] += 1.0
+        if self.last:
+            res.zero_()
+            res[:m] = h[:m, 0].to(torch.int32)
+            if bool((res[:m] > 900).any()):
+                res[48] = 1
+
+
+def _worker(rank: int, world: int, port: int, q) -> None:
+    import torch.distributed as dist
+    from potpori_b200.distchain import (FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain,
+                                        HostStageIO, run_stage)
+    from potpori_b200.target import NonFiniteLogits
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
+                         first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH)
+        if rank != 0:
+            q.put((rank, "ms", run_stage(None, rank, world, WIDTH, io=io)))
+            return
+        chain = DistChain(None, world, WIDTH, io=io)
+        prompt = list(range(10, 29))  # 19 tokens: two 8-row chunks, then three single rows
+        assert chain.prefill(prompt) == prompt[-1] + world
+        # three chunks in flight, then read in order
+        chunks = [(19, 40, [41, 42, 43]), (23, 50, []), (24, 60, [61, 62, 63, 64, 65, 66, 67])]
+        chain.mark(FLAG_WINDOW_START)
+        for pos, cur, ds in chunks:
+            chain.submit(pos, cur, ds)
+        chain.mark(FLAG_WINDOW_END)
+        chain.submit(32, 70, [71])
+        for _, cur, ds in chunks + [(32, 70, [71])]:
+            assert chain.poll() == [t + world for t in [cur] + ds]
+        assert chain.verify(34, 80, [81, 82]) == [80 + world, 81 + world, 82 + world]
+        try:
+            chain.verify(37, 990, [])
+            raise AssertionError("a non-finite result was not reported")
+        except NonFiniteLogits:
+            pass
+        assert chain.submitted == 2 + 3 + 3 + 1 + 1 + 1
+        chain.stop()
+        q.put((0, "ok", True))
+    except BaseException as e:  # reported to the test process
+        q.put((rank, "error", repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_protocol_over_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    got = {}
+    while not q.empty():
+        r, k, v = q.get()
+        got[(r, k)] = v
+    errors = {k: v for k, v in got.items() if k[1] == "error"}
+    assert not errors, errors
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert got[(0, "ok")] is True
+    # every stage saw both window marks
+    for r in range(1, world):
+        assert got[(r, "ms")] > 0.0
