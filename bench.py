@@ -36,6 +36,7 @@ if ROOT not in sys.path:
 
 METRIC = "Qwen3-4B committed tok/s at 1/2/4/8 B200; verify-pass HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
+NCCL_SMS = 4  # SMs left free for NCCL's transfer kernels on every rank of a multi-GPU run
 
 
 def parse_args():
@@ -49,6 +50,8 @@ def parse_args():
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
+    ap.add_argument("--nccl-sms", type=int, default=None,
+                    help="SMs left to NCCL's transfer kernels on every rank when N > 1")
     return ap.parse_args()
 
 
@@ -213,30 +216,42 @@ def run_ours(args):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        # The stage-to-stage messages are 144 B headers and 80 KiB hidden rows: two NCCL
+        # channels carry them, and fewer channels hold fewer SMs (see NCCL_SMS).
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     stage = Shard.random(wl.target, ranges[rank], wl.max_seq, wl.chunk, wl.target_seed,
                          device=local)
+    # With N > 1 the NCCL kernels that serve the stage-to-stage transfers hold a few SMs;
+    # the shards' kernels use the rest (their CTAs must all be resident at once).
+    n_sms = torch.cuda.get_device_properties(local).multi_processor_count
+    reserve = (NCCL_SMS if args.nccl_sms is None else args.nccl_sms) if world > 1 else 0
+    sm_budget = n_sms - reserve if reserve else 0
+    stage.set_sm_limit(sm_budget)
     width = wl.chunk
     if world > 1:
         dist.barrier()
     if rank != 0:
-        from potpori_b200.distchain import run_stage
-        ms = run_stage(stage, rank, world, width)
+        from potpori_b200.distchain import Links, run_stage
+        ms = run_stage(stage, rank, world, width, Links(world))
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
+        torch.cuda.synchronize()
+        stage.close()  # before the process group and the CUDA runtime are torn down
         dist.destroy_process_group()
         return
 
     dmodel = QwenTarget(stage) if wl.draft_is_target and world == 1 else \
         QwenTarget.random(wl.draft, wl.max_seq, wl.chunk, wl.draft_seed, device=local)
+    dmodel.shard.set_sm_limit(sm_budget)
     draft = IncrementalDraft(dmodel, wl.chunk)
     if world == 1:
         chain = LocalChain([stage])
     else:
-        from potpori_b200.distchain import FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain
-        chain = DistChain(stage, world, width)
+        from potpori_b200.distchain import FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain, Links
+        chain = DistChain(stage, world, width, Links(world))
     prompt = wl.prompt()
     drv = PipelinedDriver(draft, chain, prompt, SpecConfig(wl.gamma, wl.max_new), wl.depth)
     stream = torch.cuda.ExternalStream(stage.stream())
@@ -347,7 +362,7 @@ def run_ours(args):
         "config": {
             "workload": wl.name, "target": f"Qwen3-4B (36 layers, random BF16 weights seed {wl.target_seed})",
             "draft": f"Qwen3-0.6B (seed {wl.draft_seed})", "gamma": wl.gamma, "depth": wl.depth,
-            "max_seq": wl.max_seq, "prompt_len": wl.prompt_len, "layers_per_gpu": ranges,
+            "max_seq": wl.max_seq, "prompt_len": wl.prompt_len, "layers_per_gpu": ranges, "sm_budget": stage.sm_limit(),
             "global_batch": 1, "weights": "bf16 storage, f32 arithmetic",
             "l2": "no flush: 8.3 GB of weights streamed per verify pass, far above the 126 MB L2",
         },
@@ -364,6 +379,13 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+    # Release the shards explicitly, before the process group and the CUDA runtime are torn
+    # down (destructors that run at interpreter exit may find them gone).
+    torch.cuda.synchronize()
+    del drv, draft, chain
+    dmodel.shard.close()
+    stage.close()
+    if world > 1:
         dist.destroy_process_group()
 
 

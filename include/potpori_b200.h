@@ -169,6 +169,14 @@ uint32_t pp_shard_last_launches(const pp_shard* shard);
  * dependent launch between kernels (default on). */
 pp_status pp_shard_set_graphs(pp_shard* shard, int32_t enabled);
 pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
+/* Most CTAs (one per SM) any kernel of this shard launches; 0 = every SM, the default. The
+ * split-K GEMVs and the split attention assume all their CTAs are resident at once, so SMs
+ * held by other work on the device (the kernels that serve NCCL transfers between pipeline
+ * stages) must be left out of the budget, or the CTAs that do not fit run as a second wave.
+ * No counterpart in the reference. Must be at least n_kv_heads. Results stay within the
+ * parity tolerances: the split partition (the summation order) depends on the budget. */
+pp_status pp_shard_set_sm_limit(pp_shard* shard, uint32_t ctas);
+uint32_t pp_shard_sm_limit(const pp_shard* shard);
 
 /* Allocation-free RMSNorm + skinny GEMV (no counterpart in the reference; an addition for
  * callers that cannot allocate device memory: code running inside a host framework or memory

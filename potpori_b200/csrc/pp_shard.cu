@@ -1383,6 +1383,21 @@ pp_status pp_shard_set_graphs(pp_shard* s, int32_t enabled) {
   s->use_graphs = enabled != 0;
   return PP_OK;
 }
+pp_status pp_shard_set_sm_limit(pp_shard* s, uint32_t ctas) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  const int n = ctas == 0 || (int)ctas > s->num_sms ? s->num_sms : (int)ctas;
+  if (n < s->nkv) return fail(s, PP_E_INVALID, "an SM limit below n_kv_heads (%d)", s->nkv);
+  s->max_grid = n;
+  s->splits = n / s->nkv > 256 ? 256 : n / s->nkv;  // buffers were sized for the whole GPU
+  for (auto& e : s->exec)
+    if (e) {
+      cudaGraphExecDestroy(e);
+      e = nullptr;
+    }
+  return PP_OK;
+}
+uint32_t pp_shard_sm_limit(const pp_shard* s) { return s ? (uint32_t)s->max_grid : 0u; }
+
 pp_status pp_shard_set_pdl(pp_shard* s, int32_t enabled) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
   s->use_pdl = enabled != 0;

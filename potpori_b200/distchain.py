@@ -40,6 +40,19 @@ FLAG_WINDOW_START = 2
 FLAG_WINDOW_END = 4
 
 
+class Links:
+    """One process group per link, so transfers on different links never queue behind each
+    other: NCCL runs the ops of one communicator in order, so with a single group the head's
+    receive of chunk k's result (posted first, completing only after the whole traversal)
+    would hold back the send of chunk k+1, and the chunks could not overlap in the pipeline.
+    fwd[r]: rank r -> r + 1; ret: the last rank -> rank 0. Every rank must build it, in the
+    same order (dist.new_group is collective)."""
+
+    def __init__(self, world: int):
+        self.fwd = [dist.new_group([r, r + 1]) for r in range(world - 1)]
+        self.ret = dist.new_group([0, world - 1])
+
+
 class _DevArray:
     def __init__(self, ptr: int, n: int, typestr: str):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
@@ -184,15 +197,15 @@ class HostStageIO:
         return self._chunk
 
 
-def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
+def run_stage(shard, rank: int, world: int, width: int, links: Links, io=None) -> float:
     """Serve as stage `rank` (1 <= rank < world) until the session ends. Returns the time (ms)
     between the timed-window marks, measured on this stage's stream (0 without both marks)."""
     io = io or CudaStageIO(shard, width)
     started = ended = False
     with io.ordered():
         while True:
-            w1 = dist.irecv(io.hdr, rank - 1)
-            w2 = dist.irecv(io.hid, rank - 1)
+            w1 = dist.irecv(io.hdr, rank - 1, group=links.fwd[rank - 1])
+            w2 = dist.irecv(io.hid, rank - 1, group=links.fwd[rank - 1])
             w1.wait()
             w2.wait()
             m, flags = io.read_header()
@@ -207,11 +220,11 @@ def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
             if io.last:
                 if m == 0:
                     break
-                w = dist.isend(io.res, 0)
+                w = dist.isend(io.res, 0, group=links.ret)
                 w.wait()
             else:
-                w1 = dist.isend(io.hdr, rank + 1)
-                w2 = dist.isend(io.hid, rank + 1)
+                w1 = dist.isend(io.hdr, rank + 1, group=links.fwd[rank])
+                w2 = dist.isend(io.hid, rank + 1, group=links.fwd[rank])
                 w1.wait()
                 w2.wait()
                 if m == 0:
@@ -223,10 +236,10 @@ def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
 class DistChain:
     """The head's view of the multi-process chain (PipelinedChain / TargetChain)."""
 
-    def __init__(self, stage0, world: int, width: int, io=None):
+    def __init__(self, stage0, world: int, width: int, links: Links, io=None):
         self.io = io or CudaStageIO(stage0, width)
         assert self.io.first and not self.io.last and world > 1
-        self.world, self.width = world, width
+        self.world, self.width, self.links = world, width, links
         self.slots = self.io.result_slots(RING)
         self.inflight: deque = deque()
         self.slot = 0
@@ -250,11 +263,11 @@ class DistChain:
             io.set_step(pos, m, tokens, list(drafts), self.pending_flags)
             self.pending_flags = 0
             io.step()
-            w1 = dist.isend(io.hdr, 1)
-            w2 = dist.isend(io.hid, 1)
+            w1 = dist.isend(io.hdr, 1, group=self.links.fwd[0])
+            w2 = dist.isend(io.hid, 1, group=self.links.fwd[0])
             w1.wait()
             w2.wait()
-            wr = dist.irecv(self.slots[self.slot], self.world - 1)
+            wr = dist.irecv(self.slots[self.slot], self.world - 1, group=self.links.ret)
         self.inflight.append((self.slot, m, wr))
         self.slot = (self.slot + 1) % RING
         self.submitted += 1
@@ -299,8 +312,8 @@ class DistChain:
                 wr.wait()
         stop = self.io.stop_header(self.pending_flags)
         with self.io.ordered():
-            w1 = dist.isend(stop, 1)
-            w2 = dist.isend(self.io.hid, 1)
+            w1 = dist.isend(stop, 1, group=self.links.fwd[0])
+            w2 = dist.isend(self.io.hid, 1, group=self.links.fwd[0])
             w1.wait()
             w2.wait()
         self.io.drain()

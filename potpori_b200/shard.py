@@ -192,6 +192,14 @@ class Shard:
     def set_pdl(self, enabled: bool) -> None:
         check(self._L.pp_shard_set_pdl(self._h, int(enabled)), self._h)
 
+    def set_sm_limit(self, ctas: int) -> None:
+        """Most CTAs (SMs) any kernel of this shard uses; 0 = all. Leave out SMs that other
+        work on the device holds (e.g. NCCL transfer kernels between pipeline stages)."""
+        check(self._L.pp_shard_set_sm_limit(self._h, int(ctas)), self._h, "set_sm_limit")
+
+    def sm_limit(self) -> int:
+        return int(self._L.pp_shard_sm_limit(self._h))
+
     def _verify_struct(self, want_logits: Optional[np.ndarray]):
         vo = self._vo
         vo.argmax = self._am.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))

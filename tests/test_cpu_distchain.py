@@ -44,18 +44,19 @@ class FakeStage:
 def _worker(rank: int, world: int, port: int, q) -> None:
     import torch.distributed as dist
     from potpori_b200.distchain import (FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain,
-                                        HostStageIO, run_stage)
+                                        HostStageIO, Links, run_stage)
     from potpori_b200.target import NonFiniteLogits
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        links = Links(world)
         io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
                          first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH)
         if rank != 0:
-            q.put((rank, "ms", run_stage(None, rank, world, WIDTH, io=io)))
+            q.put((rank, "ms", run_stage(None, rank, world, WIDTH, links, io=io)))
             return
-        chain = DistChain(None, world, WIDTH, io=io)
+        chain = DistChain(None, world, WIDTH, links, io=io)
         prompt = list(range(10, 29))  # 19 tokens: two 8-row chunks, then three single rows
         assert chain.prefill(prompt) == prompt[-1] + world
         # three chunks in flight, then read in order

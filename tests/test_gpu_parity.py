@@ -200,3 +200,30 @@ def test_nonfinite_logits_are_flagged(gpu):
     res = full.verify_tokens(0, [1, 2])
     assert res.nonfinite_rows == 0b11
     assert res.argmax == [-1, -1]
+
+
+@pytest.mark.parametrize("ctas", [8, 144])
+def test_qwen3_4b_layer_under_an_sm_budget(gpu, ctas):
+    """A shard whose kernels may use only `ctas` SMs (pp_shard_set_sm_limit: the multi-GPU
+    ranks leave SMs to NCCL's transfer kernels) still matches the oracle; only the split-K and
+    key-split partition, i.e. the summation order, changes."""
+    cfg, seed = QWEN3_4B, 4
+    lay = (5, 6)
+    dev = Shard.random(cfg, lay, 4096, 0, seed=seed)
+    dev.set_sm_limit(ctas)
+    assert dev.sm_limit() == ctas
+    ref = oracle.OracleShard(cfg, lay[0], lay[1], 4096, 0)
+    ref.init_random(seed)
+    dev.fill_kv(7, 2048)
+    ref.fill_kv(7, 2048)
+    rng = np.random.default_rng(ctas)
+    pos = 2048
+    for m in (8, 1):
+        hidden = rng.standard_normal((m, cfg.hidden)).astype(np.float32)
+        got = dev.forward_hidden(pos, m, hidden)
+        want = ref.forward(pos, hidden=hidden)
+        assert rel_l2(got, want) <= 1e-3
+        pos += m
+    with pytest.raises(PPError) as e:
+        dev.set_sm_limit(cfg.n_kv_heads - 1)
+    assert e.value.status == PP_E_INVALID
