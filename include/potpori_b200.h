@@ -46,7 +46,8 @@ typedef struct pp_shard_desc {
   pp_config cfg;
   uint32_t layer_begin, layer_end;
   uint32_t capacity; /* KV positions (max_seq) */
-  uint32_t chunk;    /* verify chunk (gamma + 1); 0 = any size up to 8 */
+  uint32_t chunk;    /* verify chunk (gamma + 1), at most 16; 0 = any size up to 16. Chunks
+                        of 9..16 rows need n_heads / n_kv_heads <= 4. */
   int32_t cuda_device;
 } pp_shard_desc;
 
@@ -101,7 +102,8 @@ pp_status pp_shard_forward_hidden(pp_shard* shard, uint32_t pos, uint32_t m, con
  * src/node.rs:466-496 with device buffers). The step reads its input from the shard's own
  * input buffer (pp_shard_buffers) and its step header from the device header buffer, both
  * of which a peer copy or NCCL receive may fill; no host synchronisation. stream: a
- * cudaStream_t (NULL = the shard's stream). max_rows selects the compiled chunk width. */
+ * cudaStream_t (NULL = the shard's stream). max_rows selects the compiled chunk width
+ * (1, 2, 4, 8 or 16 rows). */
 pp_status pp_shard_step_device(pp_shard* shard, uint32_t max_rows, void* stream);
 /* Host-side enqueue of the step header (pos, m, tokens, drafts) for pp_shard_step_device.
  * flags: bit 0 = also write the full logits (last shard); the other bits travel with the

@@ -100,9 +100,9 @@ struct LayerDev {
   bool norm_set[N_COUNT] = {};
 };
 
-constexpr int kVariants = 4;  // chunk widths 1, 2, 4, 8
+constexpr int kVariants = 5;  // chunk widths 1, 2, 4, 8, 16
 constexpr int kRing = 64;     // in-flight headers / results per shard
-inline int variant_of(int m) { return m <= 1 ? 0 : m <= 2 ? 1 : m <= 4 ? 2 : 3; }
+inline int variant_of(int m) { return m <= 1 ? 0 : m <= 2 ? 1 : m <= 4 ? 2 : m <= 8 ? 3 : 4; }
 
 }  // namespace
 
@@ -499,7 +499,7 @@ pp_status set_attrs_mt(pp_shard* s) {
 pp_status set_attrs(pp_shard* s) {
   pp_status r;
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
-      (r = set_attrs_mt<8>(s)))
+      (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)))
     return r;
   return PP_OK;
 }
@@ -510,7 +510,8 @@ pp_status enqueue_variant(pp_shard* s, int vi, cudaStream_t st) {
     case 0: r = enqueue_step<1>(s, st); break;
     case 1: r = enqueue_step<2>(s, st); break;
     case 2: r = enqueue_step<4>(s, st); break;
-    default: r = enqueue_step<8>(s, st); break;
+    case 3: r = enqueue_step<8>(s, st); break;
+    default: r = enqueue_step<16>(s, st); break;
   }
   s->variant_launches[vi] = s->launches;
   return r;
@@ -582,7 +583,9 @@ pp_status check_step(pp_shard* s, uint32_t pos, uint32_t m) {
     return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
   if (s->d.chunk != 0 && m != 1 && m != s->d.chunk)
     return fail(s, PP_E_INVALID, "unsupported verify chunk size");
-  if (m > 8) return fail(s, PP_E_UNSUPPORTED, "chunks above 8 rows are not built");
+  if (m > (uint32_t)kMaxRows) return fail(s, PP_E_UNSUPPORTED, "chunks above 16 rows are not built");
+  if (m > 8 && s->G > 4)
+    return fail(s, PP_E_UNSUPPORTED, "16-row chunks need at most 4 query heads per KV head");
   return PP_OK;
 }
 
@@ -806,7 +809,7 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   if (r0) return r0;
   s->splits = s->num_sms / s->nkv > 0 ? s->num_sms / s->nkv : 1;
   if (s->splits > 256) s->splits = 256;  // the combine kernel holds up to 256 splits
-  s->nq_max = s->G * 8;
+  s->nq_max = s->G * kMaxRows;
   pp_status r;
   s->L.resize(s->nl);
   for (int l = 0; l < s->nl; ++l) {
@@ -851,14 +854,14 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   if ((r = dalloc(s, &s->ss_ffn, (size_t)s->ss_tiles * kMaxRows * 4))) return r;
   if (s->last && (r = dalloc(s, &s->logits, (size_t)kMaxRows * s->V * 4))) return r;
   if ((r = dalloc(s, &s->apart, (size_t)s->nkv * s->splits * s->nq_max * (s->hd + 4) * 4))) return r;
-  if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * 8 * 4))) return r;
+  if ((r = dalloc(s, &s->gpart, (size_t)s->max_grid * 2 * kTileRows * kMaxRows * 4))) return r;
   {
     int64_t max_tiles = s->Vp / kTileRows;
     const int64_t cand[4] = {s->qkv_rows, s->o_rows, s->gu_rows, s->d_rows};
     for (int64_t v : cand) max_tiles = v / kTileRows > max_tiles ? v / kTileRows : max_tiles;
     if ((r = dalloc(s, &s->tile_cnt, (size_t)max_tiles * 4))) return r;
   }
-  if ((r = dalloc(s, &s->recs, (size_t)s->max_grid * 8 * sizeof(ArgRec)))) return r;
+  if ((r = dalloc(s, &s->recs, (size_t)s->max_grid * kMaxRows * sizeof(ArgRec)))) return r;
   if ((r = dalloc(s, &s->done, 64))) return r;
   if ((r = dalloc(s, &s->d_desc, sizeof(StepDesc)))) return r;
   if ((r = dalloc(s, &s->d_res, sizeof(StepResult)))) return r;
@@ -893,7 +896,10 @@ pp_status pp_shard_create(const pp_shard_desc* desc, pp_shard** out) {
     return fail(nullptr, PP_E_UNSUPPORTED, "unsupported geometry");
   if (c.n_heads / c.n_kv_heads > 8)
     return fail(nullptr, PP_E_UNSUPPORTED, "more than 8 query heads per KV head");
-  if (desc->chunk > 8) return fail(nullptr, PP_E_UNSUPPORTED, "chunks above 8 rows are not built");
+  if (desc->chunk > (uint32_t)kMaxRows)
+    return fail(nullptr, PP_E_UNSUPPORTED, "chunks above 16 rows are not built");
+  if (desc->chunk > 8 && c.n_heads / c.n_kv_heads > 4)
+    return fail(nullptr, PP_E_UNSUPPORTED, "16-row chunks need at most 4 query heads per KV head");
   if (!encode_fn()) return fail(nullptr, PP_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
   s = new pp_shard();
   int prev = 0;
@@ -1205,7 +1211,9 @@ pp_status pp_shard_set_step(pp_shard* s, uint32_t pos, uint32_t m, const int32_t
 
 pp_status pp_shard_step_device(pp_shard* s, uint32_t max_rows, void* stream) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
-  if (max_rows == 0 || max_rows > 8) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..8");
+  if (max_rows == 0 || max_rows > (uint32_t)kMaxRows) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..16");
+  if (max_rows > 8 && s->G > 4)
+    return fail(s, PP_E_UNSUPPORTED, "16-row chunks need at most 4 query heads per KV head");
   CK(cudaSetDevice(s->dev));
   cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
   return run_step(s, variant_of((int)max_rows), st);
@@ -1259,7 +1267,9 @@ pp_status pp_shard_fill_kv(pp_shard* s, uint64_t seed, uint32_t rows) {
 pp_status pp_shard_profile_kernels(pp_shard* s, uint32_t max_rows, uint32_t iters, float* ms,
                                    int32_t* kinds, uint32_t cap, uint32_t* count) {
   if (!s || !ms || !kinds || !count || iters == 0) return fail(s, PP_E_INVALID, "null argument");
-  if (max_rows == 0 || max_rows > 8) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..8");
+  if (max_rows == 0 || max_rows > (uint32_t)kMaxRows) return fail(s, PP_E_UNSUPPORTED, "max_rows must be 1..16");
+  if (max_rows > 8 && s->G > 4)
+    return fail(s, PP_E_UNSUPPORTED, "16-row chunks need at most 4 query heads per KV head");
   if (pp_shard_missing(s, nullptr, 0)) return fail(s, PP_E_MISSING, "parameters missing");
   CK(cudaSetDevice(s->dev));
   // Capture the step with an event record after every kernel, then replay the graph: the

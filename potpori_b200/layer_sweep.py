@@ -2,13 +2,13 @@
 
 One Qwen3-4B decoder layer (random BF16 weights, seed 4) as a middle shard: F32 hidden rows
 ~N(0,1) in, hidden rows out. For every KV length in {128, 512, 2048, 4096} (the cache filled
-with seeded random K/V) and chunk width M in {1, 4, 8} it runs a few verify steps, each
+with seeded random K/V) and chunk width M in {1, 4, 8, 16} it runs a few verify steps, each
 appending M positions and rolling back a random 0..M-1 rejected suffix, then times every
 kernel of the step (graph replay, event per kernel) and reports latency and achieved HBM
 GB/s against the algorithmic bytes of that kernel. The tail (final norm + vocab projection
 + argmax over 151936 rows at hidden 2560) is timed the same way on a last-layer shard.
 
-    python -m potpori_b200.layer_sweep [--kv 128 512 2048 4096] [--m 1 4 8] [--json]
+    python -m potpori_b200.layer_sweep [--kv 128 512 2048 4096] [--m 1 4 8 16] [--json]
 """
 from __future__ import annotations
 
@@ -80,7 +80,7 @@ def sweep(kv_lens, ms, steps=3, iters=5, device=0, seed=4, tail=True):
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--kv", type=int, nargs="+", default=[128, 512, 2048, 4096])
-    ap.add_argument("--m", type=int, nargs="+", default=[1, 4, 8])
+    ap.add_argument("--m", type=int, nargs="+", default=[1, 4, 8, 16])
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--no-tail", action="store_true")

@@ -146,7 +146,7 @@ def test_qwen3_0_6b_whole_model_verify(gpu):
         assert res.n_accepted == n and res.correction == picks[n]
 
 
-@pytest.mark.parametrize("m", [1, 4, 8])
+@pytest.mark.parametrize("m", [1, 4, 8, 16])
 @pytest.mark.parametrize("kv_len", [128, 2048])
 def test_qwen3_4b_layer_with_rollback(gpu, m, kv_len):
     """One Qwen3-4B decoder layer (seed 4) over a random warm cache: each step appends m
