@@ -91,6 +91,14 @@ int32_t pp_shard_missing(const pp_shard* shard, char* buf, size_t len);
  * compare are tokens[1..m-1]. */
 pp_status pp_shard_forward_tokens(pp_shard* shard, uint32_t pos, const int32_t* tokens,
                                   uint32_t m, float* out_hidden, pp_verify_out* verify);
+/* Greedy decode of n single tokens on a whole-model shard (first and last), the draft's
+ * gamma loop of src/qwen/draft.rs:14-93: step i feeds token t_i at position pos + i, with
+ * t_0 = token and t_{i+1} = the greedy pick of step i; out[i] = pick i (n <= 64). The picks
+ * are fed to the next step on the device, so the host waits once for the n steps instead of
+ * once per token. PP_E_NONFINITE when a step produced non-finite logits (the picks after it
+ * are then undefined). */
+pp_status pp_shard_decode_greedy(pp_shard* shard, uint32_t pos, int32_t token, uint32_t n,
+                                 int32_t* out);
 /* ShardEngine::forward_hidden (src/node.rs:73, src/qwen/shard.rs:127-129): non-first shard.
  * hidden: [m][hidden] F32 (finite, src/qwen/model.rs:390-392). drafts: [n_drafts] tokens
  * for the tail's accept compare (may be NULL). */

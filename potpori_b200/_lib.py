@@ -30,7 +30,7 @@ EXPORTS = [
     "pp_shard_chunk_size", "pp_shard_range", "pp_shard_hidden_dim", "pp_shard_vocab_size",
     "pp_shard_model_layers", "pp_shard_device_bytes", "pp_shard_last_launches",
     "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
-    "pp_shard_set_sm_limit", "pp_shard_sm_limit",
+    "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
     "pp_norm_gemv_static", "pp_last_error", "pp_version",
 ]
 
@@ -121,6 +121,7 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_pdl": (I32, [P, I32]),
         "pp_shard_set_sm_limit": (I32, [P, U32]),
         "pp_shard_sm_limit": (U32, [P]),
+        "pp_shard_decode_greedy": (I32, [P, U32, I32, U32, pI32]),
         "pp_norm_gemv_static": (I32, [P, P, P, F, U32, U32, U32, P, P]),
         "pp_last_error": (SZ, [P, ctypes.c_char_p, SZ]),
         "pp_version": (ctypes.c_char_p, []),

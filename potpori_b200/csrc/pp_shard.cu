@@ -139,6 +139,8 @@ struct pp_shard {
   uint32_t* tile_cnt = nullptr;
   ArgRec* recs = nullptr;
   uint32_t* done = nullptr;
+  int32_t* d_decode = nullptr;  // [kDecodeMax + 1] greedy-decode picks and error bits
+  int32_t* h_decode = nullptr;  // pinned copy
   StepDesc* d_desc = nullptr;
   StepResult* d_res = nullptr;
   StepDesc* h_desc = nullptr;      // pinned ring of kRing headers
@@ -300,6 +302,21 @@ __global__ void step_begin_kernel(const StepDesc* desc, StepResult* res, int32_t
     if (first && !bad)
       for (int r = 0; r < d.m; ++r) bad |= d.tokens[r] < 0 || d.tokens[r] >= vocab;
     res->status = bad ? ST_BAD_STEP : 0;
+  }
+}
+
+// Greedy decode on the device (pp_shard_decode_greedy): after 1-row step i, record its pick
+// and, if another step follows, make it the next step's token at the next position. Errors
+// of the step (status bits, a non-finite row) accumulate in out[kDecodeMax].
+constexpr int kDecodeMax = 64;
+__global__ void decode_feed_kernel(StepDesc* desc, const StepResult* res, int32_t* out,
+                                   int32_t i, int32_t feed) {
+  const int32_t t = res->argmax[0];
+  out[i] = t;
+  out[kDecodeMax] |= res->status | (t < 0 ? ST_NONFINITE_OUT : 0);
+  if (feed) {
+    desc->pos += 1;
+    desc->tokens[0] = t < 0 ? 0 : t;  // keep later steps well-formed; the error is recorded
   }
 }
 
@@ -767,6 +784,7 @@ void pp_shard_destroy(pp_shard* s) {
   if (s->handoff_ev) cudaEventDestroy(s->handoff_ev);
   if (s->handoff_done_ev) cudaEventDestroy(s->handoff_done_ev);
   if (s->h_stage) cudaFreeHost(s->h_stage);
+  if (s->h_decode) cudaFreeHost(s->h_decode);
   if (s->stream) cudaStreamDestroy(s->stream);
   cudaSetDevice(prev);
   delete s;
@@ -863,6 +881,8 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   }
   if ((r = dalloc(s, &s->recs, (size_t)s->max_grid * kMaxRows * sizeof(ArgRec)))) return r;
   if ((r = dalloc(s, &s->done, 64))) return r;
+  if ((r = dalloc(s, &s->d_decode, (kDecodeMax + 1) * 4))) return r;
+  CK(cudaMallocHost(&s->h_decode, (kDecodeMax + 1) * 4));
   if ((r = dalloc(s, &s->d_desc, sizeof(StepDesc)))) return r;
   if ((r = dalloc(s, &s->d_res, sizeof(StepResult)))) return r;
   CK(cudaMallocHost(&s->h_desc, sizeof(StepDesc) * kRing));
@@ -1156,6 +1176,41 @@ pp_status pp_shard_forward_tokens(pp_shard* s, uint32_t pos, const int32_t* toke
   for (uint32_t i = 1; i < m; ++i) d.drafts[i - 1] = tokens[i];
   if ((r = upload_desc(s, slot, s->stream))) return r;
   return finish_host_step(s, m, out_hidden, verify);
+}
+
+pp_status pp_shard_decode_greedy(pp_shard* s, uint32_t pos, int32_t token, uint32_t n,
+                                 int32_t* out) {
+  if (!s || !out) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->first || !s->last) return fail(s, PP_E_INVALID, "greedy decode needs the whole model");
+  if (n == 0 || n > (uint32_t)kDecodeMax) return fail(s, PP_E_INVALID, "n must be 1..%d", kDecodeMax);
+  if ((uint64_t)pos + n > s->d.capacity) return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
+  if (token < 0 || token >= s->V) return fail(s, PP_E_INVALID, "invalid token input");
+  if (pp_shard_missing(s, nullptr, 0))
+    return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
+  CK(cudaSetDevice(s->dev));
+  int slot;
+  StepDesc& d = *next_desc(s, &slot);
+  d.pos = (int32_t)pos;
+  d.m = 1;
+  d.n_drafts = 0;
+  d.flags = 0;
+  d.tokens[0] = token;
+  pp_status r;
+  if ((r = upload_desc(s, slot, s->stream))) return r;
+  CK(cudaMemsetAsync(s->d_decode + kDecodeMax, 0, 4, s->stream));
+  for (uint32_t i = 0; i < n; ++i) {
+    if ((r = run_step(s, 0, s->stream))) return r;
+    decode_feed_kernel<<<1, 1, 0, s->stream>>>(s->d_desc, s->d_res, s->d_decode, (int32_t)i,
+                                                i + 1 < n ? 1 : 0);
+    CK(cudaGetLastError());
+  }
+  CK(cudaMemcpyAsync(s->h_decode, s->d_decode, (kDecodeMax + 1) * 4, cudaMemcpyDeviceToHost,
+                     s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  for (uint32_t i = 0; i < n; ++i) out[i] = s->h_decode[i];
+  StepResult st = {};
+  st.status = s->h_decode[kDecodeMax];
+  return status_of(s, st);
 }
 
 pp_status pp_shard_forward_hidden(pp_shard* s, uint32_t pos, uint32_t m, const float* hidden,

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass, field
-from typing import Optional, Sequence
+from typing import List, Optional, Sequence
 
 import numpy as np
 
@@ -191,6 +191,14 @@ class Shard:
 
     def set_pdl(self, enabled: bool) -> None:
         check(self._L.pp_shard_set_pdl(self._h, int(enabled)), self._h)
+
+    def decode_greedy(self, pos: int, token: int, n: int) -> List[int]:
+        """n single-token greedy steps fed on the device (whole-model shard): the picks."""
+        out = np.zeros(n, np.int32)
+        check(self._L.pp_shard_decode_greedy(
+            self._h, pos, int(token), n, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))),
+            self._h, f"decode_greedy(pos={pos}, n={n})")
+        return out.tolist()
 
     def set_sm_limit(self, ctas: int) -> None:
         """Most CTAs (SMs) any kernel of this shard uses; 0 = all. Leave out SMs that other

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 from typing import List
 
+from ._lib import PP_E_NONFINITE, PPError
 from .config import QwenConfig, is_eos
 from .shard import Shard
 
@@ -58,6 +59,16 @@ class QwenTarget:
     def verify(self, pos: int, cur: int, drafts: List[int]) -> List[int]:
         return self._pick(pos, [cur] + list(drafts))
 
+    def decode(self, pos: int, cur: int, n: int) -> List[int]:
+        """n greedy single-token steps from `cur` at `pos`, each fed the previous pick (on the
+        device); the n picks."""
+        try:
+            return self.shard.decode_greedy(pos, cur, n)
+        except PPError as e:
+            if e.status == PP_E_NONFINITE:
+                raise NonFiniteLogits("non-finite or empty logits") from e
+            raise
+
     def is_eos(self, token: int) -> bool:
         return is_eos(token)
 
@@ -94,9 +105,10 @@ class IncrementalDraft:
         del self.fed[start:]
         self.fed.extend(context[start:n])
         out = [cur]
-        for pos in range(n, n + gamma - 1):
-            self.fed.append(cur)
-            cur = self.model.verify(pos, cur, [])[0]
-            self.steps += 1
-            out.append(cur)
+        if gamma > 1:
+            # gamma - 1 greedy single-token steps, each pick fed to the next on the device
+            picks = self.model.decode(n, cur, gamma - 1)
+            self.fed.extend([cur] + picks[:-1])
+            self.steps += gamma - 1
+            out.extend(picks)
         return out

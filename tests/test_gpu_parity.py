@@ -227,3 +227,37 @@ def test_qwen3_4b_layer_under_an_sm_budget(gpu, ctas):
     with pytest.raises(PPError) as e:
         dev.set_sm_limit(cfg.n_kv_heads - 1)
     assert e.value.status == PP_E_INVALID
+
+
+def test_greedy_decode_on_device_matches_the_host_loop(gpu):
+    """pp_shard_decode_greedy (the draft's gamma loop, src/qwen/draft.rs:14-93, with each pick
+    fed to the next step on the device) gives the same picks as one host round trip per
+    token, and the oracle's greedy continuation where its top-2 gaps are clear."""
+    cfg, seed, cap = QWEN3_0_6B, 0, 128
+    a = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    b = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab_size, 16).tolist()
+    for s in (a, b):
+        s.verify_tokens(0, prompt[:8])
+        s.verify_tokens(8, prompt[8:])
+    ref.forward(0, tokens=prompt[:8])
+    ref.forward(8, tokens=prompt[8:])
+    got = a.decode_greedy(16, prompt[-1], 6)
+    host, cur = [], prompt[-1]
+    for i in range(6):
+        cur = b.verify_tokens(16 + i, [cur]).argmax[0]
+        host.append(cur)
+    assert got == host
+    cur = prompt[-1]
+    for i in range(6):
+        want = ref.forward(16 + i, tokens=[cur])[0]
+        t1, t2 = oracle.top2(want)
+        if t1 - t2 < TIE_GAP:
+            break
+        assert got[i] == oracle.argmax(want)
+        cur = got[i]
+    part = Shard.random(cfg, (0, 2), cap, 8, seed=seed)
+    with pytest.raises(PPError) as e:
+        part.decode_greedy(0, 1, 2)
+    assert e.value.status == PP_E_INVALID
