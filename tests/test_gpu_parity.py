@@ -261,3 +261,47 @@ def test_greedy_decode_on_device_matches_the_host_loop(gpu):
     with pytest.raises(PPError) as e:
         part.decode_greedy(0, 1, 2)
     assert e.value.status == PP_E_INVALID
+
+
+def test_speculative_stream_equals_oracle_greedy(gpu):
+    """Config 0 (Qwen3-0.6B seed 0, 41-id prompt, gamma 7, the draft a second copy of the same
+    weights, so drafts are accepted): the committed stream of the one-chunk driver
+    (src/specdecode.rs) and of the depth-4 pipelined driver (src/specpipe.rs) over the device
+    shards equals the oracle's plain greedy continuation (speculative greedy decoding is
+    lossless), up to the first position where the oracle's top-2 gap is below 1e-3."""
+    from potpori_b200.chain import LocalChain
+    from potpori_b200.specdecode import SpecConfig, run_spec_decode
+    from potpori_b200.specpipe import PipelinedDriver
+    from potpori_b200.target import IncrementalDraft, QwenTarget
+
+    cfg, seed, cap, new = QWEN3_0_6B, 0, 128, 24
+    prompt = np.random.default_rng(41).integers(0, cfg.vocab_size, 41).tolist()
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    pos, last = 0, None
+    while pos < len(prompt):
+        take = 8 if len(prompt) - pos >= 8 else 1
+        last = ref.forward(pos, tokens=prompt[pos:pos + take])[-1]
+        pos += take
+    want, gaps = [], []
+    for i in range(new):
+        t1, t2 = oracle.top2(last)
+        gaps.append(t1 - t2)
+        want.append(oracle.argmax(last))
+        last = ref.forward(pos, tokens=[want[-1]])[0]
+        pos += 1
+    clear = next((i for i, g in enumerate(gaps) if g < TIE_GAP), new)
+
+    def model():
+        return QwenTarget(Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed))
+
+    scfg = SpecConfig(7, new)
+    out, stats = run_spec_decode(IncrementalDraft(model(), 8), model(), prompt, scfg)
+    assert out[:clear] == want[:clear]
+    assert stats.toks_per_traversal() > 4  # the same weights: drafts are accepted
+
+    tgt = model()
+    drv = PipelinedDriver(IncrementalDraft(model(), 8), LocalChain([tgt.shard]), prompt, scfg, 4)
+    drv.start()
+    while drv.step():
+        pass
+    assert drv.out[:clear] == want[:clear]
