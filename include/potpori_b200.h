@@ -162,7 +162,8 @@ typedef enum pp_kernel_kind {
   PP_K_O = 5,            /* O projection + residual */
   PP_K_GATE_UP = 6,      /* post-attention norm + gate/up + SwiGLU */
   PP_K_DOWN = 7,         /* down projection + residual */
-  PP_K_HEAD = 8          /* final norm + vocab projection + argmax/top-2/accept */
+  PP_K_HEAD = 8,         /* final norm + vocab projection + argmax/top-2/accept */
+  PP_K_DECODE = 9        /* every layer of a 1-row step in one persistent kernel */
 } pp_kernel_kind;
 
 /* Time every kernel of one step: the step is captured into a graph with an event after each
@@ -187,6 +188,18 @@ pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
  * parity tolerances: the split partition (the summation order) depends on the budget. */
 pp_status pp_shard_set_sm_limit(pp_shard* shard, uint32_t ctas);
 uint32_t pp_shard_sm_limit(const pp_shard* shard);
+
+/* Run every 1-row step of a shard that holds all layers (a draft model's greedy decode, the
+ * single-token verify steps) as one persistent cooperative kernel over the shard's SM budget
+ * followed by the vocabulary head, instead of six kernels per layer (enabled = 1; 0 returns
+ * to the per-layer kernels). The kernel streams a row-major copy of the layer weights, made
+ * on first use after every weight upload and held until the shard is destroyed (0.9 GB for
+ * Qwen3-0.6B). Same step semantics as the per-layer path (src/qwen/model.rs:366-412 for one
+ * token); the F32 summation order differs, within the parity tolerances. PP_E_UNSUPPORTED for
+ * a shard without every layer or outside the kernel's sizes (hidden <= 8192, q_dim and
+ * intermediate <= 16384, all multiples of 8). No counterpart in the reference. */
+pp_status pp_shard_set_decode_kernel(pp_shard* shard, int32_t enabled);
+int32_t pp_shard_decode_kernel(const pp_shard* shard);
 
 /* Allocation-free RMSNorm + skinny GEMV (no counterpart in the reference; an addition for
  * callers that cannot allocate device memory: code running inside a host framework or memory

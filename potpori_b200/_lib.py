@@ -31,11 +31,12 @@ EXPORTS = [
     "pp_shard_model_layers", "pp_shard_device_bytes", "pp_shard_last_launches",
     "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
     "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
+    "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
     "pp_norm_gemv_static", "pp_last_error", "pp_version",
 ]
 
 KERNEL_KINDS = ["begin", "embed", "qkv", "attn", "attn_combine", "o_proj", "gate_up", "down",
-                "head"]
+                "head", "decode"]
 
 
 class PPError(RuntimeError):
@@ -121,6 +122,8 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_pdl": (I32, [P, I32]),
         "pp_shard_set_sm_limit": (I32, [P, U32]),
         "pp_shard_sm_limit": (U32, [P]),
+        "pp_shard_set_decode_kernel": (I32, [P, I32]),
+        "pp_shard_decode_kernel": (I32, [P]),
         "pp_shard_decode_greedy": (I32, [P, U32, I32, U32, pI32]),
         "pp_norm_gemv_static": (I32, [P, P, P, F, U32, U32, U32, P, P]),
         "pp_last_error": (SZ, [P, ctypes.c_char_p, SZ]),

@@ -28,6 +28,7 @@
 #include "../../include/potpori_b200.h"
 #include "pp_attn.cuh"
 #include "pp_common.cuh"
+#include "pp_decode.cuh"
 #include "pp_gemv.cuh"
 #include "pp_misc.cuh"
 
@@ -159,6 +160,15 @@ struct pp_shard {
   int gemv_max_stages = 8;
   bool use_graphs = true, use_pdl = true;
   cudaGraphExec_t exec[kVariants] = {};
+  // Single-token decode kernel (pp_shard_set_decode_kernel): row-major weight copies and the
+  // per-layer table on the device, its scratch, and whether the copies match the weights.
+  bool dec_on = false, dec_stale = true;
+  bool dec_graph = true;  // false once capturing the cooperative launch into a graph failed
+  std::vector<uint16_t*> dec_w;  // [nl][4]: QKV, O, gate/up pairs, down
+  DecodeLayer* dec_layers = nullptr;
+  float *dec_qkv = nullptr, *dec_attn = nullptr, *dec_act = nullptr, *dec_part = nullptr;
+  uint32_t* dec_sync = nullptr;
+  int dec_ns = 0, dec_vec = 0;
   uint32_t launches = 0;                 // kernels of the step being enqueued
   std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
   std::vector<int>* prof_kinds = nullptr;
@@ -322,6 +332,32 @@ __global__ void decode_feed_kernel(StepDesc* desc, const StepResult* res, int32_
 
 namespace {
 
+// Final norm + vocabulary projection + argmax/top-2/accept of a last shard (stream-K GEMV
+// over the tied embedding, operand split(x * final_norm) in xw_attn).
+template <int MT>
+pp_status launch_head(pp_shard* s, cudaStream_t st) {
+  GemvArgs h = {};
+  h.desc = s->d_desc;
+  h.res = s->d_res;
+  h.partials = s->gpart;
+  h.tile_cnt = s->tile_cnt;
+  h.recs = s->recs;
+  h.done_cnt = s->done;
+  h.eps = s->d.cfg.rms_norm_eps;
+  h.capacity = (int32_t)s->d.capacity;
+  h.n_out = s->V;
+  h.n_packed = (int32_t)s->Vp;
+  h.k = s->H;
+  h.kp = (int32_t)s->Hp;
+  h.tiles = (int32_t)(s->Vp / kTileRows);
+  h.kchunks = (int32_t)(s->Hp / kChunkK);
+  h.xsplit = s->xw_attn;
+  h.ss_in = s->ss_attn;
+  h.ss_tiles = s->ss_tiles;
+  h.logits = s->logits;
+  return launch_gemv<MT, X_STREAM, EPI_ARGMAX>(s, st, s->embed, h);
+}
+
 // The kernels of one step for chunk width MT, in stream order.
 template <int MT>
 pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
@@ -464,30 +500,116 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     }
     if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wd, dn))) return r;
   }
-  if (s->last) {
-    GemvArgs h = {};
-    h.desc = s->d_desc;
-    h.res = s->d_res;
-    h.partials = s->gpart;
-    h.tile_cnt = s->tile_cnt;
-    h.recs = s->recs;
-    h.done_cnt = s->done;
-    h.eps = s->d.cfg.rms_norm_eps;
-    h.capacity = (int32_t)s->d.capacity;
-    h.n_out = s->V;
-    h.n_packed = (int32_t)s->Vp;
-    h.k = s->H;
-    h.kp = (int32_t)s->Hp;
-    h.tiles = (int32_t)(s->Vp / kTileRows);
-    h.kchunks = (int32_t)(s->Hp / kChunkK);
-    h.xsplit = s->xw_attn;
-    h.ss_in = s->ss_attn;
-    h.ss_tiles = s->ss_tiles;
-    h.logits = s->logits;
-    if ((r = launch_gemv<MT, X_STREAM, EPI_ARGMAX>(s, st, s->embed, h)))
-      return r;
-  }
+  if (s->last && (r = launch_head<MT>(s, st))) return r;
   return PP_OK;
+}
+
+// ---- single-token decode kernel ---------------------------------------------------------------
+// Own residual rows of the smallest share of H a CTA of this grid gets, plus one.
+inline int decode_own_cap(const pp_shard* s, int grid) { return (s->H + grid - 1) / grid + 1; }
+
+pp_status decode_alloc(pp_shard* s) {
+  if (s->dec_layers) return PP_OK;
+  pp_status r;
+  const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
+  s->dec_w.assign((size_t)s->nl * 4, nullptr);
+  std::vector<DecodeLayer> tab(s->nl);
+  for (int l = 0; l < s->nl; ++l) {
+    uint16_t** w = &s->dec_w[(size_t)l * 4];
+    if ((r = dalloc(s, &w[0], (size_t)(Q + 2 * KV) * H * 2))) return r;
+    if ((r = dalloc(s, &w[1], (size_t)H * Q * 2))) return r;
+    if ((r = dalloc(s, &w[2], (size_t)2 * I * H * 2))) return r;
+    if ((r = dalloc(s, &w[3], (size_t)H * I * 2))) return r;
+    const LayerDev& Ld = s->L[l];
+    tab[l] = DecodeLayer{w[0], w[1], w[2], w[3], Ld.norm[N_ATTN], Ld.norm[N_QN], Ld.norm[N_KN],
+                         Ld.norm[N_FFN], Ld.kc, Ld.vc};
+  }
+  if ((r = dalloc(s, &s->dec_layers, tab.size() * sizeof(DecodeLayer)))) return r;
+  CK(cudaMemcpyAsync(s->dec_layers, tab.data(), tab.size() * sizeof(DecodeLayer),
+                     cudaMemcpyHostToDevice, s->stream));
+  const int max_splits = s->num_sms / s->nkv;
+  if ((r = dalloc(s, &s->dec_qkv, (size_t)(Q + 2 * KV) * 4))) return r;
+  if ((r = dalloc(s, &s->dec_attn, (size_t)Q * 4))) return r;
+  if ((r = dalloc(s, &s->dec_act, (size_t)I * 4))) return r;
+  if ((r = dalloc(s, &s->dec_part, (size_t)s->nh * max_splits * (s->hd + 4) * 4))) return r;
+  if ((r = dalloc(s, &s->dec_sync, (size_t)(2 + s->nkv) * 4))) return r;
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+// Row-major copies of the packed weights (after any weight upload).
+pp_status decode_rebuild(pp_shard* s) {
+  const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
+  for (int l = 0; l < s->nl; ++l) {
+    uint16_t** w = &s->dec_w[(size_t)l * 4];
+    const LayerDev& Ld = s->L[l];
+    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, s->Hp / kChunkK, 0);
+    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, s->Qp / kChunkK, 0);
+    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, s->Hp / kChunkK, 1);
+    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, s->Ip / kChunkK, 0);
+    CK(cudaGetLastError());
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  s->dec_stale = false;
+  return PP_OK;
+}
+
+// A 1-row step of a whole-model shard: header check, one cooperative launch of the decode
+// kernel over the shard's SM budget, the vocabulary head.
+pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
+  s->launches = 0;
+  pp_status r;
+  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
+                        (int32_t)s->d.capacity, (int32_t)1, (int32_t)s->V, (int32_t)s->first)))
+    return r;
+  CK(cudaMemsetAsync(s->dec_sync, 0, (size_t)(2 + s->nkv) * 4, st));
+  const int grid = s->max_grid;
+  DecodeArgs a = {};
+  a.layers = s->dec_layers;
+  a.nl = s->nl;
+  a.H = s->H;
+  a.Q = s->Q;
+  a.KV = s->KV;
+  a.I = s->I;
+  a.hd = s->hd;
+  a.nh = s->nh;
+  a.nkv = s->nkv;
+  a.G = s->G;
+  a.V = s->V;
+  a.capacity = (int32_t)s->d.capacity;
+  a.embed_kchunks = (int32_t)(s->Hp / kChunkK);
+  a.splits = grid / s->nkv;
+  a.ss_tiles = s->ss_tiles;
+  a.nslots = s->dec_ns;
+  a.vec_floats = s->dec_vec;
+  a.eps = s->d.cfg.rms_norm_eps;
+  a.inv_scale = 1.0f / sqrtf((float)s->hd);
+  a.embed = s->embed;
+  a.final_norm = s->final_norm;
+  a.rope = s->rope;
+  a.qkv = s->dec_qkv;
+  a.x = s->x;
+  a.attn = s->dec_attn;
+  a.act = s->dec_act;
+  a.part = s->dec_part;
+  a.sync = s->dec_sync;
+  a.xw_out = s->xw_attn;
+  a.ss_out = s->ss_attn;
+  a.desc = s->d_desc;
+  a.res = s->d_res;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = DecodeSmem(s->dec_ns, s->dec_vec, decode_own_cap(s, grid)).total();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: they meet at grid barriers
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, decode_step_kernel, a));
+  if ((r = after_launch(s, st, PP_K_DECODE))) return r;
+  return launch_head<1>(s, st);
 }
 
 template <typename K>
@@ -516,7 +638,8 @@ pp_status set_attrs_mt(pp_shard* s) {
 pp_status set_attrs(pp_shard* s) {
   pp_status r;
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
-      (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)))
+      (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
+      (r = set_max_smem(s, decode_step_kernel)))
     return r;
   return PP_OK;
 }
@@ -524,7 +647,7 @@ pp_status set_attrs(pp_shard* s) {
 pp_status enqueue_variant(pp_shard* s, int vi, cudaStream_t st) {
   pp_status r;
   switch (vi) {
-    case 0: r = enqueue_step<1>(s, st); break;
+    case 0: r = s->dec_on ? enqueue_decode_step(s, st) : enqueue_step<1>(s, st); break;
     case 1: r = enqueue_step<2>(s, st); break;
     case 2: r = enqueue_step<4>(s, st); break;
     case 3: r = enqueue_step<8>(s, st); break;
@@ -539,20 +662,33 @@ pp_status run_step(pp_shard* s, int vi, cudaStream_t st) {
   if (pp_shard_missing(s, nullptr, 0))
     return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
   s->last_variant = vi;
-  if (!s->use_graphs) return enqueue_variant(s, vi, st);
+  if (vi == 0 && s->dec_on && s->dec_stale) {
+    pp_status r = decode_rebuild(s);
+    if (r) return r;
+  }
+  const bool dec = vi == 0 && s->dec_on;
+  if (!s->use_graphs || (dec && !s->dec_graph)) return enqueue_variant(s, vi, st);
   if (!s->exec[vi]) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
     pp_status r = enqueue_variant(s, vi, s->stream);
     cudaError_t e = cudaStreamEndCapture(s->stream, &g);
-    if (r) {
-      if (g) cudaGraphDestroy(g);
-      return r;
+    const char* what = "graph capture";
+    if (e == cudaSuccess && !r) {
+      what = "graph instantiate";
+      e = cudaGraphInstantiate(&s->exec[vi], g, 0);
+      if (e != cudaSuccess) s->exec[vi] = nullptr;
     }
-    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "graph capture: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&s->exec[vi], g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    if (g) cudaGraphDestroy(g);
+    if (dec && (r || e != cudaSuccess)) {
+      // A runtime that cannot capture the cooperative launch: launch the step directly.
+      cudaGetLastError();
+      s->err.clear();
+      s->dec_graph = false;
+      return enqueue_variant(s, vi, st);
+    }
+    if (r) return r;
+    if (e != cudaSuccess) return fail(s, PP_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
   }
   CK(cudaGraphLaunch(s->exec[vi], st));
   s->last_variant = vi;
@@ -1054,6 +1190,7 @@ pp_status pp_shard_set_tensor(pp_shard* s, const char* name, pp_dtype dtype, con
     if (e != cudaSuccess) return fail(s, PP_E_CUDA, "upload %s: %s", name, cudaGetErrorString(e));
   }
   *t.flag = true;
+  s->dec_stale = true;
   return PP_OK;
 }
 
@@ -1082,6 +1219,7 @@ pp_status pp_shard_init_random(pp_shard* s, uint64_t seed, float stdv) {
     CK(cudaGetLastError());
     *t.flag = true;
   }
+  s->dec_stale = true;
   CK(cudaStreamSynchronize(s->stream));
   return PP_OK;
 }
@@ -1462,6 +1600,35 @@ pp_status pp_shard_set_sm_limit(pp_shard* s, uint32_t ctas) {
   return PP_OK;
 }
 uint32_t pp_shard_sm_limit(const pp_shard* s) { return s ? (uint32_t)s->max_grid : 0u; }
+
+pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  CK(cudaSetDevice(s->dev));
+  if (enabled && !s->dec_on) {
+    if (!(s->first && s->last))
+      return fail(s, PP_E_UNSUPPORTED, "the decode kernel runs shards that hold every layer");
+    if (s->H % 8 || s->Q % 8 || s->I % 8 || 4 * s->H > kDecSlot || 2 * s->Q > kDecSlot ||
+        2 * s->I > kDecSlot || kv_row_bytes(s->hd) > kDecKvHalf)
+      return fail(s, PP_E_UNSUPPORTED, "geometry outside the decode kernel's row and slot sizes");
+    const int vec = decode_vec_floats(s->H, s->Q, s->I, s->hd, s->G);
+    const size_t budget = dyn_smem_limit(s, decode_step_kernel);
+    const size_t fixed = DecodeSmem(0, vec, decode_own_cap(s, s->nkv)).total();
+    const int ns = budget > fixed ? (int)((budget - fixed) / kDecSlot) : 0;
+    if (ns < 2) return fail(s, PP_E_UNSUPPORTED, "the decode kernel's ring does not fit");
+    pp_status r = decode_alloc(s);
+    if (r) return r;
+    s->dec_ns = ns > 8 ? 8 : ns;
+    s->dec_vec = vec;
+    s->dec_stale = true;
+  }
+  s->dec_on = enabled != 0;
+  if (s->exec[0]) {
+    cudaGraphExecDestroy(s->exec[0]);
+    s->exec[0] = nullptr;
+  }
+  return PP_OK;
+}
+int32_t pp_shard_decode_kernel(const pp_shard* s) { return s && s->dec_on ? 1 : 0; }
 
 pp_status pp_shard_set_pdl(pp_shard* s, int32_t enabled) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");

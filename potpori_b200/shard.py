@@ -208,6 +208,15 @@ class Shard:
     def sm_limit(self) -> int:
         return int(self._L.pp_shard_sm_limit(self._h))
 
+    def set_decode_kernel(self, enabled: bool = True) -> None:
+        """Run 1-row steps of this whole-model shard as one persistent kernel (plus the vocab
+        head) instead of six kernels per layer; keeps a row-major copy of the layer weights."""
+        check(self._L.pp_shard_set_decode_kernel(self._h, 1 if enabled else 0), self._h,
+              "set_decode_kernel")
+
+    def decode_kernel(self) -> bool:
+        return bool(self._L.pp_shard_decode_kernel(self._h))
+
     def _verify_struct(self, want_logits: Optional[np.ndarray]):
         vo = self._vo
         vo.argmax = self._am.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))

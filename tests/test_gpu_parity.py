@@ -305,3 +305,62 @@ def test_speculative_stream_equals_oracle_greedy(gpu):
     while drv.step():
         pass
     assert drv.out[:clear] == want[:clear]
+
+
+def _step_logits_agree(got, want, worst, name):
+    """Logits of one 1-row step against the oracle: rel-L2 <= 1e-3 and the same greedy pick
+    unless the oracle's top-2 gap is below 1e-3."""
+    e = rel_l2(got, want)
+    assert e <= 1e-3, f"{name}: rel-L2 {e:.2e}"
+    t1, t2 = oracle.top2(want)
+    if t1 - t2 >= TIE_GAP:
+        assert int(np.argmax(got)) == oracle.argmax(want), name
+    return max(worst, e)
+
+
+def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
+    """The persistent 1-row decode kernel (pp_shard_set_decode_kernel) on Qwen3-0.6B (seed 0):
+    single-token steps at the first position (one key), after a chunked prefill, over a
+    seeded 2048-position cache (114 keys per attention split), after a rolled-back position
+    and under an SM budget give the oracle's logits (rel-L2 <= 1e-3, same pick unless the
+    top-2 gap is below 1e-3) and the per-layer kernels' (rel-L2 <= 2e-4); the device decode
+    loop gives the same picks as the per-layer kernels."""
+    cfg, seed, cap = QWEN3_0_6B, 0, 2304
+    dec = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    lay = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    dec.set_decode_kernel(True)
+    assert dec.decode_kernel() and not lay.decode_kernel()
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    rng = np.random.default_rng(7)
+    toks = rng.integers(0, cfg.vocab_size, 24).tolist()
+    worst, worst_lay = 0.0, 0.0
+
+    def step(pos, tok, name):
+        nonlocal worst, worst_lay
+        got = dec.forward_tokens(pos, [tok])[0]
+        other = lay.forward_tokens(pos, [tok])[0]
+        want = ref.forward(pos, tokens=[tok])[0]
+        worst = _step_logits_agree(got, want, worst, name)
+        worst_lay = max(worst_lay, rel_l2(got, other))
+        assert worst_lay <= 2e-4, f"{name}: {worst_lay:.2e} against the per-layer kernels"
+
+    step(0, toks[0], "pos 0")
+    for s in (dec, lay):
+        s.forward_tokens(1, toks[1:9])
+    ref.forward(1, tokens=toks[1:9])
+    for i in range(3):
+        step(9 + i, toks[9 + i], f"pos {9 + i}")
+    step(10, toks[20], "rolled back to pos 10")
+    step(11, toks[21], "pos 11 after the rollback")
+    for s in (dec, lay, ref):
+        s.fill_kv(5, 2048)
+    for i in range(3):
+        step(2048 + i, toks[12 + i], f"pos {2048 + i}")
+    dec.set_sm_limit(64)
+    step(2051, toks[15], "64-SM budget")
+    dec.set_sm_limit(0)
+    step(2052, toks[16], "all SMs again")
+    got = dec.decode_greedy(2053, toks[17], 6)
+    want = lay.decode_greedy(2053, toks[17], 6)
+    assert got == want
+    print(f"decode kernel: worst rel-L2 {worst:.2e} vs oracle, {worst_lay:.2e} vs layer kernels")
