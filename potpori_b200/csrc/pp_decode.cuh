@@ -168,7 +168,13 @@ __device__ __forceinline__ DecPlan dec_plan(const DecodeArgs& a, int b, int g, i
 
 // ---- producer --------------------------------------------------------------------------------
 __device__ __forceinline__ bool dec_acquire(DecRing& r) {
-  return r.n < (uint32_t)r.ns || mbar_wait(&r.empty[r.slot], r.phase ^ 1u);
+  if (r.n < (uint32_t)r.ns) return true;
+  // The ring is usually full: poll gently so the consumer warps keep the issue slots.
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(&r.empty[r.slot], r.phase ^ 1u)) return true;
+    __nanosleep(128);
+  }
+  return false;
 }
 
 __device__ __forceinline__ bool dec_issue_rows(DecRing& r, const void* src, int rows, int rowbytes,
