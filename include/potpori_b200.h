@@ -197,7 +197,8 @@ uint32_t pp_shard_sm_limit(const pp_shard* shard);
  * Qwen3-0.6B). Same step semantics as the per-layer path (src/qwen/model.rs:366-412 for one
  * token); the F32 summation order differs, within the parity tolerances. PP_E_UNSUPPORTED for
  * a shard without every layer or outside the kernel's sizes (hidden <= 8192, q_dim and
- * intermediate <= 16384, all multiples of 8). No counterpart in the reference. */
+ * intermediate <= 16384, all multiples of 8; 1, 2, 4 or 8 query heads per KV head). No
+ * counterpart in the reference. */
 pp_status pp_shard_set_decode_kernel(pp_shard* shard, int32_t enabled);
 int32_t pp_shard_decode_kernel(const pp_shard* shard);
 

@@ -328,11 +328,12 @@ __device__ __forceinline__ bool dec_grid_sync(const DecodeArgs& a, uint32_t targ
 // unit that holds pos, online softmax over the streamed cached rows (tiny.rs:77-101), the
 // unit's partial (max, sum, output) per query head, and the merge of the head's splits by
 // the last unit to finish.
+template <int G>  // query heads per KV head (a.G)
 __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeLayer& L,
                                               const DecPlan& P, DecRing& r, bool live, int pos,
                                               int layer, float* vec, int* flag, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
-  const int hd = a.hd, half = hd >> 1, G = a.G, h = P.h;
+  const int hd = a.hd, half = hd >> 1, h = P.h;
   float* qs = vec;             // [G][hd]
   float* kn = qs + G * hd;     // [hd]
   float* vn = kn + hd;         // [hd]
@@ -374,38 +375,36 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   // Lane l holds dims 4l..4l+3 of every query head and of the running outputs.
   const bool act = 4 * lane < hd;
   const int d0 = 4 * lane;
-  float q[8][4], o[8][4], m[8], l[8];
+  float q[G][4], o[G][4], m[G], l[G];
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
+  for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       o[g][j] = 0.f;
-      q[g][j] = (live && g < G && act) ? qs[g * hd + d0 + j] : 0.f;
+      q[g][j] = (live && act) ? qs[g * hd + d0 + j] : 0.f;
     }
   }
   // Online softmax over one or two keys (B valid when vb): the dot products of both keys are
   // reduced together so their shuffle chains overlap, then the state takes A, then B.
   auto visit2 = [&](const float (&ka)[4], const float (&va)[4], bool vb, const float (&kb)[4],
                     const float (&vb4)[4]) {
-    float sa[8], sb[8];
+    float sa[G], sb[G];
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
+    for (int g = 0; g < G; ++g) {
       sa[g] = (q[g][0] * ka[0] + q[g][1] * ka[1]) + (q[g][2] * ka[2] + q[g][3] * ka[3]);
       sb[g] = (q[g][0] * kb[0] + q[g][1] * kb[1]) + (q[g][2] * kb[2] + q[g][3] * kb[3]);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        if (g >= G) break;
+      for (int g = 0; g < G; ++g) {
         sa[g] += __shfl_xor_sync(0xffffffffu, sa[g], off);
         sb[g] += __shfl_xor_sync(0xffffffffu, sb[g], off);
       }
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      if (g >= G) break;
+    for (int g = 0; g < G; ++g) {
       float sc = sa[g] * a.inv_scale;
       float mn = fmaxf(m[g], sc);
       float al = __expf(m[g] - mn);  // 0 for the first key (m = -inf)
@@ -478,8 +477,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   // Merge the warps' partials: thread t handles (head g, dim d) of the unit's record.
   const int stride = hd + 4;
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    if (g >= G) break;
+  for (int g = 0; g < G; ++g) {
     float* mw = mrg + (size_t)(warp * G + g) * stride;
     if (lane == 0) {
       mw[0] = m[g];
@@ -516,18 +514,40 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
     *flag = atom_add_acq_rel_gpu(&a.sync[2 + h], 1u) == (uint32_t)((layer + 1) * S - 1);
   consumer_sync();
   if (*flag) {
-    // Last unit of head h: merge the S splits (exp(max_s - max) weights, split order).
+    // Last unit of head h: merge the S splits (exp(max_s - max) weights, split order). The
+    // splits' maxima and sums come in one batch of loads, then each thread's S outputs.
+    float* Ms = mrg;           // [G][S] (the warps' partials are no longer needed)
+    float* Ss = mrg + G * S;   // [G][S]
+    for (int e = tid; e < G * S; e += kConsumerWarps * 32) {
+      const int g = e / S, sp = e - g * S;
+      const float2 ml = __ldcg((const float2*)(a.part + ((size_t)(h * G + g) * S + sp) * stride));
+      Ms[e] = ml.x;
+      Ss[e] = ml.y;
+    }
+    consumer_sync();
     for (int e = tid; e < G * hd; e += kConsumerWarps * 32) {
       const int g = e / hd, d = e - g * hd;
-      const float* base = a.part + (size_t)(h * G + g) * S * stride;
+      const float* col = a.part + (size_t)(h * G + g) * S * stride + 4 + d;
+      float pv[32];
+#pragma unroll
+      for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
       float M = -INFINITY;
-      for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * stride));
+      for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
       float Ls = 0.f, O = 0.f;
-      for (int s = 0; s < S; ++s) {
-        const float ms = __ldcg(base + (size_t)s * stride);
+#pragma unroll
+      for (int sp = 0; sp < 32; ++sp) {
+        if (sp < S) {
+          const float ms = Ms[g * S + sp];
+          const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+          Ls += Ss[g * S + sp] * f;
+          O += pv[sp] * f;
+        }
+      }
+      for (int sp = 32; sp < S; ++sp) {
+        const float ms = Ms[g * S + sp];
         const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-        Ls += __ldcg(base + (size_t)s * stride + 1) * f;
-        O += __ldcg(base + (size_t)s * stride + 4 + d) * f;
+        Ls += Ss[g * S + sp] * f;
+        O += __ldcg(col + (size_t)sp * stride) * f;
       }
       a.attn[(h * G + g) * hd + d] = O / Ls;
     }
@@ -535,12 +555,13 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   return true;
 }
 
+template <int G>  // query heads per KV head (a.G)
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
+  const int NG = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int own_cap = (a.H + G - 1) / G + 1;
+  const int own_cap = (a.H + NG - 1) / NG + 1;
   const DecodeSmem lay(a.nslots, a.vec_floats, own_cap);
   DecRing r;
   r.base = smem;
@@ -568,7 +589,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
     fence_barrier_init();
   }
   __syncthreads();
-  const DecPlan P = dec_plan(a, b, G, pos);
+  const DecPlan P = dec_plan(a, b, NG, pos);
 
   // ------------------------------------------------------------------ producer thread
   if (warp == kConsumerWarps) {
@@ -649,13 +670,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
       lost = true;
       break;
     }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)G, flag, tid);
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // Attention.
-    if (P.h >= 0 && !dec_attention(a, L, P, r, live, pos, l, vec, flag, tid)) {
+    if (P.h >= 0 && !dec_attention<G>(a, L, P, r, live, pos, l, vec, flag, tid)) {
       lost = true;
       break;
     }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)G, flag, tid);
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // O projection + residual (src/qwen/model.rs:304-306).
     if (live) dec_stage_vec(a.attn, nullptr, a.Q, xa, xb, red, tid);
     if (!dec_rows(r, live, P.o1 - P.o0, a.Q * 2, P.rps_o, xa, xb, warp, lane,
@@ -672,7 +693,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
       lost = true;
       break;
     }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)G, flag, tid);
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // gate/up with the post-attention RMSNorm, SwiGLU (tiny.rs:111-115).
     if (live) {
       const float ss = dec_stage_vec(a.x, L.n_ffn, a.H, xa, xb, red, tid);
@@ -686,7 +707,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
       lost = true;
       break;
     }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)G, flag, tid);
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // down + residual.
     if (live) dec_stage_vec(a.act, nullptr, a.I, xa, xb, red, tid);
     if (!dec_rows(r, live, P.o1 - P.o0, a.I * 2, P.rps_d, xa, xb, warp, lane,
@@ -703,7 +724,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
       lost = true;
       break;
     }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)G, flag, tid);
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
   }
   if (lost) {
     if (tid == 0) {
@@ -715,7 +736,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
   if (!live || !a.final_norm) return;
   // The vocabulary head's operand: split(x * final_norm) and the sums of squares of x per
   // 128 columns (the layout input_prep_kernel writes).
-  for (int t = b; t < a.ss_tiles; t += G) {
+  for (int t = b; t < a.ss_tiles; t += NG) {
     float v = 0.f;
     const int n = t * 128 + tid;
     if (tid < 128 && n < a.H) {

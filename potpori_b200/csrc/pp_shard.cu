@@ -607,7 +607,12 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CK(cudaLaunchKernelEx(&cfg, decode_step_kernel, a));
+  switch (s->G) {  // set_decode_kernel admits 1, 2, 4 or 8 query heads per KV head
+    case 1: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<1>, a)); break;
+    case 2: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<2>, a)); break;
+    case 4: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<4>, a)); break;
+    default: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<8>, a)); break;
+  }
   if ((r = after_launch(s, st, PP_K_DECODE))) return r;
   return launch_head<1>(s, st);
 }
@@ -639,7 +644,8 @@ pp_status set_attrs(pp_shard* s) {
   pp_status r;
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
-      (r = set_max_smem(s, decode_step_kernel)))
+      (r = set_max_smem(s, decode_step_kernel<1>)) || (r = set_max_smem(s, decode_step_kernel<2>)) ||
+      (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)))
     return r;
   return PP_OK;
 }
@@ -1608,10 +1614,14 @@ pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
     if (!(s->first && s->last))
       return fail(s, PP_E_UNSUPPORTED, "the decode kernel runs shards that hold every layer");
     if (s->H % 8 || s->Q % 8 || s->I % 8 || 4 * s->H > kDecSlot || 2 * s->Q > kDecSlot ||
-        2 * s->I > kDecSlot || kv_row_bytes(s->hd) > kDecKvHalf)
+        2 * s->I > kDecSlot || kv_row_bytes(s->hd) > kDecKvHalf ||
+        (s->G != 1 && s->G != 2 && s->G != 4 && s->G != 8))
       return fail(s, PP_E_UNSUPPORTED, "geometry outside the decode kernel's row and slot sizes");
     const int vec = decode_vec_floats(s->H, s->Q, s->I, s->hd, s->G);
-    const size_t budget = dyn_smem_limit(s, decode_step_kernel);
+    size_t budget = dyn_smem_limit(s, decode_step_kernel<1>);
+    for (size_t b : {dyn_smem_limit(s, decode_step_kernel<2>), dyn_smem_limit(s, decode_step_kernel<4>),
+                     dyn_smem_limit(s, decode_step_kernel<8>)})
+      budget = b < budget ? b : budget;
     const size_t fixed = DecodeSmem(0, vec, decode_own_cap(s, s->nkv)).total();
     const int ns = budget > fixed ? (int)((budget - fixed) / kDecSlot) : 0;
     if (ns < 2) return fail(s, PP_E_UNSUPPORTED, "the decode kernel's ring does not fit");
