@@ -344,21 +344,32 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
       if (!isq && !P.has_new) continue;
       const float* src = a.qkv + (isq ? (h * G + p) * hd : a.Q + h * hd);
       const float* w = isq ? L.n_q : L.n_k;
-      float ssq = 0.f;
-      for (int i = lane; i < hd; i += 32) {
-        const float v = __ldcg(src + i);
-        ssq += v * v;
+      const float2* rp = a.rope + (size_t)pos * half;
+      // One batch of loads per lane: its raw values, norm weights and (cos, sin) pairs for
+      // dims i and i + half, i = lane + 32 t (head_dim <= 128).
+      float x0[2], x1[2], w0[2], w1[2];
+      float2 cs[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int i = lane + 32 * t;
+        const bool in = i < half;
+        x0[t] = in ? __ldcg(src + i) : 0.f;
+        x1[t] = in ? __ldcg(src + i + half) : 0.f;
+        w0[t] = in ? w[i] : 0.f;
+        w1[t] = in ? w[i + half] : 0.f;
+        cs[t] = in ? rp[i] : make_float2(0.f, 0.f);
       }
-      ssq = warp_sum(ssq);
+      const float ssq = warp_sum((x0[0] * x0[0] + x1[0] * x1[0]) + (x0[1] * x0[1] + x1[1] * x1[1]));
       const float rms = sqrtf(ssq / (float)hd + a.eps);
       float* dst = isq ? qs + p * hd : kn;
-      const float2* rp = a.rope + (size_t)pos * half;
-      for (int i = lane; i < half; i += 32) {
-        const float x0 = __ldcg(src + i) / rms * w[i];
-        const float x1 = __ldcg(src + i + half) / rms * w[i + half];
-        const float2 cs = rp[i];
-        dst[i] = x0 * cs.x - x1 * cs.y;
-        dst[i + half] = x1 * cs.x + x0 * cs.y;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int i = lane + 32 * t;
+        if (i < half) {
+          const float y0 = x0[t] / rms * w0[t], y1 = x1[t] / rms * w1[t];
+          dst[i] = y0 * cs[t].x - y1 * cs[t].y;
+          dst[i + half] = y1 * cs[t].x + y0 * cs[t].y;
+        }
       }
     }
     if (P.has_new)
