@@ -270,18 +270,32 @@ __device__ __forceinline__ bool dec_rows(DecRing& r, bool live, int rows, int ro
 // squares of src, reduced in the same order in every CTA.
 __device__ __forceinline__ float dec_stage_vec(const float* src, const float* w, int K, float4* xa,
                                                float4* xb, float* red, int tid) {
+  constexpr int T = kConsumerWarps * 32, B = 4;  // float4s per thread per batch of loads
   float ss = 0.f;
-  for (int q = tid; q < (K >> 2); q += kConsumerWarps * 32) {
-    float4 v = __ldcg((const float4*)src + q);
-    ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-    if (w) {
-      const float4 ww = ((const float4*)w)[q];
-      v.x *= ww.x;
-      v.y *= ww.y;
-      v.z *= ww.z;
-      v.w *= ww.w;
+  for (int q0 = 0; q0 < (K >> 2); q0 += B * T) {
+    float4 v[B], ww[B];
+#pragma unroll
+    for (int k = 0; k < B; ++k) {  // every load of the batch in flight together
+      const int q = q0 + tid + k * T;
+      const bool in = q < (K >> 2);
+      v[k] = in ? __ldcg((const float4*)src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ww[k] = (in && w) ? ((const float4*)w)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
     }
-    ((q & 1) ? xb : xa)[q >> 1] = v;
+#pragma unroll
+    for (int k = 0; k < B; ++k) {
+      const int q = q0 + tid + k * T;
+      if (q < (K >> 2)) {
+        float4 x = v[k];
+        ss += (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+        if (w) {
+          x.x *= ww[k].x;
+          x.y *= ww[k].y;
+          x.z *= ww[k].z;
+          x.w *= ww[k].w;
+        }
+        ((q & 1) ? xb : xa)[q >> 1] = x;
+      }
+    }
   }
   ss = warp_sum(ss);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -339,6 +353,8 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   float* vn = kn + hd;         // [hd]
   float* mrg = vn + hd;        // [warps][G][hd + 4]
   if (live) {
+    // The new value row rides along with the first batch of loads (hd <= 256 threads).
+    const float vnew = (P.has_new && tid < hd) ? __ldcg(a.qkv + a.Q + a.KV + h * hd + tid) : 0.f;
     for (int p = warp; p <= G; p += kConsumerWarps) {
       const bool isq = p < G;
       if (!isq && !P.has_new) continue;
@@ -372,8 +388,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
         }
       }
     }
-    if (P.has_new)
-      for (int i = tid; i < hd; i += kConsumerWarps * 32) vn[i] = __ldcg(a.qkv + a.Q + a.KV + h * hd + i);
+    if (P.has_new && tid < hd) vn[tid] = vnew;
     consumer_sync();
     if (P.has_new) {
       const size_t off = ((size_t)h * a.capacity + pos) * kv_row_bytes(hd);
