@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--draft-kernel", default="decode", choices=["decode", "layers"],
                     help="1-row draft steps: one persistent decode kernel, or six kernels per layer")
+    ap.add_argument("--draft-sms", type=int, default=0,
+                    help="one GPU: run the draft on this many SMs and the target on the rest, "
+                         "so draft steps and verify passes overlap (0: both use every SM)")
     ap.add_argument("--nccl-sms", type=int, default=None,
                     help="SMs left to NCCL's transfer kernels on every rank when N > 1")
     return ap.parse_args()
@@ -249,6 +252,9 @@ def run_ours(args):
     dmodel = QwenTarget(stage) if wl.draft_is_target and world == 1 else \
         QwenTarget.random(wl.draft, wl.max_seq, wl.chunk, wl.draft_seed, device=local)
     dmodel.shard.set_sm_limit(sm_budget)
+    if args.draft_sms and world == 1 and dmodel.shard is not stage:
+        dmodel.shard.set_sm_limit(args.draft_sms)
+        stage.set_sm_limit(n_sms - args.draft_sms)
     if args.draft_kernel == "decode":
         dmodel.shard.set_decode_kernel(True)
     draft = IncrementalDraft(dmodel, wl.chunk)
@@ -369,6 +375,7 @@ def run_ours(args):
             "workload": wl.name, "target": f"Qwen3-4B (36 layers, random BF16 weights seed {wl.target_seed})",
             "draft": f"Qwen3-0.6B (seed {wl.draft_seed})", "gamma": wl.gamma, "depth": wl.depth,
             "max_seq": wl.max_seq, "prompt_len": wl.prompt_len, "layers_per_gpu": ranges, "sm_budget": stage.sm_limit(),
+            "draft_sm_budget": dmodel.shard.sm_limit(),
             "draft_step": ("one persistent decode kernel + vocab head" if dmodel.shard.decode_kernel()
                            else "per-layer kernels"),
             "global_batch": 1, "weights": "bf16 storage, f32 arithmetic",
