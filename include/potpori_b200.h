@@ -202,6 +202,21 @@ uint32_t pp_shard_sm_limit(const pp_shard* shard);
 pp_status pp_shard_set_decode_kernel(pp_shard* shard, int32_t enabled);
 int32_t pp_shard_decode_kernel(const pp_shard* shard);
 
+/* Prompt-sized projection on the 5th-generation tensor cores (tcgen05 MMA, TMEM accumulator):
+ * with device pointers,
+ *   y[i][j] = sum_c W[j][c] * x[i][c]    for i < t rows, j < n, c < k,
+ * the linear of src/qwen/model.rs:166-183 at prefill sizes (a 2048-token prompt chunk is a
+ * dense contraction, not a skinny GEMV). W is BF16 in the tiled layout described at
+ * pp_norm_gemv_static (the shards' layout), x is [t][k] and y [t][n] F32. x is split into
+ * BF16 hi + lo parts in `work` (caller-owned device memory, 1024-byte aligned, at least
+ * pp_rows_gemm_work_bytes(t, k) bytes) and every K step accumulates W.hi + W.lo in F32, the
+ * reference's F32 arithmetic to about 2^-17 relative per product. *err (device memory, zero
+ * before the call) gets a nonzero bit when a bounded wait on the device expired. Asynchronous
+ * on `stream` (a cudaStream_t, NULL = default). */
+uint64_t pp_rows_gemm_work_bytes(uint32_t t, uint32_t k);
+pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const float* x, uint32_t t,
+                       float* y, void* work, uint64_t work_bytes, uint32_t* err, void* stream);
+
 /* Allocation-free RMSNorm + skinny GEMV (no counterpart in the reference; an addition for
  * callers that cannot allocate device memory: code running inside a host framework or memory
  * pool that owns every allocation, or a context where cudaMalloc/cudaFree and their implicit

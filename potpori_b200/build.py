@@ -14,7 +14,8 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libpotpori_b200.so")
-SOURCES = [os.path.join(HERE, "csrc", "pp_shard.cu"), os.path.join(HERE, "csrc", "pp_static_gemv.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "pp_shard.cu"), os.path.join(HERE, "csrc", "pp_static_gemv.cu"),
+           os.path.join(HERE, "csrc", "pp_prefill.cu")]
 DEPS = SOURCES + glob.glob(os.path.join(HERE, "csrc", "*.cuh")) + [
     os.path.join(ROOT, "include", "potpori_b200.h")]
 

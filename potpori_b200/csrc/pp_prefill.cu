@@ -1,0 +1,282 @@
+// Prompt-sized projection on the 5th-generation tensor cores (tcgen05 + TMEM):
+//   y[t][j] = sum_c W[j][c] * x[t][c]   for t < T rows (a prompt chunk), j < n, c < k,
+// W BF16 in the shards' tiled layout, x and y F32 — the linear of src/qwen/model.rs:166-183
+// at the M = 2048 prefill of the 8-stage workload, where the shape is a dense contraction.
+//
+// Layout and arithmetic. A tiled weight block (128 rows x 64 columns, the 16-byte unit u of
+// row r at u ^ (r & 7)) is already the canonical K-major SWIZZLE_128B operand of the MMA
+// (8-row atoms of 1024 bytes), so one 1-D bulk copy moves it into shared memory unchanged.
+// The activations are split x = hi + lo (hi = bf16(x), lo = bf16(x - hi), about 2^-17
+// relative) by pp_rows_split_kernel into blocks of the same form (256 rows x 64 columns per
+// part), and every K step issues two MMAs, W.hi and W.lo, into one F32 accumulator: the
+// products of BF16 are exact and the sum is the reference's F32 arithmetic to its rounding.
+//
+// Kernel (one CTA per 128 weight rows x 256 activation rows, 192 threads):
+//  * warp 0, one thread: per 64-column chunk, the weight block (16 KB) and the two activation
+//    parts (32 KB each) into one of two 80 KB stages (bulk copies, mbarrier transaction
+//    counts; no multicast);
+//  * warp 1: allocates 256 TMEM columns (128 lanes x 256 F32: the whole 128 x 256 tile), and
+//    one thread issues tcgen05.mma (kind::f16, M = 128, N = 256, K = 16) and returns each
+//    stage to the producer with tcgen05.commit on its empty barrier;
+//  * warps 2-5: after the last commit, tcgen05.ld the accumulator rows (warp w reads TMEM
+//    lanes 32 (w % 4) .. + 31) and store y with consecutive lanes on consecutive j.
+// Every wait is bounded; a wait that expires sets the error word and the CTA still frees
+// its TMEM and lets its copies land before it exits.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "../../include/potpori_b200.h"
+#include "pp_common.cuh"
+
+using namespace pp;
+
+namespace pp {
+
+constexpr int kRgM = 128;                      // weight rows per tile (TMEM lanes)
+constexpr int kRgN = 256;                      // activation rows per tile (TMEM columns)
+constexpr int kRgWBytes = kRgM * kChunkK * 2;  // 16 KB weight block
+constexpr int kRgXBytes = kRgN * kChunkK * 2;  // 32 KB per activation part
+constexpr int kRgStage = kRgWBytes + 2 * kRgXBytes;
+constexpr int kRgStages = 2;
+constexpr int kRgThreads = 192;
+constexpr size_t kRgSmem = (size_t)kRgStages * kRgStage + 256 + 1024;
+
+// Instruction descriptor of tcgen05.mma kind::f16: F32 accumulator, BF16 A and B, both
+// K-major, N = 256 (bits 17-22: N / 8), M = 128 (bits 24-28: M / 16).
+constexpr uint32_t kRgIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRgN >> 3) << 17) |
+                              ((uint32_t)(kRgM >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major SWIZZLE_128B operand at byte address saddr
+// (1024-aligned): start >> 4, leading offset 1 (unused for this swizzle), stride between
+// 8-row atoms 1024 B (>> 4 = 64), descriptor version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t rg_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void rg_mma(uint32_t tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(adesc), "l"(bdesc), "r"(kRgIdesc), "r"(acc));
+}
+__device__ __forceinline__ void rg_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void rg_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void rg_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Splits F32 rows x[t][c] (row stride ldx) into the MMA's activation blocks:
+// xs[tb][chunk][part][256 rows][64 columns] BF16, part 0 = hi, 1 = lo, the 16-byte unit u of
+// row r at u ^ (r & 7); rows past T and columns past k are zero. One thread per (row, unit).
+__global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int32_t k,
+                                     int32_t kchunks, int32_t tblocks, uint8_t* xs) {
+  const int64_t units = (int64_t)tblocks * kRgN * kchunks * 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < units;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / (kchunks * 8);
+    const int u = (int)(i - row * (kchunks * 8));  // unit over the whole padded row
+    const int c = u >> 3, uu = u & 7;
+    const int tb = (int)(row / kRgN), r = (int)(row % kRgN);
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint16_t h[2], l[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int col = c * kChunkK + uu * 8 + 2 * e + q;
+        const float v = (row < T && col < k) ? x[row * (int64_t)ldx + col] : 0.f;
+        split_bf16(v, h[q], l[q]);
+      }
+      hi[e] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+      lo[e] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
+    }
+    uint8_t* blk = xs + ((size_t)tb * kchunks + c) * 2 * kRgXBytes;
+    const size_t off = (size_t)r * 128 + (size_t)((uu ^ (r & 7)) << 4);
+    *(uint4*)(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *(uint4*)(blk + kRgXBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// Grid (n tiles, T blocks of 256), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
+__global__ void __launch_bounds__(kRgThreads, 1)
+    pp_rows_gemm_kernel(const uint16_t* w, const uint8_t* xs, float* y, int32_t ldy, int32_t n,
+                        int32_t T, int32_t kchunks, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + (size_t)kRgStages * kRgStage);
+  uint64_t* empty = full + kRgStages;
+  uint64_t* done = empty + kRgStages;
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, tb = blockIdx.y;
+
+  if (tid == 0) {
+    for (int s = 0; s < kRgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {  // the whole warp allocates; the address lands in shared memory
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kRgN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  rg_fence_before();
+  __syncthreads();
+  rg_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int c = 0; c < kchunks; ++c) {
+        const int s = c % kRgStages;
+        const uint32_t use = (uint32_t)(c / kRgStages);
+        if (c >= kRgStages && !mbar_wait(&empty[s], (use - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + (size_t)s * kRgStage;
+        mbar_arrive_expect_tx(&full[s], kRgStage);
+        bulk_load(st, w + ((size_t)tile * kchunks + c) * (kRgM * kChunkK), kRgWBytes, &full[s]);
+        const uint8_t* xb = xs + ((size_t)tb * kchunks + c) * 2 * kRgXBytes;
+        bulk_load(st + kRgWBytes, xb, kRgXBytes, &full[s]);
+        bulk_load(st + kRgWBytes + kRgXBytes, xb + kRgXBytes, kRgXBytes, &full[s]);
+        issued = c + 1;
+      }
+      if (!ok) {
+        atomicOr(err, 1u);
+        for (int c = issued > kRgStages ? issued - kRgStages : 0; c < issued; ++c)
+          mbar_wait(&full[c % kRgStages], (uint32_t)(c / kRgStages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int c = 0; c < kchunks && ok; ++c) {
+        const int s = c % kRgStages;
+        if (!mbar_wait(&full[s], (uint32_t)(c / kRgStages) & 1u)) {
+          ok = false;
+          break;
+        }
+        rg_fence_after();
+        const uint32_t base = smem_u32(smem + (size_t)s * kRgStage);
+        const uint64_t a = rg_desc(base), bh = rg_desc(base + kRgWBytes),
+                       bl = rg_desc(base + kRgWBytes + kRgXBytes);
+#pragma unroll
+        for (int j = 0; j < kChunkK / 16; ++j) {  // K = 16 per MMA: +32 bytes = +2 in the descriptor
+          rg_mma(tmem, a + 2 * j, bh + 2 * j, (c | j) != 0);
+          rg_mma(tmem, a + 2 * j, bl + 2 * j, 1u);
+        }
+        rg_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      if (!ok) atomicOr(err, 2u);
+      rg_commit(done);  // arrives when every MMA issued above has completed
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32 (w % 4) ..; lane = weight row, column = row of x.
+    const int q = warp & 3;
+    const bool ok = mbar_wait(done, 0);
+    rg_fence_after();
+    if (ok) {
+      const int j = tile * kRgM + q * 32 + lane;
+      for (int cc = 0; cc < kRgN / 32; ++cc) {
+        uint32_t v[32];
+        const uint32_t addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+            "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, "
+            "%26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+              "=r"(v[30]), "=r"(v[31])
+            : "r"(addr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (j < n) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int t = tb * kRgN + cc * 32 + e;
+            if (t < T) y[(size_t)t * ldy + j] = __uint_as_float(v[e]);
+          }
+        }
+      }
+    } else if (lane == 0) {
+      atomicOr(err, 4u);
+    }
+  }
+  rg_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    rg_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kRgN));
+  }
+}
+
+}  // namespace pp
+
+namespace {
+pp_status rg_fail(pp_status st, const char* msg) {
+  pp::set_global_error(msg);
+  return st;
+}
+}  // namespace
+
+extern "C" uint64_t pp_rows_gemm_work_bytes(uint32_t t, uint32_t k) {
+  const uint64_t tblocks = (t + kRgN - 1) / kRgN, kchunks = (k + kChunkK - 1) / kChunkK;
+  return tblocks * kchunks * 2 * (uint64_t)kRgXBytes;
+}
+
+extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const float* x,
+                                  uint32_t t, float* y, void* work, uint64_t work_bytes,
+                                  uint32_t* err, void* stream) {
+  if (!w_tiled || !x || !y || !work || !err) return rg_fail(PP_E_INVALID, "null argument");
+  if (n == 0 || k == 0 || t == 0 || n > (1u << 24) || k > (1u << 20) || t > (1u << 20))
+    return rg_fail(PP_E_INVALID, "sizes out of range");
+  if (work_bytes < pp_rows_gemm_work_bytes(t, k))
+    return rg_fail(PP_E_INVALID, "work buffer smaller than pp_rows_gemm_work_bytes(t, k)");
+  if ((uintptr_t)w_tiled % 16 || (uintptr_t)work % 1024)
+    return rg_fail(PP_E_INVALID, "w_tiled must be 16-byte and work 1024-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return rg_fail(PP_E_CUDA, "no current device");
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(pp_rows_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kRgSmem) != cudaSuccess)
+      return rg_fail(PP_E_CUDA, "cannot reserve the GEMM's shared memory");
+    attr_done[dev] = true;
+  }
+  const int kchunks = (int)((k + kChunkK - 1) / kChunkK);
+  const int tblocks = (int)((t + kRgN - 1) / kRgN);
+  const int tiles = (int)((n + kRgM - 1) / kRgM);
+  const int64_t units = (int64_t)tblocks * kRgN * kchunks * 8;
+  const int sgrid = (int)((units + 255) / 256 < 4096 ? (units + 255) / 256 : 4096);
+  pp_rows_split_kernel<<<sgrid, 256, 0, st>>>(x, (int32_t)k, (int32_t)t, (int32_t)k, kchunks,
+                                              tblocks, (uint8_t*)work);
+  pp_rows_gemm_kernel<<<dim3(tiles, tblocks), kRgThreads, kRgSmem, st>>>(
+      w_tiled, (const uint8_t*)work, y, (int32_t)n, (int32_t)n, (int32_t)t, kchunks, err);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    char msg[160];
+    snprintf(msg, sizeof msg, "pp_rows_gemm launch: %s", cudaGetErrorString(e));
+    return rg_fail(PP_E_CUDA, msg);
+  }
+  return PP_OK;
+}
