@@ -7,16 +7,16 @@
 // row r at u ^ (r & 7)) is already the canonical K-major SWIZZLE_128B operand of the MMA
 // (8-row atoms of 1024 bytes), so one 1-D bulk copy moves it into shared memory unchanged.
 // The activations are split x = hi + lo (hi = bf16(x), lo = bf16(x - hi), about 2^-17
-// relative) by pp_rows_split_kernel into blocks of the same form (256 rows x 64 columns per
+// relative) by pp_rows_split_kernel into blocks of the same form (128 rows x 64 columns per
 // part), and every K step issues two MMAs, W.hi and W.lo, into one F32 accumulator: the
 // products of BF16 are exact and the sum is the reference's F32 arithmetic to its rounding.
 //
-// Kernel (one CTA per 128 weight rows x 256 activation rows, 192 threads):
+// Kernel (one CTA per 128 weight rows x 128 activation rows, 192 threads):
 //  * warp 0, one thread: per 64-column chunk, the weight block (16 KB) and the two activation
-//    parts (32 KB each) into one of two 80 KB stages (bulk copies, mbarrier transaction
+//    parts (16 KB each) into one of four 48 KB stages (bulk copies, mbarrier transaction
 //    counts; no multicast);
-//  * warp 1: allocates 256 TMEM columns (128 lanes x 256 F32: the whole 128 x 256 tile), and
-//    one thread issues tcgen05.mma (kind::f16, M = 128, N = 256, K = 16) and returns each
+//  * warp 1: allocates 128 TMEM columns (128 lanes x 128 F32: the whole 128 x 128 tile), and
+//    one thread issues tcgen05.mma (kind::f16, M = 128, N = 128, K = 16) and returns each
 //    stage to the producer with tcgen05.commit on its empty barrier;
 //  * warps 2-5: after the last commit, tcgen05.ld the accumulator rows (warp w reads TMEM
 //    lanes 32 (w % 4) .. + 31) and store y with consecutive lanes on consecutive j.
@@ -34,16 +34,16 @@ using namespace pp;
 namespace pp {
 
 constexpr int kRgM = 128;                      // weight rows per tile (TMEM lanes)
-constexpr int kRgN = 256;                      // activation rows per tile (TMEM columns)
+constexpr int kRgN = 128;                      // activation rows per tile (TMEM columns)
 constexpr int kRgWBytes = kRgM * kChunkK * 2;  // 16 KB weight block
-constexpr int kRgXBytes = kRgN * kChunkK * 2;  // 32 KB per activation part
+constexpr int kRgXBytes = kRgN * kChunkK * 2;  // 16 KB per activation part
 constexpr int kRgStage = kRgWBytes + 2 * kRgXBytes;
-constexpr int kRgStages = 2;
+constexpr int kRgStages = 4;  // 4 x 48 KB: a refill from L2 outlasts one stage's MMAs
 constexpr int kRgThreads = 192;
 constexpr size_t kRgSmem = (size_t)kRgStages * kRgStage + 256 + 1024;
 
 // Instruction descriptor of tcgen05.mma kind::f16: F32 accumulator, BF16 A and B, both
-// K-major, N = 256 (bits 17-22: N / 8), M = 128 (bits 24-28: M / 16).
+// K-major, N = 128 (bits 17-22: N / 8), M = 128 (bits 24-28: M / 16).
 constexpr uint32_t kRgIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRgN >> 3) << 17) |
                               ((uint32_t)(kRgM >> 4) << 24);
 
@@ -75,7 +75,7 @@ __device__ __forceinline__ void rg_fence_after() {
 }
 
 // Splits F32 rows x[t][c] (row stride ldx) into the MMA's activation blocks:
-// xs[tb][chunk][part][256 rows][64 columns] BF16, part 0 = hi, 1 = lo, the 16-byte unit u of
+// xs[tb][chunk][part][128 rows][64 columns] BF16, part 0 = hi, 1 = lo, the 16-byte unit u of
 // row r at u ^ (r & 7); rows past T and columns past k are zero. One thread per (row, unit).
 __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int32_t k,
                                      int32_t kchunks, int32_t tblocks, uint8_t* xs) {
@@ -106,7 +106,7 @@ __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int
   }
 }
 
-// Grid (n tiles, T blocks of 256), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
+// Grid (n tiles, T blocks of 128), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
 __global__ void __launch_bounds__(kRgThreads, 1)
     pp_rows_gemm_kernel(const uint16_t* w, const uint8_t* xs, float* y, int32_t ldy, int32_t n,
                         int32_t T, int32_t kchunks, uint32_t* err) {
