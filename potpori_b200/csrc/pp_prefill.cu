@@ -106,7 +106,7 @@ __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int
   }
 }
 
-// Grid (n tiles, T blocks of 128), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
+// Grid (T blocks of 128, n tiles), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
 __global__ void __launch_bounds__(kRgThreads, 1)
     pp_rows_gemm_kernel(const uint16_t* w, const uint8_t* xs, float* y, int32_t ldy, int32_t n,
                         int32_t T, int32_t kchunks, uint32_t* err) {
@@ -117,7 +117,9 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   uint64_t* done = empty + kRgStages;
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, tb = blockIdx.y;
+  // Token blocks vary fastest: the CTAs in flight together share a weight tile (read from
+  // DRAM about once) and all token blocks of the activations stay in L2.
+  const int tb = blockIdx.x, tile = blockIdx.y;
 
   if (tid == 0) {
     for (int s = 0; s < kRgStages; ++s) {
@@ -270,7 +272,7 @@ extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t 
   const int sgrid = (int)((units + 255) / 256 < 4096 ? (units + 255) / 256 : 4096);
   pp_rows_split_kernel<<<sgrid, 256, 0, st>>>(x, (int32_t)k, (int32_t)t, (int32_t)k, kchunks,
                                               tblocks, (uint8_t*)work);
-  pp_rows_gemm_kernel<<<dim3(tiles, tblocks), kRgThreads, kRgSmem, st>>>(
+  pp_rows_gemm_kernel<<<dim3(tblocks, tiles), kRgThreads, kRgSmem, st>>>(
       w_tiled, (const uint8_t*)work, y, (int32_t)n, (int32_t)n, (int32_t)t, kchunks, err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
