@@ -51,8 +51,11 @@ def parse_args():
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
-    ap.add_argument("--draft-kernel", default="decode", choices=["decode", "layers"],
-                    help="1-row draft steps: one persistent decode kernel, or six kernels per layer")
+    ap.add_argument("--draft-kernel", default="auto", choices=["auto", "decode", "layers"],
+                    help="1-row draft steps: one persistent decode kernel, or six kernels per "
+                         "layer; auto = the decode kernel on one GPU, the per-layer kernels when "
+                         "NCCL transfer kernels share rank 0's SMs (the decode kernel's "
+                         "cooperative launch waits for them)")
     ap.add_argument("--draft-sms", type=int, default=0,
                     help="one GPU: run the draft on this many SMs and the target on the rest, "
                          "so draft steps and verify passes overlap (0: both use every SM)")
@@ -255,7 +258,7 @@ def run_ours(args):
     if args.draft_sms and world == 1 and dmodel.shard is not stage:
         dmodel.shard.set_sm_limit(args.draft_sms)
         stage.set_sm_limit(n_sms - args.draft_sms)
-    if args.draft_kernel == "decode":
+    if args.draft_kernel == "decode" or (args.draft_kernel == "auto" and world == 1):
         dmodel.shard.set_decode_kernel(True)
     draft = IncrementalDraft(dmodel, wl.chunk)
     if world == 1:
