@@ -11,15 +11,18 @@
 // part), and every K step issues two MMAs, W.hi and W.lo, into one F32 accumulator: the
 // products of BF16 are exact and the sum is the reference's F32 arithmetic to its rounding.
 //
-// Kernel (one CTA per 128 weight rows x 128 activation rows, 192 threads):
-//  * warp 0, one thread: per 64-column chunk, the weight block (16 KB) and the two activation
-//    parts (16 KB each) into one of four 48 KB stages (bulk copies, mbarrier transaction
-//    counts; no multicast);
-//  * warp 1: allocates 128 TMEM columns (128 lanes x 128 F32: the whole 128 x 128 tile), and
-//    one thread issues tcgen05.mma (kind::f16, M = 128, N = 128, K = 16) and returns each
-//    stage to the producer with tcgen05.commit on its empty barrier;
-//  * warps 2-5: after the last commit, tcgen05.ld the accumulator rows (warp w reads TMEM
-//    lanes 32 (w % 4) .. + 31) and store y with consecutive lanes on consecutive j.
+// Kernel (persistent, one CTA per SM looping over 128 weight rows x 128 activation rows units,
+// 192 threads):
+//  * warp 0, one thread: per 64-column chunk of every unit of the CTA, the weight block
+//    (16 KB) and the two activation parts (16 KB each) into a ring of four 48 KB stages (bulk
+//    copies, mbarrier transaction counts; no multicast), without draining between units;
+//  * warp 1: allocates 256 TMEM columns (two 128 x 128 F32 accumulators), and one thread
+//    issues tcgen05.mma (kind::f16, M = 128, N = 128, K = 16) into the accumulator of the
+//    unit, returns each stage to the producer with tcgen05.commit on its empty barrier and
+//    marks the accumulator full when the unit's last chunk is in;
+//  * warps 2-5: tcgen05.ld a full accumulator (warp w reads TMEM lanes 32 (w % 4) .. + 31),
+//    store y with consecutive lanes on consecutive j, and hand the accumulator back, so one
+//    unit's epilogue runs under the next unit's MMAs.
 // Every wait is bounded; a wait that expires sets the error word and the CTA still frees
 // its TMEM and lets its copies land before it exits.
 #include <cuda_runtime.h>
@@ -106,25 +109,33 @@ __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int
   }
 }
 
-// Grid (T blocks of 128, n tiles), kRgThreads threads, kRgSmem bytes of dynamic shared memory.
+// Persistent: one CTA per SM (gridDim.x <= units), kRgThreads threads, kRgSmem bytes of
+// dynamic shared memory. Work unit u = (weight tile u / tblocks, token block u % tblocks): token
+// blocks vary fastest, so the CTAs in flight share weight tiles (each read from DRAM about
+// once) and the activations stay in L2. CTA b takes u = b, b + gridDim.x, ...; its producer
+// streams the chunks of all its units through the stage ring without draining between them,
+// and two TMEM accumulators let the epilogue of one unit run under the MMAs of the next.
 __global__ void __launch_bounds__(kRgThreads, 1)
     pp_rows_gemm_kernel(const uint16_t* w, const uint8_t* xs, float* y, int32_t ldy, int32_t n,
-                        int32_t T, int32_t kchunks, uint32_t* err) {
+                        int32_t T, int32_t kchunks, int32_t tblocks, int32_t units, uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + (size_t)kRgStages * kRgStage);
   uint64_t* empty = full + kRgStages;
-  uint64_t* done = empty + kRgStages;
+  uint64_t* afull = empty + kRgStages;  // [2] accumulator b holds a finished unit
+  uint64_t* aempty = afull + 2;         // [2] accumulator b was drained by the epilogue
+  uint64_t* done = aempty + 2;          // every MMA of this CTA has completed
   uint32_t* tmem_slot = (uint32_t*)(done + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Token blocks vary fastest: the CTAs in flight together share a weight tile (read from
-  // DRAM about once) and all token blocks of the activations stay in L2.
-  const int tb = blockIdx.x, tile = blockIdx.y;
 
   if (tid == 0) {
     for (int s = 0; s < kRgStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&afull[b], 1);
+      mbar_init(&aempty[b], 4);  // the four epilogue warps
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -132,7 +143,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   if (warp == 1) {  // the whole warp allocates; the address lands in shared memory
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kRgN));
+                 "r"(2 * kRgN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   rg_fence_before();
@@ -142,62 +153,82 @@ __global__ void __launch_bounds__(kRgThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
+      int it = 0;  // chunks issued by this CTA
       bool ok = true;
-      for (int c = 0; c < kchunks; ++c) {
-        const int s = c % kRgStages;
-        const uint32_t use = (uint32_t)(c / kRgStages);
-        if (c >= kRgStages && !mbar_wait(&empty[s], (use - 1) & 1u)) {
-          ok = false;
-          break;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tb = u % tblocks, tile = u / tblocks;
+        for (int c = 0; c < kchunks; ++c) {
+          const int s = it % kRgStages;
+          const uint32_t use = (uint32_t)(it / kRgStages);
+          if (it >= kRgStages && !mbar_wait(&empty[s], (use - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + (size_t)s * kRgStage;
+          mbar_arrive_expect_tx(&full[s], kRgStage);
+          bulk_load(st, w + ((size_t)tile * kchunks + c) * (kRgM * kChunkK), kRgWBytes, &full[s]);
+          const uint8_t* xb = xs + ((size_t)tb * kchunks + c) * 2 * kRgXBytes;
+          bulk_load(st + kRgWBytes, xb, kRgXBytes, &full[s]);
+          bulk_load(st + kRgWBytes + kRgXBytes, xb + kRgXBytes, kRgXBytes, &full[s]);
+          ++it;
         }
-        uint8_t* st = smem + (size_t)s * kRgStage;
-        mbar_arrive_expect_tx(&full[s], kRgStage);
-        bulk_load(st, w + ((size_t)tile * kchunks + c) * (kRgM * kChunkK), kRgWBytes, &full[s]);
-        const uint8_t* xb = xs + ((size_t)tb * kchunks + c) * 2 * kRgXBytes;
-        bulk_load(st + kRgWBytes, xb, kRgXBytes, &full[s]);
-        bulk_load(st + kRgWBytes + kRgXBytes, xb + kRgXBytes, kRgXBytes, &full[s]);
-        issued = c + 1;
       }
       if (!ok) {
         atomicOr(err, 1u);
-        for (int c = issued > kRgStages ? issued - kRgStages : 0; c < issued; ++c)
+        for (int c = it > kRgStages ? it - kRgStages : 0; c < it; ++c)
           mbar_wait(&full[c % kRgStages], (uint32_t)(c / kRgStages) & 1u);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = true;
-      for (int c = 0; c < kchunks && ok; ++c) {
-        const int s = c % kRgStages;
-        if (!mbar_wait(&full[s], (uint32_t)(c / kRgStages) & 1u)) {
+      int it = 0, i = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait(&aempty[b], (uint32_t)((i >> 1) - 1) & 1u)) {
           ok = false;
           break;
         }
         rg_fence_after();
-        const uint32_t base = smem_u32(smem + (size_t)s * kRgStage);
-        const uint64_t a = rg_desc(base), bh = rg_desc(base + kRgWBytes),
-                       bl = rg_desc(base + kRgWBytes + kRgXBytes);
+        const uint32_t acc = tmem + (uint32_t)(b * kRgN);
+        for (int c = 0; c < kchunks; ++c, ++it) {
+          const int s = it % kRgStages;
+          if (!mbar_wait(&full[s], (uint32_t)(it / kRgStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          rg_fence_after();
+          const uint32_t base = smem_u32(smem + (size_t)s * kRgStage);
+          const uint64_t a = rg_desc(base), bh = rg_desc(base + kRgWBytes),
+                         bl = rg_desc(base + kRgWBytes + kRgXBytes);
 #pragma unroll
-        for (int j = 0; j < kChunkK / 16; ++j) {  // K = 16 per MMA: +32 bytes = +2 in the descriptor
-          rg_mma(tmem, a + 2 * j, bh + 2 * j, (c | j) != 0);
-          rg_mma(tmem, a + 2 * j, bl + 2 * j, 1u);
+          for (int j = 0; j < kChunkK / 16; ++j) {  // K = 16 per MMA: +32 bytes = +2 in the descriptor
+            rg_mma(acc, a + 2 * j, bh + 2 * j, (c | j) != 0);
+            rg_mma(acc, a + 2 * j, bl + 2 * j, 1u);
+          }
+          rg_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
-        rg_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        if (ok) rg_commit(&afull[b]);  // the unit's accumulator is complete
       }
       if (!ok) atomicOr(err, 2u);
-      rg_commit(done);  // arrives when every MMA issued above has completed
+      rg_commit(done);
+      mbar_wait(done, 0);  // no MMA of this CTA still runs when TMEM is freed
     }
   } else {
     // Epilogue: warp w reads TMEM lanes 32 (w % 4) ..; lane = weight row, column = row of x.
     const int q = warp & 3;
-    const bool ok = mbar_wait(done, 0);
-    rg_fence_after();
-    if (ok) {
+    int i = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+      const int b = i & 1, tb = u % tblocks, tile = u / tblocks;
+      if (!mbar_wait(&afull[b], (uint32_t)(i >> 1) & 1u)) {
+        if (lane == 0) atomicOr(err, 4u);
+        break;
+      }
+      rg_fence_after();
       const int j = tile * kRgM + q * 32 + lane;
       for (int cc = 0; cc < kRgN / 32; ++cc) {
         uint32_t v[32];
-        const uint32_t addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32);
+        const uint32_t addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kRgN + cc * 32);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
             "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, "
@@ -218,15 +249,17 @@ __global__ void __launch_bounds__(kRgThreads, 1)
           }
         }
       }
-    } else if (lane == 0) {
-      atomicOr(err, 4u);
+      rg_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aempty[b]);  // the MMA thread may refill accumulator b
     }
   }
   rg_fence_before();
   __syncthreads();
   if (warp == 1) {
     rg_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kRgN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kRgN));
   }
 }
 
@@ -268,12 +301,19 @@ extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t 
   const int kchunks = (int)((k + kChunkK - 1) / kChunkK);
   const int tblocks = (int)((t + kRgN - 1) / kRgN);
   const int tiles = (int)((n + kRgM - 1) / kRgM);
-  const int64_t units = (int64_t)tblocks * kRgN * kchunks * 8;
-  const int sgrid = (int)((units + 255) / 256 < 4096 ? (units + 255) / 256 : 4096);
+  const int units = tiles * tblocks;
+  static int num_sms[64] = {};
+  if (!num_sms[dev] &&
+      cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return rg_fail(PP_E_CUDA, "cannot read the SM count");
+  const int grid = units < num_sms[dev] ? units : num_sms[dev];
+  const int64_t sunits = (int64_t)tblocks * kRgN * kchunks * 8;
+  const int sgrid = (int)((sunits + 255) / 256 < 4096 ? (sunits + 255) / 256 : 4096);
   pp_rows_split_kernel<<<sgrid, 256, 0, st>>>(x, (int32_t)k, (int32_t)t, (int32_t)k, kchunks,
                                               tblocks, (uint8_t*)work);
-  pp_rows_gemm_kernel<<<dim3(tblocks, tiles), kRgThreads, kRgSmem, st>>>(
-      w_tiled, (const uint8_t*)work, y, (int32_t)n, (int32_t)n, (int32_t)t, kchunks, err);
+  pp_rows_gemm_kernel<<<grid, kRgThreads, kRgSmem, st>>>(w_tiled, (const uint8_t*)work, y,
+                                                        (int32_t)n, (int32_t)n, (int32_t)t,
+                                                        kchunks, tblocks, units, err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     char msg[160];
