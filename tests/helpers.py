@@ -84,3 +84,16 @@ def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def tile_weights(w: np.ndarray) -> np.ndarray:
+    """W [n][k] BF16 bits in the shards' tiled layout: blocks of 128 rows x 64 columns, tile
+    major, the 16-byte unit u of row r of a block at u ^ (r % 8); padding zero."""
+    n, k = w.shape
+    kc, tiles = -(-k // 64), -(-n // 128)
+    out = np.zeros(tiles * kc * 128 * 64, np.uint16)
+    j = np.arange(n, dtype=np.int64)[:, None]
+    c = np.arange(k, dtype=np.int64)[None, :]
+    off = ((((j // 128) * kc + c // 64) * 128 + j % 128) * 64) + ((((c % 64) // 8) ^ (j % 8)) * 8) + c % 8
+    out[off] = w
+    return out

@@ -12,7 +12,7 @@ import pytest
 
 import oracle
 from helpers import load_fixture, rel_l2, tiny_weights
-from potpori_b200._lib import PP_E_INVALID, PP_E_NONFINITE, PPError
+from potpori_b200._lib import PP_E_INVALID, PP_E_NONFINITE, PP_E_UNSUPPORTED, PPError
 from potpori_b200.config import QWEN3_0_6B, QWEN3_4B, TINY
 from potpori_b200.shard import Shard
 
@@ -363,4 +363,9 @@ def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
     got = dec.decode_greedy(2053, toks[17], 6)
     want = lay.decode_greedy(2053, toks[17], 6)
     assert got == want
+    part = Shard.random(cfg, (0, 2), 64, 8, seed=seed)
+    with pytest.raises(PPError) as e:
+        part.set_decode_kernel(True)  # the kernel runs shards that hold every layer
+    assert e.value.status == PP_E_UNSUPPORTED
+    assert not part.decode_kernel()
     print(f"decode kernel: worst rel-L2 {worst:.2e} vs oracle, {worst_lay:.2e} vs layer kernels")

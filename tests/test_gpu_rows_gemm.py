@@ -12,9 +12,8 @@ import ctypes
 import numpy as np
 import pytest
 
-from helpers import f32_to_bf16_bits, rel_l2
+from helpers import f32_to_bf16_bits, rel_l2, tile_weights
 from potpori_b200 import _lib
-from test_zz_no_alloc import tile_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -27,7 +26,7 @@ def _run(L, torch, w_bits, x, reps=1):
     n, k = w_bits.shape
     t = x.shape[0]
     dev = torch.device("cuda", 0)
-    w_t = torch.from_numpy(tile_bf16(w_bits).view(np.int16)).to(dev)
+    w_t = torch.from_numpy(tile_weights(w_bits).view(np.int16)).to(dev)
     x_t = torch.from_numpy(x).to(dev)
     y_t = torch.full((t, n), float("nan"), dtype=torch.float32, device=dev)
     wb = int(L.pp_rows_gemm_work_bytes(t, k))
