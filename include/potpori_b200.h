@@ -189,6 +189,17 @@ pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
 pp_status pp_shard_set_sm_limit(pp_shard* shard, uint32_t ctas);
 uint32_t pp_shard_sm_limit(const pp_shard* shard);
 
+/* Prompt prefill of a shard that holds every layer: positions pos .. pos + t - 1 (t <= 2048)
+ * of the prompt `tokens` go through all layers at once and their K/V rows are written into
+ * the cache, as the reference's prefill does in chunk-sized verify steps
+ * (src/qwen/target.rs:62-84). The projections run on the tensor cores (pp_rows_gemm), the
+ * attention as the split kernel over 16-row sub-chunks. It produces no logits: the caller
+ * runs the last prompt token as a 1-row step (pp_shard_forward_tokens) for its greedy pick.
+ * Allocates its row buffers (about 0.2 GB for Qwen3-0.6B, 0.5 GB for 4B) on first use.
+ * PP_E_UNSUPPORTED for a shard without every layer or with more than 4 query heads per KV
+ * head. Synchronous. */
+pp_status pp_shard_prefill(pp_shard* shard, uint32_t pos, const int32_t* tokens, uint32_t t);
+
 /* Run every 1-row step of a shard that holds all layers (a draft model's greedy decode, the
  * single-token verify steps) as one persistent cooperative kernel over the shard's SM budget
  * followed by the vocabulary head, instead of six kernels per layer (enabled = 1; 0 returns

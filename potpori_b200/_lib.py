@@ -31,7 +31,7 @@ EXPORTS = [
     "pp_shard_model_layers", "pp_shard_device_bytes", "pp_shard_last_launches",
     "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
     "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
-    "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
+    "pp_shard_prefill", "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
     "pp_rows_gemm_work_bytes", "pp_rows_gemm", "pp_norm_gemv_static", "pp_last_error", "pp_version",
 ]
 
@@ -122,6 +122,7 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_pdl": (I32, [P, I32]),
         "pp_shard_set_sm_limit": (I32, [P, U32]),
         "pp_shard_sm_limit": (U32, [P]),
+        "pp_shard_prefill": (I32, [P, U32, pI32, U32]),
         "pp_shard_set_decode_kernel": (I32, [P, I32]),
         "pp_shard_decode_kernel": (I32, [P]),
         "pp_shard_decode_greedy": (I32, [P, U32, I32, U32, pI32]),

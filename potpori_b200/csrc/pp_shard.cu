@@ -31,6 +31,7 @@
 #include "pp_decode.cuh"
 #include "pp_gemv.cuh"
 #include "pp_misc.cuh"
+#include "pp_prefill_rows.cuh"
 
 using namespace pp;
 
@@ -169,6 +170,17 @@ struct pp_shard {
   float *dec_qkv = nullptr, *dec_attn = nullptr, *dec_act = nullptr, *dec_part = nullptr;
   uint32_t* dec_sync = nullptr;
   int dec_ns = 0, dec_vec = 0;
+  // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the tcgen05
+  // projection's work area, its error word, one step header per 16-row attention sub-chunk.
+  struct {
+    float *x = nullptr, *xn = nullptr, *tmp = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr,
+          *gu = nullptr, *act = nullptr;
+    void* work = nullptr;
+    uint64_t work_bytes = 0;
+    uint32_t* err = nullptr;
+    StepDesc* descs = nullptr;
+    int32_t* tokens = nullptr;
+  } pf;
   uint32_t launches = 0;                 // kernels of the step being enqueued
   std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
   std::vector<int>* prof_kinds = nullptr;
@@ -615,6 +627,111 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   }
   if ((r = after_launch(s, st, PP_K_DECODE))) return r;
   return launch_head<1>(s, st);
+}
+
+
+// ---- prompt prefill ------------------------------------------------------------------------
+constexpr int kPrefillMax = 2048;  // rows of one pp_shard_prefill call
+
+pp_status prefill_alloc(pp_shard* s) {
+  if (s->pf.x) return PP_OK;
+  pp_status r;
+  const size_t T = kPrefillMax;
+  if ((r = dalloc(s, &s->pf.x, T * s->H * 4))) return r;
+  if ((r = dalloc(s, &s->pf.xn, T * s->H * 4))) return r;
+  if ((r = dalloc(s, &s->pf.tmp, T * s->H * 4))) return r;
+  if ((r = dalloc(s, &s->pf.qkv, T * (s->Q + 2 * s->KV) * 4))) return r;
+  if ((r = dalloc(s, &s->pf.q, T * s->Q * 4))) return r;
+  if ((r = dalloc(s, &s->pf.att, T * s->Q * 4))) return r;
+  if ((r = dalloc(s, &s->pf.gu, T * s->gu_rows * 4))) return r;
+  if ((r = dalloc(s, &s->pf.act, T * s->I * 4))) return r;
+  uint64_t wb = pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->H);
+  const uint64_t cand[2] = {pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->Q),
+                            pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->I)};
+  for (uint64_t c : cand) wb = c > wb ? c : wb;
+  uint8_t* w = nullptr;
+  if ((r = dalloc(s, &w, wb + 1024))) return r;
+  s->pf.work = (void*)(((uintptr_t)w + 1023) & ~(uintptr_t)1023);
+  s->pf.work_bytes = wb;
+  if ((r = dalloc(s, &s->pf.err, 16))) return r;
+  if ((r = dalloc(s, &s->pf.descs, (T / 16) * sizeof(StepDesc)))) return r;
+  if ((r = dalloc(s, &s->pf.tokens, T * 4))) return r;
+  return PP_OK;
+}
+
+// y[t][n] = x[t][k] . W^T on the tensor cores into the shard's prefill buffers.
+pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, const float* x, int t, float* y) {
+  const pp_status st = pp_rows_gemm(w, (uint32_t)n, (uint32_t)k, x, (uint32_t)t, y, s->pf.work,
+                                    s->pf.work_bytes, s->pf.err, s->stream);
+  if (st) {
+    char msg[256];
+    pp_last_error(nullptr, msg, sizeof msg);
+    return fail(s, st, "prompt projection: %s", msg);
+  }
+  return PP_OK;
+}
+
+// Every layer of a whole-model shard over t prompt rows at positions pos.. (embedding, and per
+// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, split attention per
+// 16-row sub-chunk, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
+// residual; the last layer stops after its K/V rows, which is all a prefill leaves behind).
+pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
+  cudaStream_t st = s->stream;
+  const int H = s->H, Q = s->Q, KV = s->KV, I = s->I, hd = s->hd;
+  const float eps = s->d.cfg.rms_norm_eps;
+  pp_status r;
+  CK(cudaMemsetAsync(s->pf.err, 0, 4, st));
+  CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
+  pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
+  CK(cudaGetLastError());
+  const int qpw = (s->G * 16 + 7) / 8;
+  const size_t asmem = attn_smem_bytes(hd, qpw);
+  const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
+  for (int l = 0; l < s->nl; ++l) {
+    LayerDev& Ld = s->L[l];
+    pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, s->pf.xn);
+    CK(cudaGetLastError());
+    if ((r = prefill_gemm(s, Ld.wqkv, Q + 2 * KV, H, s->pf.xn, t, s->pf.qkv))) return r;
+    pre_qkv_kernel<<<dim3(t, s->nh + 2 * s->nkv), qthreads, 0, st>>>(
+        s->pf.qkv, t, (int32_t)pos, s->nh, s->nkv, hd, eps, Ld.norm[N_QN], Ld.norm[N_KN], s->rope,
+        Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
+    CK(cudaGetLastError());
+    if (l + 1 == s->nl) break;
+    for (int i = 0; i * 16 < t; ++i) {
+      AttnArgs at = {};
+      at.q = s->pf.q + (size_t)i * 16 * Q;
+      at.kcache = Ld.kc;
+      at.vcache = Ld.vc;
+      at.part = s->apart;
+      at.n_heads = s->nh;
+      at.n_kv = s->nkv;
+      at.head_dim = hd;
+      at.capacity = (int32_t)s->d.capacity;
+      at.splits = s->splits;
+      at.q_dim = Q;
+      at.nq_max = s->nq_max;
+      at.scale = sqrtf((float)hd);
+      at.desc = s->pf.descs + i;
+      at.res = s->d_res;
+      const dim3 grid(s->nkv, s->splits), block(kAttnThreads);
+      if (qpw <= 2) attn_split_kernel<16, 2><<<grid, block, asmem, st>>>(at);
+      else if (qpw <= 4) attn_split_kernel<16, 4><<<grid, block, asmem, st>>>(at);
+      else attn_split_kernel<16, 8><<<grid, block, asmem, st>>>(at);
+      CK(cudaGetLastError());
+      pre_attn_combine_kernel<<<dim3(s->nh, 16), hd < 32 ? 32 : hd, 0, st>>>(
+          at, s->pf.att + (size_t)i * 16 * Q, Q);
+      CK(cudaGetLastError());
+    }
+    if ((r = prefill_gemm(s, Ld.wo, H, Q, s->pf.att, t, s->pf.tmp))) return r;
+    pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
+    pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, s->pf.xn);
+    if ((r = prefill_gemm(s, Ld.wgu, (int)s->gu_rows, H, s->pf.xn, t, s->pf.gu))) return r;
+    pre_swiglu_kernel<<<1024, 256, 0, st>>>(s->pf.gu, (int32_t)s->gu_rows, I, (int64_t)t, s->pf.act);
+    if ((r = prefill_gemm(s, Ld.wd, H, I, s->pf.act, t, s->pf.tmp))) return r;
+    pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
+    CK(cudaGetLastError());
+  }
+  return PP_OK;
 }
 
 template <typename K>
@@ -1320,6 +1437,43 @@ pp_status pp_shard_forward_tokens(pp_shard* s, uint32_t pos, const int32_t* toke
   for (uint32_t i = 1; i < m; ++i) d.drafts[i - 1] = tokens[i];
   if ((r = upload_desc(s, slot, s->stream))) return r;
   return finish_host_step(s, m, out_hidden, verify);
+}
+
+pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uint32_t t) {
+  if (!s || !tokens) return fail(s, PP_E_INVALID, "null argument");
+  if (!(s->first && s->last))
+    return fail(s, PP_E_UNSUPPORTED, "the prompt prefill runs shards that hold every layer");
+  if (s->G > 4) return fail(s, PP_E_UNSUPPORTED, "the prompt prefill needs at most 4 query heads per KV head");
+  if (t == 0 || t > (uint32_t)kPrefillMax) return fail(s, PP_E_INVALID, "t must be 1..2048 rows");
+  if ((uint64_t)pos + t > s->d.capacity) return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
+  for (uint32_t i = 0; i < t; ++i)  // src/qwen/model.rs:383-389
+    if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
+      return fail(s, PP_E_INVALID, "invalid token input");
+  if (pp_shard_missing(s, nullptr, 0))
+    return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
+  CK(cudaSetDevice(s->dev));
+  pp_status r = prefill_alloc(s);
+  if (r) return r;
+  std::vector<StepDesc> descs((t + 15) / 16);
+  for (size_t i = 0; i < descs.size(); ++i) {
+    StepDesc d = {};
+    d.pos = (int32_t)(pos + 16 * i);
+    d.m = (int32_t)(t - 16 * i < 16 ? t - 16 * i : 16);
+    descs[i] = d;
+  }
+  CK(cudaMemcpyAsync(s->pf.descs, descs.data(), descs.size() * sizeof(StepDesc),
+                     cudaMemcpyHostToDevice, s->stream));
+  CK(cudaMemcpyAsync(s->pf.tokens, tokens, (size_t)t * 4, cudaMemcpyHostToDevice, s->stream));
+  if ((r = enqueue_prefill(s, pos, (int)t))) {
+    cudaStreamSynchronize(s->stream);
+    return r;
+  }
+  uint32_t err = 0;
+  CK(cudaMemcpyAsync(&err, s->pf.err, 4, cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(s->h_res, s->d_res, sizeof(StepResult), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  if (err) return fail(s, PP_E_TIMEOUT, "a bounded wait of the prompt projection expired");
+  return status_of(s, *s->h_res);
 }
 
 pp_status pp_shard_decode_greedy(pp_shard* s, uint32_t pos, int32_t token, uint32_t n,

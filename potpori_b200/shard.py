@@ -208,6 +208,21 @@ class Shard:
     def sm_limit(self) -> int:
         return int(self._L.pp_shard_sm_limit(self._h))
 
+    PREFILL_MAX = 2048
+
+    def can_prefill(self) -> bool:
+        """Whether prefill() runs here: a shard with every layer, <= 4 query heads per KV head."""
+        cfg = self.cfg
+        return self.first and self.last and cfg.n_heads // cfg.n_kv_heads <= 4
+
+    def prefill(self, pos: int, tokens: Sequence[int]) -> None:
+        """Write the K/V rows of prompt tokens at pos.. through every layer at once (tensor-core
+        projections), in pieces of up to 2048 rows; no logits."""
+        for i in range(0, len(tokens), self.PREFILL_MAX):
+            piece = np.asarray(tokens[i:i + self.PREFILL_MAX], np.int32)
+            check(self._L.pp_shard_prefill(self._h, pos + i, piece.ctypes.data_as(
+                ctypes.POINTER(ctypes.c_int32)), len(piece)), self._h, f"prefill(pos={pos + i})")
+
     def set_decode_kernel(self, enabled: bool = True) -> None:
         """Run 1-row steps of this whole-model shard as one persistent kernel (plus the vocab
         head) instead of six kernels per layer; keeps a row-major copy of the layer weights."""

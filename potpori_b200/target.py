@@ -48,6 +48,14 @@ class QwenTarget:
         return r.argmax
 
     def prefill(self, prompt: List[int]) -> int:
+        """The greedy pick after the prompt. The reference feeds the prompt in chunk-sized
+        verify steps (target.rs:62-84); a shard that can (Shard.can_prefill) writes the K/V
+        rows of all but the last token in one pass per 2048 rows on the tensor cores instead,
+        and the last token runs as the 1-row step that yields the pick, the same result to
+        the rounding of F32 arithmetic."""
+        if len(prompt) > 1 and self.shard.can_prefill():
+            self.shard.prefill(0, prompt[:-1])
+            return self._pick(len(prompt) - 1, prompt[-1:])[0]
         chunk = self.shard.chunk_size() or len(prompt)
         pos, last = 0, 0
         while pos < len(prompt):
@@ -84,6 +92,13 @@ class IncrementalDraft:
         return self.model.capacity()
 
     def _feed_range(self, ctx: List[int], start: int, end: int) -> int:
+        if end - start > self.chunk and self.model.shard.can_prefill():
+            # A long catch-up (the prompt): one prefill pass, then the last token's 1-row step.
+            self.model.shard.prefill(start, ctx[start:end - 1])
+            self.steps += 1
+            last = self.model.verify(end - 1, ctx[end - 1], [])[-1]
+            self.steps += 1
+            return last
         pos, last = start, 0
         while pos < end:
             take = self.chunk if self.chunk > 1 and end - pos >= self.chunk else 1

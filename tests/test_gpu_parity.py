@@ -369,3 +369,50 @@ def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
     assert e.value.status == PP_E_UNSUPPORTED
     assert not part.decode_kernel()
     print(f"decode kernel: worst rel-L2 {worst:.2e} vs oracle, {worst_lay:.2e} vs layer kernels")
+
+
+def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
+    """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections, split
+    attention per 16-row sub-chunk) leaves the K/V rows of the reference's chunked prefill
+    (src/qwen/target.rs:62-84): after it, the next steps give the logits of the chunked verify
+    path (rel-L2 <= 2e-4) and of the oracle (rel-L2 <= 1e-3, same pick unless the top-2 gap is
+    below 1e-3). Config 0 (Qwen3-0.6B seed 0, 41-token prompt from position 0) and a 2-layer
+    model of Qwen3-4B geometry (G = 4) over 173 tokens from position 5 (ragged sub-chunks)."""
+    from potpori_b200.config import QwenConfig
+
+    cases = [(QWEN3_0_6B, 0, 0, 41),
+             (QwenConfig(2, 2560, 9728, 128, 32, 8, 151936, 1e-6, 1e6), 4, 5, 173)]
+    for cfg, seed, pos0, n in cases:
+        cap = 256
+        rng = np.random.default_rng(seed + 100)
+        prompt = rng.integers(0, cfg.vocab_size, pos0 + n).tolist()
+        pre = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+        chk = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+        ref = _oracle_whole(cfg, seed, cap, 8)
+        assert pre.can_prefill()
+        end = pos0 + n - 1  # every prompt token but the last
+        # The first pos0 positions go the chunked way on every side, then the prefill.
+        pos = 0
+        while pos < end:
+            take = 8 if end - pos >= 8 else 1
+            if pos < pos0:
+                take = 8 if pos0 - pos >= 8 else 1
+                pre.forward_tokens(pos, prompt[pos:pos + take])
+            chk.forward_tokens(pos, prompt[pos:pos + take])
+            ref.forward(pos, tokens=prompt[pos:pos + take])
+            pos += take
+        pre.prefill(pos0, prompt[pos0:end])
+        cur = prompt[end]
+        for step in range(2):
+            got = pre.forward_tokens(end + step, [cur])[0]
+            other = chk.forward_tokens(end + step, [cur])[0]
+            want = ref.forward(end + step, tokens=[cur])[0]
+            _step_logits_agree(got, want, 0.0, f"{cfg.layers}-layer model, step {step}")
+            e = rel_l2(got, other)
+            assert e <= 2e-4, f"{cfg.layers}-layer model, step {step}: {e:.2e} against the chunked path"
+            cur = int(np.argmax(want))
+    part = Shard.random(QWEN3_0_6B, (0, 2), 64, 8, seed=0)
+    assert not part.can_prefill()
+    with pytest.raises(PPError) as e:
+        part.prefill(0, [1, 2, 3])
+    assert e.value.status == PP_E_UNSUPPORTED
