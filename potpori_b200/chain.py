@@ -60,6 +60,16 @@ class LocalChain:
         return r.argmax
 
     def prefill(self, prompt: List[int]) -> int:
+        """The greedy pick after the prompt. The reference streams the prompt through the
+        chain in chunk-sized steps (src/node.rs:538-566); a one-shard chain whose shard can
+        (Shard.can_prefill) writes the K/V rows of all but the last token in one pass instead
+        and submits the last token as the step that yields the pick."""
+        if len(self.stages) == 1 and len(prompt) > 1 and self.stages[0].can_prefill():
+            while self.inflight:
+                self.poll()
+            self.stages[0].prefill(0, prompt[:-1])
+            self.submit(len(prompt) - 1, prompt[-1], [])
+            return self.poll()[-1]
         pos = 0
         while pos < len(prompt):
             take = self.chunk if len(prompt) - pos >= self.chunk else 1
