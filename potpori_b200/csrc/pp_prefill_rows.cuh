@@ -100,24 +100,47 @@ __global__ void pre_swiglu_kernel(const float* gu, int32_t gu_rows, int32_t I, i
   }
 }
 
-// Merge of the attention splits of one (query head hq, chunk row r) into F32 rows
-// out[r][hq * hd + d] (the combine of attn_combine_kernel with a row-major F32 output for the
-// projection that follows). Grid (n_heads, 16), block max(32, hd).
-__global__ void pre_attn_combine_kernel(const AttnArgs a, float* out, int32_t ldo) {
-  constexpr int MT = 16;
-  if (bad_step(a.desc, a.capacity, MT)) return;
-  const int hq = blockIdx.x, r = blockIdx.y;
-  if (r >= a.desc->m) return;
-  __shared__ float sm_m[256], sm_w[256];
+// Attention of every 16-row sub-chunk of a prompt chunk in one launch: grid
+// (n_kv, splits, chunks); CTA (KV head h, split s, sub-chunk z) runs the split kernel's unit
+// with the sub-chunk's step header descs[z], its query rows q + 16 z rows and its partials at
+// part + z part_stride ([n_kv][splits][nq_max][4 + hd] per sub-chunk). A split past the keys of
+// its sub-chunk writes an empty partial (max -inf, sum 0). The last sub-chunks see the most
+// keys, so they take the lowest block indices and start first.
+template <int NT>
+__global__ void __launch_bounds__(kAttnThreads) pre_attn_kernel(const AttnArgs a,
+                                                                const StepDesc* descs,
+                                                                size_t part_stride) {
+  extern __shared__ uint8_t attn_smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
+  const AttnSmem L(a.head_dim, NT, kAttnStages);
+  AttnArgs az = a;
+  const int z = gridDim.z - 1 - blockIdx.z;
+  az.desc = descs + z;
+  az.q = a.q + (size_t)z * 16 * a.q_dim;
+  az.part = a.part + (size_t)z * part_stride;
+  if (bad_step(az.desc, az.capacity, 16)) return;
+  if (threadIdx.x == 0) attn_init_barriers(L, sm);
+  consumer_sync();  // barrier init visible to every thread
+  uint32_t uses = 0;
+  attn_unit<16, NT>(az, blockIdx.x, blockIdx.y, L, sm, uses);
+}
+
+// Merge of the splits of (query head hq, row r) of sub-chunk z into F32 rows
+// out[16 z + r][hq * hd + d] (the combine of attn_combine_kernel with a row-major F32 output
+// for the projection that follows). Grid (n_heads, 16, chunks), block max(32, hd).
+__global__ void pre_attn_combine_kernel(const AttnArgs a, const StepDesc* descs,
+                                        size_t part_stride, float* out, int32_t ldo) {
+  const int hq = blockIdx.x, r = blockIdx.y, z = blockIdx.z;
+  if (bad_step(descs + z, a.capacity, 16) || r >= descs[z].m) return;
+  __shared__ float sm_m[64], sm_w[64];
   __shared__ float red_l;
   const int G = a.n_heads / a.n_kv;
   const int h = hq / G, g = hq - h * G;
-  const int qi = g * MT + r;
-  const int hd = a.head_dim, t = threadIdx.x, nthr = blockDim.x;
+  const int hd = a.head_dim, t = threadIdx.x, S = a.splits;
   const size_t stride = (size_t)a.nq_max * (hd + 4);
-  const float* base = a.part + ((size_t)h * a.splits * a.nq_max + qi) * (hd + 4);
-  const int S = a.splits;
-  for (int s = t; s < S; s += nthr) {
+  const float* base = a.part + (size_t)z * part_stride +
+                      ((size_t)h * S * a.nq_max + (size_t)(g * 16 + r)) * (hd + 4);
+  for (int s = t; s < S; s += blockDim.x) {
     const float2 ml = __ldcg((const float2*)(base + s * stride));
     sm_m[s] = ml.x;
     sm_w[s] = ml.y;
@@ -138,7 +161,7 @@ __global__ void pre_attn_combine_kernel(const AttnArgs a, float* out, int32_t ld
   if (t < hd) {
     float o = 0.f;
     for (int s = 0; s < S; ++s) o += __ldcg(base + s * stride + 4 + t) * sm_w[s];
-    out[(size_t)r * ldo + hq * hd + t] = o / red_l;
+    out[(size_t)(16 * z + r) * ldo + hq * hd + t] = o / red_l;
   }
 }
 

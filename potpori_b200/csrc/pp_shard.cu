@@ -9,6 +9,7 @@
 // header, so it is captured once per chunk width into a CUDA graph and replayed; kernels are
 // chained with programmatic dependent launch so each GEMV streams its weights while the
 // previous kernel drains.
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <fcntl.h>
@@ -180,6 +181,8 @@ struct pp_shard {
     uint32_t* err = nullptr;
     StepDesc* descs = nullptr;
     int32_t* tokens = nullptr;
+    float* part = nullptr;  // attention partials of every sub-chunk
+    size_t part_stride = 0;  // floats per sub-chunk: n_kv * kPrefillSplits * 16 G * (hd + 4)
   } pf;
   uint32_t launches = 0;                 // kernels of the step being enqueued
   std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
@@ -632,6 +635,7 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
 
 // ---- prompt prefill ------------------------------------------------------------------------
 constexpr int kPrefillMax = 2048;  // rows of one pp_shard_prefill call
+constexpr int kPrefillSplits = 4;  // most key splits of one sub-chunk's attention
 
 pp_status prefill_alloc(pp_shard* s) {
   if (s->pf.x) return PP_OK;
@@ -656,6 +660,8 @@ pp_status prefill_alloc(pp_shard* s) {
   if ((r = dalloc(s, &s->pf.err, 16))) return r;
   if ((r = dalloc(s, &s->pf.descs, (T / 16) * sizeof(StepDesc)))) return r;
   if ((r = dalloc(s, &s->pf.tokens, T * 4))) return r;
+  s->pf.part_stride = (size_t)s->nkv * kPrefillSplits * (16 * s->G) * (s->hd + 4);
+  if ((r = dalloc(s, &s->pf.part, (T / 16) * s->pf.part_stride * 4))) return r;
   return PP_OK;
 }
 
@@ -672,8 +678,8 @@ pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, const float
 }
 
 // Every layer of a whole-model shard over t prompt rows at positions pos.. (embedding, and per
-// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, split attention per
-// 16-row sub-chunk, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
+// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, causal attention of
+// every 16-row sub-chunk in one launch plus one combine, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
 // residual; the last layer stops after its K/V rows, which is all a prefill leaves behind).
 pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   cudaStream_t st = s->stream;
@@ -687,6 +693,9 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   const int qpw = (s->G * 16 + 7) / 8;
   const size_t asmem = attn_smem_bytes(hd, qpw);
   const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
+  // Key splits per sub-chunk: enough that no CTA walks more than 64 key tiles (2048 keys).
+  const int nsub = (t + 15) / 16, ntiles = (int)((pos + t + kAttnTile - 1) / kAttnTile);
+  const int splits = std::min(kPrefillSplits, std::max(1, (ntiles + 63) / 64));
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
     pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, s->pf.xn);
@@ -697,29 +706,28 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
     if (l + 1 == s->nl) break;
-    for (int i = 0; i * 16 < t; ++i) {
+    {
       AttnArgs at = {};
-      at.q = s->pf.q + (size_t)i * 16 * Q;
+      at.q = s->pf.q;
       at.kcache = Ld.kc;
       at.vcache = Ld.vc;
-      at.part = s->apart;
+      at.part = s->pf.part;
       at.n_heads = s->nh;
       at.n_kv = s->nkv;
       at.head_dim = hd;
       at.capacity = (int32_t)s->d.capacity;
-      at.splits = s->splits;
+      at.splits = splits;
       at.q_dim = Q;
-      at.nq_max = s->nq_max;
+      at.nq_max = 16 * s->G;
       at.scale = sqrtf((float)hd);
-      at.desc = s->pf.descs + i;
       at.res = s->d_res;
-      const dim3 grid(s->nkv, s->splits), block(kAttnThreads);
-      if (qpw <= 2) attn_split_kernel<16, 2><<<grid, block, asmem, st>>>(at);
-      else if (qpw <= 4) attn_split_kernel<16, 4><<<grid, block, asmem, st>>>(at);
-      else attn_split_kernel<16, 8><<<grid, block, asmem, st>>>(at);
+      const dim3 grid(s->nkv, splits, nsub), block(kAttnThreads);
+      if (qpw <= 2) pre_attn_kernel<2><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
+      else if (qpw <= 4) pre_attn_kernel<4><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
+      else pre_attn_kernel<8><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
       CK(cudaGetLastError());
-      pre_attn_combine_kernel<<<dim3(s->nh, 16), hd < 32 ? 32 : hd, 0, st>>>(
-          at, s->pf.att + (size_t)i * 16 * Q, Q);
+      pre_attn_combine_kernel<<<dim3(s->nh, 16, nsub), hd < 32 ? 32 : hd, 0, st>>>(
+          at, s->pf.descs, s->pf.part_stride, s->pf.att, Q);
       CK(cudaGetLastError());
     }
     if ((r = prefill_gemm(s, Ld.wo, H, Q, s->pf.att, t, s->pf.tmp))) return r;
@@ -762,7 +770,9 @@ pp_status set_attrs(pp_shard* s) {
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
       (r = set_max_smem(s, decode_step_kernel<1>)) || (r = set_max_smem(s, decode_step_kernel<2>)) ||
-      (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)))
+      (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)) ||
+      (r = set_max_smem(s, pre_attn_kernel<2>)) || (r = set_max_smem(s, pre_attn_kernel<4>)) ||
+      (r = set_max_smem(s, pre_attn_kernel<8>)))
     return r;
   return PP_OK;
 }

@@ -372,8 +372,8 @@ def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
 
 
 def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
-    """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections, split
-    attention per 16-row sub-chunk) leaves the K/V rows of the reference's chunked prefill
+    """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections, the
+    attention of every 16-row sub-chunk in one launch) leaves the K/V rows of the reference's chunked prefill
     (src/qwen/target.rs:62-84): after it, the next steps give the logits of the chunked verify
     path (rel-L2 <= 2e-4) and of the oracle (rel-L2 <= 1e-3, same pick unless the top-2 gap is
     below 1e-3). Config 0 (Qwen3-0.6B seed 0, 41-token prompt from position 0) and a 2-layer
@@ -416,3 +416,38 @@ def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
     with pytest.raises(PPError) as e:
         part.prefill(0, [1, 2, 3])
     assert e.value.status == PP_E_UNSUPPORTED
+
+
+@pytest.mark.gpu
+def test_prefill_past_2048_keys_matches_the_chunked_path(gpu):
+    """Two prefill calls over a 2199-token prompt (2048 rows from position 0, then 151 rows
+    from position 2048, whose sub-chunks see more than 2048 keys and take two key splits)
+    leave the K/V rows of the chunked verify path: the next two steps agree within
+    rel-L2 2e-4 and pick the same token unless its top-2 gap is below 1e-3. A 2-layer model of Qwen3-0.6B geometry."""
+    from potpori_b200.config import QwenConfig
+
+    cfg = QwenConfig(2, 1024, 3072, 128, 16, 8, 151936, 1e-6, 1e6)
+    cap, n = 2304, 2200
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, n).tolist()
+    pre = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=1)
+    chk = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=1)
+    end = n - 1
+    pre.prefill(0, prompt[:2048])
+    pre.prefill(2048, prompt[2048:end])
+    pos = 0
+    while pos < end:
+        take = 8 if end - pos >= 8 else 1
+        chk.forward_tokens(pos, prompt[pos:pos + take])
+        pos += take
+    cur = prompt[end]
+    for step in range(2):
+        got = pre.forward_tokens(end + step, [cur])[0]
+        other = chk.forward_tokens(end + step, [cur])[0]
+        e = rel_l2(got, other)
+        assert e <= 2e-4, f"step {step}: {e:.2e} against the chunked path"
+        top2 = np.sort(other)[-2:]
+        if top2[1] - top2[0] > 1e-3 * abs(top2[1]):
+            assert int(np.argmax(got)) == int(np.argmax(other))
+        cur = int(np.argmax(other))
+    pre.close()
+    chk.close()
