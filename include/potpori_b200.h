@@ -193,11 +193,11 @@ uint32_t pp_shard_sm_limit(const pp_shard* shard);
  * of the prompt `tokens` go through all layers at once and their K/V rows are written into
  * the cache, as the reference's prefill does in chunk-sized verify steps
  * (src/qwen/target.rs:62-84). The projections run on the tensor cores (pp_rows_gemm), the
- * attention as the split kernel over 16-row sub-chunks. It produces no logits: the caller
+ * causal attention flash-style over the whole chunk. It produces no logits: the caller
  * runs the last prompt token as a 1-row step (pp_shard_forward_tokens) for its greedy pick.
  * Allocates its row buffers (about 0.2 GB for Qwen3-0.6B, 0.5 GB for 4B) on first use.
- * PP_E_UNSUPPORTED for a shard without every layer or with more than 4 query heads per KV
- * head. Synchronous. */
+ * PP_E_UNSUPPORTED for a shard without every layer, with a head size other than 128 or with
+ * other than 1, 2, 4 or 8 query heads per KV head. Synchronous. */
 pp_status pp_shard_prefill(pp_shard* shard, uint32_t pos, const int32_t* tokens, uint32_t t);
 
 /* Run every 1-row step of a shard that holds all layers (a draft model's greedy decode, the

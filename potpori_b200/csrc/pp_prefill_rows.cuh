@@ -100,68 +100,231 @@ __global__ void pre_swiglu_kernel(const float* gu, int32_t gu_rows, int32_t I, i
   }
 }
 
-// Attention of every 16-row sub-chunk of a prompt chunk in one launch: grid
-// (n_kv, splits, chunks); CTA (KV head h, split s, sub-chunk z) runs the split kernel's unit
-// with the sub-chunk's step header descs[z], its query rows q + 16 z rows and its partials at
-// part + z part_stride ([n_kv][splits][nq_max][4 + hd] per sub-chunk). A split past the keys of
-// its sub-chunk writes an empty partial (max -inf, sum 0). The last sub-chunks see the most
-// keys, so they take the lowest block indices and start first.
-template <int NT>
-__global__ void __launch_bounds__(kAttnThreads) pre_attn_kernel(const AttnArgs a,
-                                                                const StepDesc* descs,
-                                                                size_t part_stride) {
-  extern __shared__ uint8_t attn_smem_raw[];
-  uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
-  const AttnSmem L(a.head_dim, NT, kAttnStages);
-  AttnArgs az = a;
-  const int z = gridDim.z - 1 - blockIdx.z;
-  az.desc = descs + z;
-  az.q = a.q + (size_t)z * 16 * a.q_dim;
-  az.part = a.part + (size_t)z * part_stride;
-  if (bad_step(az.desc, az.capacity, 16)) return;
-  if (threadIdx.x == 0) attn_init_barriers(L, sm);
-  consumer_sync();  // barrier init visible to every thread
-  uint32_t uses = 0;
-  attn_unit<16, NT>(az, blockIdx.x, blockIdx.y, L, sm, uses);
+// ---- causal attention of a prompt chunk ---------------------------------------------------
+// Flash-style: one CTA per (KV head h, block of BQ = 128 / G prompt rows), 8 warps, warp w the
+// 16 rows r0..r0+15 of query head h G + g. The query fragments stay in registers, the 32-key
+// K/V tiles of the cache stream through a ring of bulk copies, and per tile a warp computes
+// S = Q K^T (16 x 32) on the tensor cores, the online softmax of its rows in registers
+// (running max, rescale, running sum), and O += P V with P taken straight from the S
+// accumulators. Every F32 operand is carried as hi + lo BF16 with the three products
+// hi.hi + hi.lo + lo.hi, as in the verify pass's attention; scores are divided by
+// sqrt(head_dim) and row r sees keys 0..pos + r (tiny.rs:77-101). The normalised rows go to
+// out[r][(h G + g) 128 + d] (F32, the O projection's input). Head size 128; G = 1, 2, 4 or 8;
+// grid (n_kv, ceil(t / BQ)), 256 threads, flash_smem_bytes() of dynamic shared memory.
+constexpr int kFlashHd = 128;
+constexpr int kFlashRowB = 4 * kFlashHd;  // a cache row: hi and lo parts of 128 dims
+constexpr int kFlashStages = 3;
+constexpr int kFlashTileB = kAttnTile * kFlashRowB;  // one K (or V) tile
+__host__ __device__ constexpr size_t flash_smem_bytes() {
+  return (size_t)kFlashStages * 2 * kFlashTileB + 128 * (size_t)kFlashRowB + 8 * kFlashStages + 128;
 }
 
-// Merge of the splits of (query head hq, row r) of sub-chunk z into F32 rows
-// out[16 z + r][hq * hd + d] (the combine of attn_combine_kernel with a row-major F32 output
-// for the projection that follows). Grid (n_heads, 16, chunks), block max(32, hd).
-__global__ void pre_attn_combine_kernel(const AttnArgs a, const StepDesc* descs,
-                                        size_t part_stride, float* out, int32_t ldo) {
-  const int hq = blockIdx.x, r = blockIdx.y, z = blockIdx.z;
-  if (bad_step(descs + z, a.capacity, 16) || r >= descs[z].m) return;
-  __shared__ float sm_m[64], sm_w[64];
-  __shared__ float red_l;
-  const int G = a.n_heads / a.n_kv;
-  const int h = hq / G, g = hq - h * G;
-  const int hd = a.head_dim, t = threadIdx.x, S = a.splits;
-  const size_t stride = (size_t)a.nq_max * (hd + 4);
-  const float* base = a.part + (size_t)z * part_stride +
-                      ((size_t)h * S * a.nq_max + (size_t)(g * 16 + r)) * (hd + 4);
-  for (int s = t; s < S; s += blockDim.x) {
-    const float2 ml = __ldcg((const float2*)(base + s * stride));
-    sm_m[s] = ml.x;
-    sm_w[s] = ml.y;
+__device__ __forceinline__ uint32_t pack_bf16x2(uint16_t lo_half, uint16_t hi_half) {
+  return (uint32_t)lo_half | ((uint32_t)hi_half << 16);
+}
+// (a, b) as the hi and lo BF16x2 words of an MMA fragment register (a in the low half).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  uint16_t ah, al, bh, bl;
+  split_bf16(a, ah, al);
+  split_bf16(b, bh, bl);
+  hi = pack_bf16x2(ah, bh);
+  lo = pack_bf16x2(al, bl);
+}
+
+__global__ void __launch_bounds__(256, 1)
+    pre_flash_kernel(const float* q, const uint8_t* kc, const uint8_t* vc, int32_t capacity,
+                     int32_t nh, int32_t nkv, int32_t pos, int32_t t, float scale,
+                     float* out, StepResult* res) {
+  constexpr int HD = kFlashHd, RB = kFlashRowB, TB = kFlashTileB, NS = kFlashStages;
+  extern __shared__ uint8_t flash_smem_raw[];
+  uint8_t* ring = (uint8_t*)(((uintptr_t)flash_smem_raw + 127) & ~(uintptr_t)127);
+  uint8_t* qsm = ring + (size_t)NS * 2 * TB;
+  uint64_t* full = (uint64_t*)(qsm + 128 * RB);
+
+  const int G = nh / nkv, BQ = 128 / G, wpg = BQ / 16;
+  const int h = blockIdx.x, b = gridDim.y - 1 - blockIdx.y;  // the longest blocks start first
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  const int g = warp / wpg, r0 = b * BQ + (warp - g * wpg) * 16;
+  const int Q = nh * HD;
+  const int kend = min(pos + t, pos + b * BQ + BQ);  // keys visible to the block's last row
+  const int ntiles = (kend + kAttnTile - 1) / kAttnTile;
+  const float inv_scale = 1.0f / scale;
+  const uint8_t* kb = kc + (size_t)h * capacity * RB;
+  const uint8_t* vb = vc + (size_t)h * capacity * RB;
+
+  auto issue = [&](int tile) {
+    const int bi = tile % NS, j0 = tile * kAttnTile;
+    const uint32_t bytes = (uint32_t)min(kAttnTile, kend - j0) * RB;
+    uint8_t* dst = ring + (size_t)bi * 2 * TB;
+    mbar_arrive_expect_tx(&full[bi], 2 * bytes);
+    bulk_load(dst, kb + (size_t)j0 * RB, bytes, &full[bi]);
+    bulk_load(dst + TB, vb + (size_t)j0 * RB, bytes, &full[bi]);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
+    fence_barrier_init();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
   }
-  __syncthreads();
-  if (t == 0) {
-    float mx = -INFINITY;
-    for (int s = 0; s < S; ++s) mx = fmaxf(mx, sm_m[s]);
-    float l = 0.f;
-    for (int s = 0; s < S; ++s) {
-      const float f = (sm_m[s] == -INFINITY) ? 0.f : expf(sm_m[s] - mx);
-      l += sm_w[s] * f;
-      sm_w[s] = f;
+
+  // The block's query vectors (qi = 16 w + i: warp w's row i) as hi/lo rows in the cache-row
+  // layout; rows past the chunk are zero.
+  for (int e = tid; e < 128 * (HD / 8); e += 256) {
+    const int qi = e >> 4, d0 = (e & 15) * 8;
+    const int w = qi >> 4, gq = w / wpg, row = b * BQ + (w - gq * wpg) * 16 + (qi & 15);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (row < t) {
+      const float4* src = (const float4*)(q + (size_t)row * Q + (size_t)(h * G + gq) * HD + d0);
+      const float4 x0 = src[0], x1 = src[1];
+      v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+      v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
     }
-    red_l = l;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) split_pair(v[2 * k], v[2 * k + 1], hw[k], lw[k]);
+    uint8_t* row_p = qsm + (size_t)qi * RB;
+    *(uint4*)(row_p + kv_offset(qi, d0, 0, HD)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *(uint4*)(row_p + kv_offset(qi, d0, 1, HD)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
   __syncthreads();
-  if (t < hd) {
-    float o = 0.f;
-    for (int s = 0; s < S; ++s) o += __ldcg(base + s * stride + 4 + t) * sm_w[s];
-    out[(size_t)(16 * z + r) * ldo + hq * hd + t] = o / red_l;
+  uint32_t qa[HD / 16][2][4];  // [k step][hi, lo] A fragments of the warp's 16 rows
+  {
+    const int qrow = warp * 16 + (lane & 15);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      const uint8_t* qp = qsm + (size_t)qrow * RB + (((2 * ks + (lane >> 4)) ^ (qrow & 7)) << 4);
+      ldmatrix_x4a(qa[ks][0], qp);
+      ldmatrix_x4a(qa[ks][1], qp + 2 * HD);
+    }
+  }
+  // Last key of each of the thread's two rows (g4 and g4 + 8), and of the warp.
+  const int limA = min(pos + r0 + g4, kend - 1), limB = min(pos + r0 + g4 + 8, kend - 1);
+  const int wlim = min(pos + r0 + 15, kend - 1);
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  int tile = 0;
+  for (; tile < ntiles; ++tile) {
+    const int bi = tile % NS, j0 = tile * kAttnTile;
+    const int nrows = min(kAttnTile, kend - j0);
+    const uint8_t* kt = ring + (size_t)bi * 2 * TB;
+    uint8_t* vt = ring + (size_t)bi * 2 * TB + TB;
+    // V rows past the keys are zeroed (P is 0 there, and 0 * stale bits must be 0).
+    for (int e = nrows * RB / 16 + tid; e < TB / 16; e += 256)
+      ((uint4*)vt)[e] = make_uint4(0u, 0u, 0u, 0u);
+    const bool got = mbar_wait(&full[bi], (uint32_t)(tile / NS) & 1u);
+    if (__syncthreads_or(!got)) break;
+    if (j0 <= wlim) {
+      float s[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          const int krow = 16 * np + (lane & 7) + ((lane >> 4) << 3);
+          const int u = 2 * ks + ((lane >> 3) & 1);
+          const uint8_t* kp = kt + (size_t)krow * RB + ((u ^ (krow & 7)) << 4);
+          uint32_t kh[4], kl[4];
+          ldmatrix_x4a(kh, kp);
+          ldmatrix_x4a(kl, kp + 2 * HD);
+          mma_bf16_16816(s[2 * np], qa[ks][0], kh[0], kh[1]);
+          mma_bf16_16816(s[2 * np], qa[ks][0], kl[0], kl[1]);
+          mma_bf16_16816(s[2 * np], qa[ks][1], kh[0], kh[1]);
+          mma_bf16_16816(s[2 * np + 1], qa[ks][0], kh[2], kh[3]);
+          mma_bf16_16816(s[2 * np + 1], qa[ks][0], kl[2], kl[3]);
+          mma_bf16_16816(s[2 * np + 1], qa[ks][1], kh[2], kh[3]);
+        }
+      }
+      // Scale, causal mask, online softmax of rows g4 (elements 0, 1) and g4 + 8 (2, 3).
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = j0 + 8 * j + 2 * t4 + (e & 1);
+          const float v = key <= (e < 2 ? limA : limB) ? s[j][e] * inv_scale : -INFINITY;
+          s[j][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      float alpha[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+        const float mn = fmaxf(mrow[i], mx[i]);
+        alpha[i] = (mrow[i] == -INFINITY) ? 0.f : __expf(mrow[i] - mn);
+        mrow[i] = mn;
+        lrow[i] *= alpha[i];
+      }
+#pragma unroll
+      for (int n = 0; n < HD / 8; ++n) {
+        o[n][0] *= alpha[0];
+        o[n][1] *= alpha[0];
+        o[n][2] *= alpha[1];
+        o[n][3] *= alpha[1];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p = (s[j][e] == -INFINITY) ? 0.f : __expf(s[j][e] - mrow[e >> 1]);
+          s[j][e] = p;
+          lrow[e >> 1] += p;
+        }
+      // O += P V: P's A fragments are the S accumulators of key tiles 2 ks and 2 ks + 1.
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t ph[4], pl[4];
+        split_pair(s[2 * ks][0], s[2 * ks][1], ph[0], pl[0]);
+        split_pair(s[2 * ks][2], s[2 * ks][3], ph[1], pl[1]);
+        split_pair(s[2 * ks + 1][0], s[2 * ks + 1][1], ph[2], pl[2]);
+        split_pair(s[2 * ks + 1][2], s[2 * ks + 1][3], ph[3], pl[3]);
+        const int vrow = 16 * ks + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+        for (int dp = 0; dp < HD / 16; ++dp) {
+          const int u = 2 * dp + (lane >> 4);
+          const uint8_t* vp = vt + (size_t)vrow * RB + ((u ^ (vrow & 7)) << 4);
+          uint32_t vh[4], vl[4];
+          ldmatrix_x4_trans(vh, vp);
+          ldmatrix_x4_trans(vl, vp + 2 * HD);
+          mma_bf16_16816(o[2 * dp], ph, vh[0], vh[1]);
+          mma_bf16_16816(o[2 * dp], ph, vl[0], vl[1]);
+          mma_bf16_16816(o[2 * dp], pl, vh[0], vh[1]);
+          mma_bf16_16816(o[2 * dp + 1], ph, vh[2], vh[3]);
+          mma_bf16_16816(o[2 * dp + 1], ph, vl[2], vl[3]);
+          mma_bf16_16816(o[2 * dp + 1], pl, vh[2], vh[3]);
+        }
+      }
+    }
+    __syncthreads();  // the tile's buffer is free
+    if (tid == 0 && tile + NS < ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(tile + NS);
+    }
+  }
+  if (tile < ntiles) {  // a wait expired: report, and let the copies in flight land
+    if (tid == 0) {
+      atomicOr(&res->status, ST_TIMEOUT);
+      for (int tt = tile; tt < ntiles && tt < tile + NS; ++tt) mbar_wait(&full[tt % NS], (uint32_t)(tt / NS) & 1u);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
+  }
+  const int rowA = r0 + g4, rowB = rowA + 8;
+  float* ob = out + (size_t)(h * G + g) * HD + 2 * t4;
+#pragma unroll
+  for (int n = 0; n < HD / 8; ++n) {
+    if (rowA < t) *(float2*)(ob + (size_t)rowA * Q + 8 * n) = make_float2(o[n][0] / lrow[0], o[n][1] / lrow[0]);
+    if (rowB < t) *(float2*)(ob + (size_t)rowB * Q + 8 * n) = make_float2(o[n][2] / lrow[1], o[n][3] / lrow[1]);
   }
 }
 

@@ -9,7 +9,6 @@
 // header, so it is captured once per chunk width into a CUDA graph and replayed; kernels are
 // chained with programmatic dependent launch so each GEMV streams its weights while the
 // previous kernel drains.
-#include <algorithm>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <fcntl.h>
@@ -172,17 +171,14 @@ struct pp_shard {
   uint32_t* dec_sync = nullptr;
   int dec_ns = 0, dec_vec = 0;
   // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the tcgen05
-  // projection's work area, its error word, one step header per 16-row attention sub-chunk.
+  // projection's work area and its error word, the prompt's tokens.
   struct {
     float *x = nullptr, *xn = nullptr, *tmp = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr,
           *gu = nullptr, *act = nullptr;
     void* work = nullptr;
     uint64_t work_bytes = 0;
     uint32_t* err = nullptr;
-    StepDesc* descs = nullptr;
     int32_t* tokens = nullptr;
-    float* part = nullptr;  // attention partials of every sub-chunk
-    size_t part_stride = 0;  // floats per sub-chunk: n_kv * kPrefillSplits * 16 G * (hd + 4)
   } pf;
   uint32_t launches = 0;                 // kernels of the step being enqueued
   std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
@@ -635,7 +631,6 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
 
 // ---- prompt prefill ------------------------------------------------------------------------
 constexpr int kPrefillMax = 2048;  // rows of one pp_shard_prefill call
-constexpr int kPrefillSplits = 4;  // most key splits of one sub-chunk's attention
 
 pp_status prefill_alloc(pp_shard* s) {
   if (s->pf.x) return PP_OK;
@@ -658,10 +653,7 @@ pp_status prefill_alloc(pp_shard* s) {
   s->pf.work = (void*)(((uintptr_t)w + 1023) & ~(uintptr_t)1023);
   s->pf.work_bytes = wb;
   if ((r = dalloc(s, &s->pf.err, 16))) return r;
-  if ((r = dalloc(s, &s->pf.descs, (T / 16) * sizeof(StepDesc)))) return r;
   if ((r = dalloc(s, &s->pf.tokens, T * 4))) return r;
-  s->pf.part_stride = (size_t)s->nkv * kPrefillSplits * (16 * s->G) * (s->hd + 4);
-  if ((r = dalloc(s, &s->pf.part, (T / 16) * s->pf.part_stride * 4))) return r;
   return PP_OK;
 }
 
@@ -678,8 +670,8 @@ pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, const float
 }
 
 // Every layer of a whole-model shard over t prompt rows at positions pos.. (embedding, and per
-// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, causal attention of
-// every 16-row sub-chunk in one launch plus one combine, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
+// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, flash-style causal
+// attention over the whole chunk, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
 // residual; the last layer stops after its K/V rows, which is all a prefill leaves behind).
 pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   cudaStream_t st = s->stream;
@@ -690,12 +682,8 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
   pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
   CK(cudaGetLastError());
-  const int qpw = (s->G * 16 + 7) / 8;
-  const size_t asmem = attn_smem_bytes(hd, qpw);
   const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
-  // Key splits per sub-chunk: enough that no CTA walks more than 64 key tiles (2048 keys).
-  const int nsub = (t + 15) / 16, ntiles = (int)((pos + t + kAttnTile - 1) / kAttnTile);
-  const int splits = std::min(kPrefillSplits, std::max(1, (ntiles + 63) / 64));
+  const int bq = 128 / s->G;  // prompt rows per attention CTA
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
     pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, s->pf.xn);
@@ -706,30 +694,10 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
     if (l + 1 == s->nl) break;
-    {
-      AttnArgs at = {};
-      at.q = s->pf.q;
-      at.kcache = Ld.kc;
-      at.vcache = Ld.vc;
-      at.part = s->pf.part;
-      at.n_heads = s->nh;
-      at.n_kv = s->nkv;
-      at.head_dim = hd;
-      at.capacity = (int32_t)s->d.capacity;
-      at.splits = splits;
-      at.q_dim = Q;
-      at.nq_max = 16 * s->G;
-      at.scale = sqrtf((float)hd);
-      at.res = s->d_res;
-      const dim3 grid(s->nkv, splits, nsub), block(kAttnThreads);
-      if (qpw <= 2) pre_attn_kernel<2><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
-      else if (qpw <= 4) pre_attn_kernel<4><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
-      else pre_attn_kernel<8><<<grid, block, asmem, st>>>(at, s->pf.descs, s->pf.part_stride);
-      CK(cudaGetLastError());
-      pre_attn_combine_kernel<<<dim3(s->nh, 16, nsub), hd < 32 ? 32 : hd, 0, st>>>(
-          at, s->pf.descs, s->pf.part_stride, s->pf.att, Q);
-      CK(cudaGetLastError());
-    }
+    pre_flash_kernel<<<dim3(s->nkv, (t + bq - 1) / bq), 256, flash_smem_bytes(), st>>>(
+        s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
+        sqrtf((float)hd), s->pf.att, s->d_res);
+    CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wo, H, Q, s->pf.att, t, s->pf.tmp))) return r;
     pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
     pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, s->pf.xn);
@@ -771,8 +739,7 @@ pp_status set_attrs(pp_shard* s) {
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
       (r = set_max_smem(s, decode_step_kernel<1>)) || (r = set_max_smem(s, decode_step_kernel<2>)) ||
       (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)) ||
-      (r = set_max_smem(s, pre_attn_kernel<2>)) || (r = set_max_smem(s, pre_attn_kernel<4>)) ||
-      (r = set_max_smem(s, pre_attn_kernel<8>)))
+      (r = set_max_smem(s, pre_flash_kernel)))
     return r;
   return PP_OK;
 }
@@ -1453,7 +1420,8 @@ pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uin
   if (!s || !tokens) return fail(s, PP_E_INVALID, "null argument");
   if (!(s->first && s->last))
     return fail(s, PP_E_UNSUPPORTED, "the prompt prefill runs shards that hold every layer");
-  if (s->G > 4) return fail(s, PP_E_UNSUPPORTED, "the prompt prefill needs at most 4 query heads per KV head");
+  if (s->hd != kFlashHd || (s->G != 1 && s->G != 2 && s->G != 4 && s->G != 8))
+    return fail(s, PP_E_UNSUPPORTED, "the prompt prefill takes head size 128 and 1, 2, 4 or 8 query heads per KV head");
   if (t == 0 || t > (uint32_t)kPrefillMax) return fail(s, PP_E_INVALID, "t must be 1..2048 rows");
   if ((uint64_t)pos + t > s->d.capacity) return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
   for (uint32_t i = 0; i < t; ++i)  // src/qwen/model.rs:383-389
@@ -1464,15 +1432,6 @@ pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uin
   CK(cudaSetDevice(s->dev));
   pp_status r = prefill_alloc(s);
   if (r) return r;
-  std::vector<StepDesc> descs((t + 15) / 16);
-  for (size_t i = 0; i < descs.size(); ++i) {
-    StepDesc d = {};
-    d.pos = (int32_t)(pos + 16 * i);
-    d.m = (int32_t)(t - 16 * i < 16 ? t - 16 * i : 16);
-    descs[i] = d;
-  }
-  CK(cudaMemcpyAsync(s->pf.descs, descs.data(), descs.size() * sizeof(StepDesc),
-                     cudaMemcpyHostToDevice, s->stream));
   CK(cudaMemcpyAsync(s->pf.tokens, tokens, (size_t)t * 4, cudaMemcpyHostToDevice, s->stream));
   if ((r = enqueue_prefill(s, pos, (int)t))) {
     cudaStreamSynchronize(s->stream);

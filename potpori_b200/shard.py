@@ -211,9 +211,11 @@ class Shard:
     PREFILL_MAX = 2048
 
     def can_prefill(self) -> bool:
-        """Whether prefill() runs here: a shard with every layer, <= 4 query heads per KV head."""
+        """Whether prefill() runs here: a shard with every layer, head size 128 and 1, 2, 4 or 8
+        query heads per KV head (every Qwen3 size)."""
         cfg = self.cfg
-        return self.first and self.last and cfg.n_heads // cfg.n_kv_heads <= 4
+        return (self.first and self.last and cfg.head_dim == 128
+                and cfg.n_heads // cfg.n_kv_heads in (1, 2, 4, 8))
 
     def prefill(self, pos: int, tokens: Sequence[int]) -> None:
         """Write the K/V rows of prompt tokens at pos.. through every layer at once (tensor-core
