@@ -47,13 +47,13 @@ class QwenTarget:
             raise NonFiniteLogits("non-finite or empty logits")
         return r.argmax
 
-    def prefill(self, prompt: List[int]) -> int:
+    def prefill(self, prompt: List[int], one_pass: bool = True) -> int:
         """The greedy pick after the prompt. The reference feeds the prompt in chunk-sized
         verify steps (target.rs:62-84); a shard that can (Shard.can_prefill) writes the K/V
         rows of all but the last token in one pass per 2048 rows on the tensor cores instead,
         and the last token runs as the 1-row step that yields the pick, the same result to
-        the rounding of F32 arithmetic."""
-        if len(prompt) > 1 and self.shard.can_prefill():
+        the rounding of F32 arithmetic. one_pass=False keeps the chunked steps."""
+        if one_pass and len(prompt) > 1 and self.shard.can_prefill():
             self.shard.prefill(0, prompt[:-1])
             return self._pick(len(prompt) - 1, prompt[-1:])[0]
         chunk = self.shard.chunk_size() or len(prompt)
