@@ -101,22 +101,22 @@ __global__ void pre_swiglu_kernel(const float* gu, int32_t gu_rows, int32_t I, i
 }
 
 // ---- causal attention of a prompt chunk ---------------------------------------------------
-// Flash-style: one CTA per (KV head h, block of BQ = 128 / G prompt rows), 8 warps, warp w the
-// 16 rows r0..r0+15 of query head h G + g. The query fragments stay in registers, the 32-key
+// Flash-style: one CTA per (KV head h, block of BQ = 16 NW / G prompt rows), NW warps, warp w
+// the 16 rows r0..r0+15 of query head h G + g. The query fragments stay in registers, the 32-key
 // K/V tiles of the cache stream through a ring of bulk copies, and per tile a warp computes
 // S = Q K^T (16 x 32) on the tensor cores, the online softmax of its rows in registers
 // (running max, rescale, running sum), and O += P V with P taken straight from the S
 // accumulators. Every F32 operand is carried as hi + lo BF16 with the three products
 // hi.hi + hi.lo + lo.hi, as in the verify pass's attention; scores are divided by
 // sqrt(head_dim) and row r sees keys 0..pos + r (tiny.rs:77-101). The normalised rows go to
-// out[r][(h G + g) 128 + d] (F32, the O projection's input). Head size 128; G = 1, 2, 4 or 8;
-// grid (n_kv, ceil(t / BQ)), 256 threads, flash_smem_bytes() of dynamic shared memory.
+// out[r][(h G + g) 128 + d] (F32, the O projection's input). Head size 128, G <= NW; grid
+// (n_kv, ceil(t / BQ)), 32 NW threads, flash_smem_bytes(NW, NS) of dynamic shared memory
+// (NS K/V tiles in flight).
 constexpr int kFlashHd = 128;
 constexpr int kFlashRowB = 4 * kFlashHd;  // a cache row: hi and lo parts of 128 dims
-constexpr int kFlashStages = 3;
 constexpr int kFlashTileB = kAttnTile * kFlashRowB;  // one K (or V) tile
-__host__ __device__ constexpr size_t flash_smem_bytes() {
-  return (size_t)kFlashStages * 2 * kFlashTileB + 128 * (size_t)kFlashRowB + 8 * kFlashStages + 128;
+__host__ __device__ constexpr size_t flash_smem_bytes(int nw, int ns) {
+  return (size_t)ns * 2 * kFlashTileB + 16 * nw * (size_t)kFlashRowB + 8 * ns + 128;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(uint16_t lo_half, uint16_t hi_half) {
@@ -131,17 +131,18 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
   lo = pack_bf16x2(al, bl);
 }
 
-__global__ void __launch_bounds__(256, 1)
+template <int NW, int NS>
+__global__ void __launch_bounds__(32 * NW, 256 / (32 * NW))
     pre_flash_kernel(const float* q, const uint8_t* kc, const uint8_t* vc, int32_t capacity,
                      int32_t nh, int32_t nkv, int32_t pos, int32_t t, float scale,
                      float* out, StepResult* res) {
-  constexpr int HD = kFlashHd, RB = kFlashRowB, TB = kFlashTileB, NS = kFlashStages;
+  constexpr int HD = kFlashHd, RB = kFlashRowB, TB = kFlashTileB, NT = 32 * NW, NQ = 16 * NW;
   extern __shared__ uint8_t flash_smem_raw[];
   uint8_t* ring = (uint8_t*)(((uintptr_t)flash_smem_raw + 127) & ~(uintptr_t)127);
   uint8_t* qsm = ring + (size_t)NS * 2 * TB;
-  uint64_t* full = (uint64_t*)(qsm + 128 * RB);
+  uint64_t* full = (uint64_t*)(qsm + NQ * RB);
 
-  const int G = nh / nkv, BQ = 128 / G, wpg = BQ / 16;
+  const int G = nh / nkv, BQ = NQ / G, wpg = BQ / 16;
   const int h = blockIdx.x, b = gridDim.y - 1 - blockIdx.y;  // the longest blocks start first
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g4 = lane >> 2, t4 = lane & 3;
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(256, 1)
 
   // The block's query vectors (qi = 16 w + i: warp w's row i) as hi/lo rows in the cache-row
   // layout; rows past the chunk are zero.
-  for (int e = tid; e < 128 * (HD / 8); e += 256) {
+  for (int e = tid; e < NQ * (HD / 8); e += NT) {
     const int qi = e >> 4, d0 = (e & 15) * 8;
     const int w = qi >> 4, gq = w / wpg, row = b * BQ + (w - gq * wpg) * 16 + (qi & 15);
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(256, 1)
     const uint8_t* kt = ring + (size_t)bi * 2 * TB;
     uint8_t* vt = ring + (size_t)bi * 2 * TB + TB;
     // V rows past the keys are zeroed (P is 0 there, and 0 * stale bits must be 0).
-    for (int e = nrows * RB / 16 + tid; e < TB / 16; e += 256)
+    for (int e = nrows * RB / 16 + tid; e < TB / 16; e += NT)
       ((uint4*)vt)[e] = make_uint4(0u, 0u, 0u, 0u);
     const bool got = mbar_wait(&full[bi], (uint32_t)(tile / NS) & 1u);
     if (__syncthreads_or(!got)) break;

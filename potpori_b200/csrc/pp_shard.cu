@@ -683,7 +683,7 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
   CK(cudaGetLastError());
   const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
-  const int bq = 128 / s->G;  // prompt rows per attention CTA
+  const int bq = (s->G <= 4 ? 64 : 128) / s->G;  // prompt rows per attention CTA
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
     pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, s->pf.xn);
@@ -694,9 +694,15 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
     if (l + 1 == s->nl) break;
-    pre_flash_kernel<<<dim3(s->nkv, (t + bq - 1) / bq), 256, flash_smem_bytes(), st>>>(
-        s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
-        sqrtf((float)hd), s->pf.att, s->d_res);
+    const dim3 fgrid(s->nkv, (t + bq - 1) / bq);
+    if (s->G <= 4)
+      pre_flash_kernel<4, 2><<<fgrid, 128, flash_smem_bytes(4, 2), st>>>(
+          s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
+          sqrtf((float)hd), s->pf.att, s->d_res);
+    else
+      pre_flash_kernel<8, 3><<<fgrid, 256, flash_smem_bytes(8, 3), st>>>(
+          s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
+          sqrtf((float)hd), s->pf.att, s->d_res);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wo, H, Q, s->pf.att, t, s->pf.tmp))) return r;
     pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
@@ -739,7 +745,8 @@ pp_status set_attrs(pp_shard* s) {
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
       (r = set_max_smem(s, decode_step_kernel<1>)) || (r = set_max_smem(s, decode_step_kernel<2>)) ||
       (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)) ||
-      (r = set_max_smem(s, pre_flash_kernel)))
+      (r = set_max_smem(s, pre_flash_kernel<4, 2>)) ||
+      (r = set_max_smem(s, pre_flash_kernel<8, 3>)))
     return r;
   return PP_OK;
 }
