@@ -31,15 +31,14 @@
 
 #include "../../include/potpori_b200.h"
 #include "pp_common.cuh"
+#include "pp_rows_blocks.cuh"
 
 using namespace pp;
 
 namespace pp {
 
 constexpr int kRgM = 128;                      // weight rows per tile (TMEM lanes)
-constexpr int kRgN = 128;                      // activation rows per tile (TMEM columns)
 constexpr int kRgWBytes = kRgM * kChunkK * 2;  // 16 KB weight block
-constexpr int kRgXBytes = kRgN * kChunkK * 2;  // 16 KB per activation part
 constexpr int kRgStage = kRgWBytes + 2 * kRgXBytes;
 constexpr int kRgStages = 4;  // 4 x 48 KB: a refill from L2 outlasts one stage's MMAs
 constexpr int kRgThreads = 192;
@@ -77,9 +76,8 @@ __device__ __forceinline__ void rg_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Splits F32 rows x[t][c] (row stride ldx) into the MMA's activation blocks:
-// xs[tb][chunk][part][128 rows][64 columns] BF16, part 0 = hi, 1 = lo, the 16-byte unit u of
-// row r at u ^ (r & 7); rows past T and columns past k are zero. One thread per (row, unit).
+// Splits F32 rows x[t][c] (row stride ldx) into the MMA's activation blocks (the layout of
+// pp_rows_blocks.cuh); rows past T and columns past k are zero. One thread per (row, unit).
 __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int32_t k,
                                      int32_t kchunks, int32_t tblocks, uint8_t* xs) {
   const int64_t units = (int64_t)tblocks * kRgN * kchunks * 8;
@@ -87,25 +85,13 @@ __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = i / (kchunks * 8);
     const int u = (int)(i - row * (kchunks * 8));  // unit over the whole padded row
-    const int c = u >> 3, uu = u & 7;
-    const int tb = (int)(row / kRgN), r = (int)(row % kRgN);
-    uint32_t hi[4], lo[4];
+    float v[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      uint16_t h[2], l[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int col = c * kChunkK + uu * 8 + 2 * e + q;
-        const float v = (row < T && col < k) ? x[row * (int64_t)ldx + col] : 0.f;
-        split_bf16(v, h[q], l[q]);
-      }
-      hi[e] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-      lo[e] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
+    for (int e = 0; e < 8; ++e) {
+      const int col = u * 8 + e;
+      v[e] = (row < T && col < k) ? x[row * (int64_t)ldx + col] : 0.f;
     }
-    uint8_t* blk = xs + ((size_t)tb * kchunks + c) * 2 * kRgXBytes;
-    const size_t off = (size_t)r * 128 + (size_t)((uu ^ (r & 7)) << 4);
-    *(uint4*)(blk + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *(uint4*)(blk + kRgXBytes + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    rows_store_unit(xs, kchunks, (int)row, u, v);
   }
 }
 
@@ -117,7 +103,8 @@ __global__ void pp_rows_split_kernel(const float* x, int32_t ldx, int32_t T, int
 // and two TMEM accumulators let the epilogue of one unit run under the MMAs of the next.
 __global__ void __launch_bounds__(kRgThreads, 1)
     pp_rows_gemm_kernel(const uint16_t* w, const uint8_t* xs, float* y, int32_t ldy, int32_t n,
-                        int32_t T, int32_t kchunks, int32_t tblocks, int32_t units, uint32_t* err) {
+                        int32_t T, int32_t kchunks, int32_t tblocks, int32_t units, int32_t accumulate,
+                        uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + (size_t)kRgStages * kRgStage);
@@ -245,6 +232,12 @@ __global__ void __launch_bounds__(kRgThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int t = tb * kRgN + cc * 32 + e;
+            if (t < T && accumulate)  // every load in flight before the first store
+              v[e] = __float_as_uint(y[(size_t)t * ldy + j] + __uint_as_float(v[e]));
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int t = tb * kRgN + cc * 32 + e;
             if (t < T) y[(size_t)t * ldy + j] = __uint_as_float(v[e]);
           }
         }
@@ -277,17 +270,15 @@ extern "C" uint64_t pp_rows_gemm_work_bytes(uint32_t t, uint32_t k) {
   return tblocks * kchunks * 2 * (uint64_t)kRgXBytes;
 }
 
-extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const float* x,
-                                  uint32_t t, float* y, void* work, uint64_t work_bytes,
-                                  uint32_t* err, void* stream) {
-  if (!w_tiled || !x || !y || !work || !err) return rg_fail(PP_E_INVALID, "null argument");
-  if (n == 0 || k == 0 || t == 0 || n > (1u << 24) || k > (1u << 20) || t > (1u << 20))
+namespace pp {
+pp_status rows_gemm_blocks(const uint16_t* w_tiled, uint32_t n, uint32_t k, const uint8_t* xs,
+                           uint32_t t, float* y, uint32_t ldy, bool accumulate, uint32_t* err,
+                           cudaStream_t st) {
+  if (!w_tiled || !xs || !y || !err) return rg_fail(PP_E_INVALID, "null argument");
+  if (n == 0 || k == 0 || t == 0 || n > (1u << 24) || k > (1u << 20) || t > (1u << 20) || ldy < n)
     return rg_fail(PP_E_INVALID, "sizes out of range");
-  if (work_bytes < pp_rows_gemm_work_bytes(t, k))
-    return rg_fail(PP_E_INVALID, "work buffer smaller than pp_rows_gemm_work_bytes(t, k)");
-  if ((uintptr_t)w_tiled % 16 || (uintptr_t)work % 1024)
+  if ((uintptr_t)w_tiled % 16 || (uintptr_t)xs % 1024)
     return rg_fail(PP_E_INVALID, "w_tiled must be 16-byte and work 1024-byte aligned");
-  cudaStream_t st = (cudaStream_t)stream;
   static bool attr_done[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
@@ -307,13 +298,9 @@ extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t 
       cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return rg_fail(PP_E_CUDA, "cannot read the SM count");
   const int grid = units < num_sms[dev] ? units : num_sms[dev];
-  const int64_t sunits = (int64_t)tblocks * kRgN * kchunks * 8;
-  const int sgrid = (int)((sunits + 255) / 256 < 4096 ? (sunits + 255) / 256 : 4096);
-  pp_rows_split_kernel<<<sgrid, 256, 0, st>>>(x, (int32_t)k, (int32_t)t, (int32_t)k, kchunks,
-                                              tblocks, (uint8_t*)work);
-  pp_rows_gemm_kernel<<<grid, kRgThreads, kRgSmem, st>>>(w_tiled, (const uint8_t*)work, y,
-                                                        (int32_t)n, (int32_t)n, (int32_t)t,
-                                                        kchunks, tblocks, units, err);
+  pp_rows_gemm_kernel<<<grid, kRgThreads, kRgSmem, st>>>(w_tiled, xs, y, (int32_t)ldy, (int32_t)n,
+                                                        (int32_t)t, kchunks, tblocks, units,
+                                                        accumulate ? 1 : 0, err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     char msg[160];
@@ -321,4 +308,25 @@ extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t 
     return rg_fail(PP_E_CUDA, msg);
   }
   return PP_OK;
+}
+}  // namespace pp
+
+extern "C" pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const float* x,
+                                  uint32_t t, float* y, void* work, uint64_t work_bytes,
+                                  uint32_t* err, void* stream) {
+  if (!w_tiled || !x || !y || !work || !err) return rg_fail(PP_E_INVALID, "null argument");
+  if (n == 0 || k == 0 || t == 0 || n > (1u << 24) || k > (1u << 20) || t > (1u << 20))
+    return rg_fail(PP_E_INVALID, "sizes out of range");
+  if (work_bytes < pp_rows_gemm_work_bytes(t, k))
+    return rg_fail(PP_E_INVALID, "work buffer smaller than pp_rows_gemm_work_bytes(t, k)");
+  if ((uintptr_t)w_tiled % 16 || (uintptr_t)work % 1024)
+    return rg_fail(PP_E_INVALID, "w_tiled must be 16-byte and work 1024-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int kchunks = (int)((k + kChunkK - 1) / kChunkK);
+  const int tblocks = (int)((t + kRgN - 1) / kRgN);
+  const int64_t sunits = (int64_t)tblocks * kRgN * kchunks * 8;
+  const int sgrid = (int)((sunits + 255) / 256 < 4096 ? (sunits + 255) / 256 : 4096);
+  pp_rows_split_kernel<<<sgrid, 256, 0, st>>>(x, (int32_t)k, (int32_t)t, (int32_t)k, kchunks,
+                                              tblocks, (uint8_t*)work);
+  return rows_gemm_blocks(w_tiled, n, k, (const uint8_t*)work, t, y, n, false, err, st);
 }

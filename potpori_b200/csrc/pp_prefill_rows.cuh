@@ -1,12 +1,15 @@
 // Row kernels of the prompt prefill (pp_shard_prefill): the pieces between the tcgen05
-// projections (pp_rows_gemm) when a whole prompt chunk of t rows goes through the layers at
-// once. Rows are F32 with a row stride equal to their width. The arithmetic is the verify
+// projections (rows_gemm_blocks) when a whole prompt chunk of t rows goes through the layers
+// at once. Rows are F32 with a row stride equal to their width; the inputs of the projections
+// are written straight into their BF16 hi + lo activation blocks (pp_rows_blocks.cuh), and
+// the residual adds happen in the projections' epilogues. The arithmetic is the verify
 // pass's: RMSNorm x * (1 / sqrt(mean(x^2) + eps)) * w (tiny.rs:20-23), per-head QK-norm and
 // rotate-half RoPE at the absolute position with the K/V rows written into the cache
 // (model.rs:267-302, tiny.rs:24-37), SwiGLU g / (1 + e^-g) * u (tiny.rs:111-115).
 #pragma once
 #include "pp_attn.cuh"
 #include "pp_common.cuh"
+#include "pp_rows_blocks.cuh"
 
 namespace pp {
 
@@ -18,8 +21,11 @@ __global__ void pre_embed_kernel(const uint16_t* table, int32_t kchunks, const i
     x[(size_t)t * h + c] = __uint_as_float((uint32_t)table[tiled_offset(tok, c, kchunks)] << 16);
 }
 
-// y[t][c] = x[t][c] * (1 / sqrt(mean_c x[t][c]^2 + eps)) * w[c]; grid (t), 256 threads.
-__global__ void pre_rmsnorm_kernel(const float* x, const float* w, int32_t h, float eps, float* y) {
+// RMSNorm of row t, x[t][c] * (1 / sqrt(mean_c x[t][c]^2 + eps)) * w[c], written straight
+// into the projection's activation blocks (kchunks 64-column chunks, columns past h zero);
+// grid (t), 256 threads.
+__global__ void pre_norm_split_kernel(const float* x, const float* w, int32_t h, float eps,
+                                      int32_t kchunks, uint8_t* xs) {
   __shared__ float red[8];
   const float* xr = x + (size_t)blockIdx.x * h;
   float ss = 0.f;
@@ -27,18 +33,18 @@ __global__ void pre_rmsnorm_kernel(const float* x, const float* w, int32_t h, fl
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-  const float rinv = 1.0f / sqrtf(t / (float)h + eps);
-  float* yr = y + (size_t)blockIdx.x * h;
-  for (int c = threadIdx.x; c < h; c += blockDim.x) yr[c] = xr[c] * rinv * w[c];
-}
-
-// x[i] += d[i] for i < n (the residual adds after O and down); grid-stride.
-__global__ void pre_add_kernel(float* x, const float* d, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    x[i] += d[i];
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float rinv = 1.0f / sqrtf(tot / (float)h + eps);
+  for (int u = threadIdx.x; u < kchunks * 8; u += blockDim.x) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = 8 * u + e;
+      v[e] = c < h ? xr[c] * rinv * w[c] : 0.f;
+    }
+    rows_store_unit(xs, kchunks, (int)blockIdx.x, u, v);
+  }
 }
 
 // Projections qkv[t][Q + 2 KV] of rows at positions pos + t: per head RMSNorm with q_norm /
@@ -85,18 +91,30 @@ __global__ void pre_qkv_kernel(const float* qkv, int32_t t_rows, int32_t pos, in
   }
 }
 
-// SwiGLU over the packed gate/up output (64-row blocks: gate rows then up rows of each 128):
-// act[t][j] = g / (1 + e^-g) * u, j < I; grid-stride over t * I.
-__global__ void pre_swiglu_kernel(const float* gu, int32_t gu_rows, int32_t I, int64_t t_rows,
-                                  float* act) {
-  const int64_t n = t_rows * I;
+// SwiGLU over the packed gate/up output (64-row blocks: gate rows then up rows of each 128),
+// act[t][j] = g / (1 + e^-g) * u for j < I, written straight into the down projection's
+// activation blocks (kchunks 64-column chunks, columns past I zero); one thread per row and 8
+// columns, grid-stride.
+__global__ void pre_swiglu_split_kernel(const float* gu, int32_t gu_rows, int32_t I,
+                                        int32_t t_rows, int32_t kchunks, uint8_t* xs) {
+  const int64_t per_row = (int64_t)kchunks * 8, n = (int64_t)t_rows * per_row;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = e / I;
-    const int j = (int)(e - t * I);
-    const int pg = (j >> 6) * 128 + (j & 63);
-    const float g = gu[t * gu_rows + pg], u = gu[t * gu_rows + pg + 64];
-    act[e] = g / (1.0f + expf(-g)) * u;
+    const int row = (int)(e / per_row), u = (int)(e - row * per_row);
+    const float* src = gu + (size_t)row * gu_rows;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = 8 * u + q;
+      float a = 0.f;
+      if (j < I) {
+        const int pg = (j >> 6) * 128 + (j & 63);
+        const float g = src[pg], up = src[pg + 64];
+        a = g / (1.0f + expf(-g)) * up;
+      }
+      v[q] = a;
+    }
+    rows_store_unit(xs, kchunks, row, u, v);
   }
 }
 
@@ -108,8 +126,9 @@ __global__ void pre_swiglu_kernel(const float* gu, int32_t gu_rows, int32_t I, i
 // (running max, rescale, running sum), and O += P V with P taken straight from the S
 // accumulators. Every F32 operand is carried as hi + lo BF16 with the three products
 // hi.hi + hi.lo + lo.hi, as in the verify pass's attention; scores are divided by
-// sqrt(head_dim) and row r sees keys 0..pos + r (tiny.rs:77-101). The normalised rows go to
-// out[r][(h G + g) 128 + d] (F32, the O projection's input). Head size 128, G <= NW; grid
+// sqrt(head_dim) and row r sees keys 0..pos + r (tiny.rs:77-101). The normalised row r, columns
+// (h G + g) 128 + d, goes straight into the O projection's activation blocks xs (q_dim / 64
+// chunks). Head size 128, G <= NW; grid
 // (n_kv, ceil(t / BQ)), 32 NW threads, flash_smem_bytes(NW, NS) of dynamic shared memory
 // (NS K/V tiles in flight).
 constexpr int kFlashHd = 128;
@@ -135,7 +154,7 @@ template <int NW, int NS>
 __global__ void __launch_bounds__(32 * NW, 256 / (32 * NW))
     pre_flash_kernel(const float* q, const uint8_t* kc, const uint8_t* vc, int32_t capacity,
                      int32_t nh, int32_t nkv, int32_t pos, int32_t t, float scale,
-                     float* out, StepResult* res) {
+                     uint8_t* xs, StepResult* res) {
   constexpr int HD = kFlashHd, RB = kFlashRowB, TB = kFlashTileB, NT = 32 * NW, NQ = 16 * NW;
   extern __shared__ uint8_t flash_smem_raw[];
   uint8_t* ring = (uint8_t*)(((uintptr_t)flash_smem_raw + 127) & ~(uintptr_t)127);
@@ -320,12 +339,12 @@ __global__ void __launch_bounds__(32 * NW, 256 / (32 * NW))
     lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
     lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
   }
-  const int rowA = r0 + g4, rowB = rowA + 8;
-  float* ob = out + (size_t)(h * G + g) * HD + 2 * t4;
+  const int rowA = r0 + g4, rowB = rowA + 8, kcq = Q / kChunkK;
+  const int col = (h * G + g) * HD + 2 * t4;
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) {
-    if (rowA < t) *(float2*)(ob + (size_t)rowA * Q + 8 * n) = make_float2(o[n][0] / lrow[0], o[n][1] / lrow[0]);
-    if (rowB < t) *(float2*)(ob + (size_t)rowB * Q + 8 * n) = make_float2(o[n][2] / lrow[1], o[n][3] / lrow[1]);
+    if (rowA < t) rows_store_pair(xs, kcq, rowA, col + 8 * n, o[n][0] / lrow[0], o[n][1] / lrow[0]);
+    if (rowB < t) rows_store_pair(xs, kcq, rowB, col + 8 * n, o[n][2] / lrow[1], o[n][3] / lrow[1]);
   }
 }
 

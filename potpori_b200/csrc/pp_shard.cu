@@ -170,11 +170,10 @@ struct pp_shard {
   float *dec_qkv = nullptr, *dec_attn = nullptr, *dec_act = nullptr, *dec_part = nullptr;
   uint32_t* dec_sync = nullptr;
   int dec_ns = 0, dec_vec = 0;
-  // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the tcgen05
-  // projection's work area and its error word, the prompt's tokens.
+  // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the
+  // projections' activation blocks (work) and error word, the prompt's tokens.
   struct {
-    float *x = nullptr, *xn = nullptr, *tmp = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr,
-          *gu = nullptr, *act = nullptr;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *gu = nullptr;
     void* work = nullptr;
     uint64_t work_bytes = 0;
     uint32_t* err = nullptr;
@@ -637,13 +636,9 @@ pp_status prefill_alloc(pp_shard* s) {
   pp_status r;
   const size_t T = kPrefillMax;
   if ((r = dalloc(s, &s->pf.x, T * s->H * 4))) return r;
-  if ((r = dalloc(s, &s->pf.xn, T * s->H * 4))) return r;
-  if ((r = dalloc(s, &s->pf.tmp, T * s->H * 4))) return r;
   if ((r = dalloc(s, &s->pf.qkv, T * (s->Q + 2 * s->KV) * 4))) return r;
   if ((r = dalloc(s, &s->pf.q, T * s->Q * 4))) return r;
-  if ((r = dalloc(s, &s->pf.att, T * s->Q * 4))) return r;
   if ((r = dalloc(s, &s->pf.gu, T * s->gu_rows * 4))) return r;
-  if ((r = dalloc(s, &s->pf.act, T * s->I * 4))) return r;
   uint64_t wb = pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->H);
   const uint64_t cand[2] = {pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->Q),
                             pp_rows_gemm_work_bytes((uint32_t)T, (uint32_t)s->I)};
@@ -657,10 +652,13 @@ pp_status prefill_alloc(pp_shard* s) {
   return PP_OK;
 }
 
-// y[t][n] = x[t][k] . W^T on the tensor cores into the shard's prefill buffers.
-pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, const float* x, int t, float* y) {
-  const pp_status st = pp_rows_gemm(w, (uint32_t)n, (uint32_t)k, x, (uint32_t)t, y, s->pf.work,
-                                    s->pf.work_bytes, s->pf.err, s->stream);
+// y[t][n] (row stride ldy) = or += (accumulate) x . W^T on the tensor cores, x being the
+// activation blocks in the shard's prefill work area.
+pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, int t, float* y, int ldy,
+                       bool accumulate) {
+  const pp_status st = rows_gemm_blocks(w, (uint32_t)n, (uint32_t)k, (const uint8_t*)s->pf.work,
+                                        (uint32_t)t, y, (uint32_t)ldy, accumulate, s->pf.err,
+                                        s->stream);
   if (st) {
     char msg[256];
     pp_last_error(nullptr, msg, sizeof msg);
@@ -670,13 +668,17 @@ pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, const float
 }
 
 // Every layer of a whole-model shard over t prompt rows at positions pos.. (embedding, and per
-// layer RMSNorm, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache, flash-style causal
-// attention over the whole chunk, tcgen05 O + residual, RMSNorm, tcgen05 gate/up, SwiGLU, tcgen05 down +
-// residual; the last layer stops after its K/V rows, which is all a prefill leaves behind).
+// layer RMSNorm into activation blocks, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache,
+// flash-style causal attention over the whole chunk into activation blocks, tcgen05 O added
+// to the residual rows, RMSNorm into blocks, tcgen05 gate/up, SwiGLU into blocks, tcgen05 down
+// added to the residual rows; the last layer stops after its K/V rows, which is all a
+// prefill leaves behind).
 pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   cudaStream_t st = s->stream;
   const int H = s->H, Q = s->Q, KV = s->KV, I = s->I, hd = s->hd;
+  const int kcH = (H + kChunkK - 1) / kChunkK, kcI = (I + kChunkK - 1) / kChunkK;
   const float eps = s->d.cfg.rms_norm_eps;
+  uint8_t* xs = (uint8_t*)s->pf.work;
   pp_status r;
   CK(cudaMemsetAsync(s->pf.err, 0, 4, st));
   CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
@@ -684,11 +686,13 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   CK(cudaGetLastError());
   const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
   const int bq = (s->G <= 4 ? 64 : 128) / s->G;  // prompt rows per attention CTA
+  const int64_t swiglu_units = (int64_t)t * kcI * 8;
+  const int swiglu_grid = (int)((swiglu_units + 255) / 256 < 4096 ? (swiglu_units + 255) / 256 : 4096);
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
-    pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, s->pf.xn);
+    pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, kcH, xs);
     CK(cudaGetLastError());
-    if ((r = prefill_gemm(s, Ld.wqkv, Q + 2 * KV, H, s->pf.xn, t, s->pf.qkv))) return r;
+    if ((r = prefill_gemm(s, Ld.wqkv, Q + 2 * KV, H, t, s->pf.qkv, Q + 2 * KV, false))) return r;
     pre_qkv_kernel<<<dim3(t, s->nh + 2 * s->nkv), qthreads, 0, st>>>(
         s->pf.qkv, t, (int32_t)pos, s->nh, s->nkv, hd, eps, Ld.norm[N_QN], Ld.norm[N_KN], s->rope,
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
@@ -698,20 +702,19 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
     if (s->G <= 4)
       pre_flash_kernel<4, 2><<<fgrid, 128, flash_smem_bytes(4, 2), st>>>(
           s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
-          sqrtf((float)hd), s->pf.att, s->d_res);
+          sqrtf((float)hd), xs, s->d_res);
     else
       pre_flash_kernel<8, 3><<<fgrid, 256, flash_smem_bytes(8, 3), st>>>(
           s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
-          sqrtf((float)hd), s->pf.att, s->d_res);
+          sqrtf((float)hd), xs, s->d_res);
     CK(cudaGetLastError());
-    if ((r = prefill_gemm(s, Ld.wo, H, Q, s->pf.att, t, s->pf.tmp))) return r;
-    pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
-    pre_rmsnorm_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, s->pf.xn);
-    if ((r = prefill_gemm(s, Ld.wgu, (int)s->gu_rows, H, s->pf.xn, t, s->pf.gu))) return r;
-    pre_swiglu_kernel<<<1024, 256, 0, st>>>(s->pf.gu, (int32_t)s->gu_rows, I, (int64_t)t, s->pf.act);
-    if ((r = prefill_gemm(s, Ld.wd, H, I, s->pf.act, t, s->pf.tmp))) return r;
-    pre_add_kernel<<<1024, 256, 0, st>>>(s->pf.x, s->pf.tmp, (int64_t)t * H);
+    if ((r = prefill_gemm(s, Ld.wo, H, Q, t, s->pf.x, H, true))) return r;
+    pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, kcH, xs);
     CK(cudaGetLastError());
+    if ((r = prefill_gemm(s, Ld.wgu, (int)s->gu_rows, H, t, s->pf.gu, (int)s->gu_rows, false))) return r;
+    pre_swiglu_split_kernel<<<swiglu_grid, 256, 0, st>>>(s->pf.gu, (int32_t)s->gu_rows, I, t, kcI, xs);
+    CK(cudaGetLastError());
+    if ((r = prefill_gemm(s, Ld.wd, H, I, t, s->pf.x, H, true))) return r;
   }
   return PP_OK;
 }
