@@ -26,7 +26,8 @@ struct AttnArgs {
   StepResult* res;
 };
 
-constexpr int kAttnStages = 3;  // K/V tiles in flight per CTA
+constexpr int kAttnStages = 2;  // K/V tiles in flight per CTA
+constexpr int kAttnSplitsPerSm = 2;  // key splits per KV head: this many per SM of the budget
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -333,8 +334,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
 // Merge of the splits of one (query head hq, chunk row r) by `nthr` threads (t = 0..nthr-1,
 // nthr >= head_dim, synchronised on named barrier `bar_id`), one thread per dimension. Every
 // split's (max, sum) pair and output value is fetched in one batch of independent loads (up
-// to 32 splits per round trip); the merge weights are exp(max_s - max), summed in split
-// order. sm_m / sm_w: [splits] floats of shared memory, red_l: one float.
+// to 64 splits per round trip); the merge weights are exp(max_s - max), formed by the first
+// warp (lane k sums splits k, k + 32, ..., then a butterfly over the lanes; nthr >= 32).
+// sm_m / sm_w: [splits] floats of shared memory, red_l: one float.
 template <int MT>
 __device__ __forceinline__ void combine_unit(const AttnArgs& a, int hq, int r, int t, int nthr,
                                              int bar_id, float* sm_m, float* sm_w, float* red_l) {
@@ -350,31 +352,34 @@ __device__ __forceinline__ void combine_unit(const AttnArgs& a, int hq, int r, i
     sm_m[s] = ml.x;
     sm_w[s] = ml.y;
   }
-  // Output values of the first 32 splits, in flight while the weights are formed.
+  // Output values of the first kPv splits, in flight while the weights are formed.
+  constexpr int kPv = 64;
   const int dd = t;
-  float pv[32];
+  float pv[kPv];
 #pragma unroll
-  for (int q = 0; q < 32; ++q)
+  for (int q = 0; q < kPv; ++q)
     pv[q] = (q < S && dd < hd) ? __ldcg(base + q * stride + 4 + dd) : 0.f;
   named_sync(bar_id, nthr);
-  if (t == 0) {
+  if (t < 32) {  // the first warp: lane k takes splits k, k + 32, ...
     float mx = -INFINITY;
-    for (int s = 0; s < S; ++s) mx = fmaxf(mx, sm_m[s]);
+    for (int s = t; s < S; s += 32) mx = fmaxf(mx, sm_m[s]);
+    mx = warp_max(mx);
     float l = 0.f;
-    for (int s = 0; s < S; ++s) {
+    for (int s = t; s < S; s += 32) {
       const float f = (sm_m[s] == -INFINITY) ? 0.f : expf(sm_m[s] - mx);
       l += sm_w[s] * f;
       sm_w[s] = f;  // now the scale of split s
     }
-    *red_l = l;
+    l = warp_sum(l);
+    if (t == 0) *red_l = l;
   }
   named_sync(bar_id, nthr);
   if (dd < hd) {
     float o = 0.f;
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
+    for (int q = 0; q < kPv; ++q)
       if (q < S) o += pv[q] * sm_w[q];
-    for (int s = 32; s < S; ++s) o += __ldcg(base + s * stride + 4 + dd) * sm_w[s];
+    for (int s = kPv; s < S; ++s) o += __ldcg(base + s * stride + 4 + dd) * sm_w[s];
     store_split<MT>(a.out_split, r, hq * hd + dd, o / *red_l);
   }
   named_sync(bar_id, nthr);  // sm_m / sm_w / red_l are free again

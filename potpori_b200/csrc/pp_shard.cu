@@ -1071,7 +1071,7 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
   CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   pp_status r0 = set_attrs(s);
   if (r0) return r0;
-  s->splits = s->num_sms / s->nkv > 0 ? s->num_sms / s->nkv : 1;
+  s->splits = kAttnSplitsPerSm * s->num_sms / s->nkv > 0 ? kAttnSplitsPerSm * s->num_sms / s->nkv : 1;
   if (s->splits > 256) s->splits = 256;  // the combine kernel holds up to 256 splits
   s->nq_max = s->G * kMaxRows;
   pp_status r;
@@ -1730,7 +1730,7 @@ pp_status pp_shard_set_sm_limit(pp_shard* s, uint32_t ctas) {
   const int n = ctas == 0 || (int)ctas > s->num_sms ? s->num_sms : (int)ctas;
   if (n < s->nkv) return fail(s, PP_E_INVALID, "an SM limit below n_kv_heads (%d)", s->nkv);
   s->max_grid = n;
-  s->splits = n / s->nkv > 256 ? 256 : n / s->nkv;  // buffers were sized for the whole GPU
+  s->splits = kAttnSplitsPerSm * n / s->nkv > 256 ? 256 : kAttnSplitsPerSm * n / s->nkv;  // buffers were sized for the whole GPU
   for (auto& e : s->exec)
     if (e) {
       cudaGraphExecDestroy(e);
