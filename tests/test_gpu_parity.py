@@ -372,12 +372,12 @@ def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
 
 
 def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
-    """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections, the
-    attention of every 16-row sub-chunk in one launch) leaves the K/V rows of the reference's chunked prefill
+    """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections,
+    flash-style causal attention) leaves the K/V rows of the reference's chunked prefill
     (src/qwen/target.rs:62-84): after it, the next steps give the logits of the chunked verify
     path (rel-L2 <= 2e-4) and of the oracle (rel-L2 <= 1e-3, same pick unless the top-2 gap is
     below 1e-3). Config 0 (Qwen3-0.6B seed 0, 41-token prompt from position 0) and a 2-layer
-    model of Qwen3-4B geometry (G = 4) over 173 tokens from position 5 (ragged sub-chunks)."""
+    model of Qwen3-4B geometry (G = 4) over 173 tokens from position 5 (a ragged last block)."""
     from potpori_b200.config import QwenConfig
 
     cases = [(QWEN3_0_6B, 0, 0, 41),
@@ -421,9 +421,9 @@ def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
 @pytest.mark.gpu
 def test_prefill_past_2048_keys_matches_the_chunked_path(gpu):
     """Two prefill calls over a 2199-token prompt (2048 rows from position 0, then 151 rows
-    from position 2048, whose sub-chunks see more than 2048 keys and take two key splits)
-    leave the K/V rows of the chunked verify path: the next two steps agree within
-    rel-L2 2e-4 and pick the same token unless its top-2 gap is below 1e-3. A 2-layer model of Qwen3-0.6B geometry."""
+    from position 2048, whose rows see more than 2048 keys) leave the K/V rows of the chunked
+    verify path: the next two steps agree within rel-L2 2e-4 and pick the same token unless
+    its top-2 gap is below 1e-3. A 2-layer model of Qwen3-0.6B geometry."""
     from potpori_b200.config import QwenConfig
 
     cfg = QwenConfig(2, 1024, 3072, 128, 16, 8, 151936, 1e-6, 1e6)
