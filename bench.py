@@ -58,7 +58,8 @@ def parse_args():
                          "cooperative launch waits for them)")
     ap.add_argument("--draft-sms", type=int, default=0,
                     help="one GPU: run the draft on this many SMs and the target on the rest, "
-                         "so draft steps and verify passes overlap (0: both use every SM)")
+                         "so draft steps and verify passes overlap; N > 1: the draft's grid on "
+                         "rank 0 only (0: every SM of the budget)")
     ap.add_argument("--nccl-sms", type=int, default=None,
                     help="SMs left to NCCL's transfer kernels on every rank when N > 1")
     return ap.parse_args()
@@ -255,9 +256,10 @@ def run_ours(args):
     dmodel = QwenTarget(stage) if wl.draft_is_target and world == 1 else \
         QwenTarget.random(wl.draft, wl.max_seq, wl.chunk, wl.draft_seed, device=local)
     dmodel.shard.set_sm_limit(sm_budget)
-    if args.draft_sms and world == 1 and dmodel.shard is not stage:
+    if args.draft_sms and dmodel.shard is not stage:
         dmodel.shard.set_sm_limit(args.draft_sms)
-        stage.set_sm_limit(n_sms - args.draft_sms)
+        if world == 1:  # disjoint budgets; with N > 1 only the draft's grid shrinks
+            stage.set_sm_limit(n_sms - args.draft_sms)
     if args.draft_kernel == "decode" or (args.draft_kernel == "auto" and world == 1):
         dmodel.shard.set_decode_kernel(True)
     draft = IncrementalDraft(dmodel, wl.chunk)

@@ -49,45 +49,46 @@ __global__ void pre_norm_split_kernel(const float* x, const float* w, int32_t h,
 
 // Projections qkv[t][Q + 2 KV] of rows at positions pos + t: per head RMSNorm with q_norm /
 // k_norm and RoPE, queries to q[t][Q], keys and values into the cache rows of their heads.
-// Grid (t, n_heads + 2 n_kv), one thread per dim pair (hd / 2 threads, hd <= 128).
-__global__ void pre_qkv_kernel(const float* qkv, int32_t t_rows, int32_t pos, int32_t nh,
-                               int32_t nkv, int32_t hd, float eps, const float* qn, const float* kn,
-                               const float2* rope, uint8_t* kc, uint8_t* vc, int32_t capacity,
-                               float* q) {
-  __shared__ float red[4];
-  const int t = blockIdx.x, head = blockIdx.y, i = threadIdx.x, half = hd >> 1;
-  const int Q = nh * hd, KV = nkv * hd;
-  const float* src = qkv + (size_t)t * (Q + 2 * KV) + (size_t)head * hd;
+// Head size 128 (hd is checked by the caller). Grid (t, ceil((n_heads + 2 n_kv) / 4)), 256
+// threads: four heads per block, 64 threads per head, one per dim pair (i, i + 64).
+__global__ void __launch_bounds__(256)
+    pre_qkv_kernel(const float* qkv, int32_t t_rows, int32_t pos, int32_t nh, int32_t nkv,
+                   int32_t hd, float eps, const float* qn, const float* kn, const float2* rope,
+                   uint8_t* kc, uint8_t* vc, int32_t capacity, float* q) {
+  constexpr int HD = 128, HALF = 64;
+  __shared__ float red[8];
+  const int t = blockIdx.x, i = threadIdx.x & (HALF - 1), hl = threadIdx.x / HALF;
+  const int head = blockIdx.y * 4 + hl;
+  const int Q = nh * HD, KV = nkv * HD;
+  const bool valid = head < nh + 2 * nkv;
+  const float* src = qkv + (size_t)t * (Q + 2 * KV) + (size_t)head * HD;
   const int p = pos + t;
+  const float x0 = valid ? src[i] : 0.f, x1 = valid ? src[i + HALF] : 0.f;
+  const float ss_w = warp_sum(x0 * x0 + x1 * x1);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss_w;
+  __syncthreads();
+  if (!valid) return;
   if (head >= nh + nkv) {  // value row
-    uint8_t* row = vc + ((size_t)(head - nh - nkv) * capacity + p) * kv_row_bytes(hd);
-    if (i < half) {
-      kv_store(row, p, i, hd, src[i]);
-      kv_store(row, p, i + half, hd, src[i + half]);
-    }
+    uint8_t* row = vc + ((size_t)(head - nh - nkv) * capacity + p) * kv_row_bytes(HD);
+    kv_store(row, p, i, HD, x0);
+    kv_store(row, p, i + HALF, HD, x1);
     return;
   }
-  const float x0 = i < half ? src[i] : 0.f, x1 = i < half ? src[i + half] : 0.f;
-  float ss = warp_sum(x0 * x0 + x1 * x1);
-  if ((i & 31) == 0) red[i >> 5] = ss;
-  __syncthreads();
-  ss = 0.f;
-  for (int w = 0; w < (int)((blockDim.x + 31) >> 5); ++w) ss += red[w];
-  if (i >= half) return;
-  const float rms = sqrtf(ss / (float)hd + eps);
+  const float ss = red[2 * hl] + red[2 * hl + 1];
+  const float rms = sqrtf(ss / (float)HD + eps);
   const bool isq = head < nh;
   const float* w = isq ? qn : kn;
-  const float y0 = x0 / rms * w[i], y1 = x1 / rms * w[i + half];
-  const float2 cs = rope[(size_t)p * half + i];
+  const float y0 = x0 / rms * w[i], y1 = x1 / rms * w[i + HALF];
+  const float2 cs = rope[(size_t)p * HALF + i];
   const float o0 = y0 * cs.x - y1 * cs.y, o1 = y1 * cs.x + y0 * cs.y;
   if (isq) {
-    float* dst = q + (size_t)t * Q + (size_t)head * hd;
+    float* dst = q + (size_t)t * Q + (size_t)head * HD;
     dst[i] = o0;
-    dst[i + half] = o1;
+    dst[i + HALF] = o1;
   } else {
-    uint8_t* row = kc + ((size_t)(head - nh) * capacity + p) * kv_row_bytes(hd);
-    kv_store(row, p, i, hd, o0);
-    kv_store(row, p, i + half, hd, o1);
+    uint8_t* row = kc + ((size_t)(head - nh) * capacity + p) * kv_row_bytes(HD);
+    kv_store(row, p, i, HD, o0);
+    kv_store(row, p, i + HALF, HD, o1);
   }
 }
 

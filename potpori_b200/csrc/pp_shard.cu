@@ -684,7 +684,6 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
   pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
   CK(cudaGetLastError());
-  const int qthreads = hd / 2 < 32 ? 32 : hd / 2;
   const int bq = (s->G <= 4 ? 64 : 128) / s->G;  // prompt rows per attention CTA
   const int64_t swiglu_units = (int64_t)t * kcI * 8;
   const int swiglu_grid = (int)((swiglu_units + 255) / 256 < 4096 ? (swiglu_units + 255) / 256 : 4096);
@@ -693,7 +692,7 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
     pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, kcH, xs);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wqkv, Q + 2 * KV, H, t, s->pf.qkv, Q + 2 * KV, false))) return r;
-    pre_qkv_kernel<<<dim3(t, s->nh + 2 * s->nkv), qthreads, 0, st>>>(
+    pre_qkv_kernel<<<dim3(t, (s->nh + 2 * s->nkv + 3) / 4), 256, 0, st>>>(
         s->pf.qkv, t, (int32_t)pos, s->nh, s->nkv, hd, eps, Ld.norm[N_QN], Ld.norm[N_KN], s->rope,
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
