@@ -38,6 +38,7 @@ if ROOT not in sys.path:
 METRIC = "Qwen3-4B committed tok/s at 1/2/4/8 B200; verify-pass HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
 NCCL_SMS = 4  # SMs left free for NCCL's transfer kernels on every rank of a multi-GPU run
+DRAFT_SLACK = 8  # with N > 1, SMs of rank 0's budget the draft's decode kernel leaves free
 
 
 def parse_args():
@@ -53,9 +54,9 @@ def parse_args():
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--draft-kernel", default="auto", choices=["auto", "decode", "layers"],
                     help="1-row draft steps: one persistent decode kernel, or six kernels per "
-                         "layer; auto = the decode kernel on one GPU, the per-layer kernels when "
-                         "NCCL transfer kernels share rank 0's SMs (the decode kernel's "
-                         "cooperative launch waits for them)")
+                         "layer; auto = the decode kernel, with N > 1 on DRAFT_SLACK fewer SMs "
+                         "than rank 0's budget (its cooperative launch must find them free "
+                         "while NCCL's transfer kernels hold some)")
     ap.add_argument("--draft-sms", type=int, default=0,
                     help="one GPU: run the draft on this many SMs and the target on the rest, "
                          "so draft steps and verify passes overlap; N > 1: the draft's grid on "
@@ -260,8 +261,12 @@ def run_ours(args):
         dmodel.shard.set_sm_limit(args.draft_sms)
         if world == 1:  # disjoint budgets; with N > 1 only the draft's grid shrinks
             stage.set_sm_limit(n_sms - args.draft_sms)
-    if args.draft_kernel == "decode" or (args.draft_kernel == "auto" and world == 1):
+    if args.draft_kernel in ("decode", "auto"):
         dmodel.shard.set_decode_kernel(True)
+        if world > 1 and not args.draft_sms:
+            # The cooperative grid must find its SMs free while NCCL's transfer kernels and
+            # the stage's kernels come and go on rank 0: leave it DRAFT_SLACK more SMs.
+            dmodel.shard.set_sm_limit(sm_budget - DRAFT_SLACK)
     draft = IncrementalDraft(dmodel, wl.chunk)
     if world == 1:
         chain = LocalChain([stage])

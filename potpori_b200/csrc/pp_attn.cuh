@@ -27,7 +27,7 @@ struct AttnArgs {
 };
 
 constexpr int kAttnStages = 2;  // K/V tiles in flight per CTA
-constexpr int kAttnSplitsPerSm = 2;  // key splits per KV head: this many per SM of the budget
+constexpr int kAttnSplitsPerSm = 2;  // key splits per KV head: at most this many per SM of the budget
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -159,6 +159,7 @@ struct pp_shard {
   // vocabulary head at the measured HBM copy rate in a chain of launches; 12 is slightly
   // slower. PP_GEMV_STAGES overrides it (2..12).
   int gemv_max_stages = 8;
+  int attn_per_sm = kAttnSplitsPerSm;  // attention key splits per KV head and SM of the budget
   bool use_graphs = true, use_pdl = true;
   cudaGraphExec_t exec[kVariants] = {};
   // Single-token decode kernel (pp_shard_set_decode_kernel): row-major weight copies and the
@@ -1067,10 +1068,14 @@ static pp_status create_impl(const pp_shard_desc* desc, pp_shard* s) {
     const int v = atoi(e);
     if (v >= 2 && v <= 12) s->gemv_max_stages = v;
   }
+  if (const char* e = getenv("PP_ATTN_SPLITS_PER_SM")) {
+    const int v = atoi(e);
+    if (v >= 1 && v <= kAttnSplitsPerSm) s->attn_per_sm = v;
+  }
   CK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
   pp_status r0 = set_attrs(s);
   if (r0) return r0;
-  s->splits = kAttnSplitsPerSm * s->num_sms / s->nkv > 0 ? kAttnSplitsPerSm * s->num_sms / s->nkv : 1;
+  s->splits = s->attn_per_sm * s->num_sms / s->nkv > 0 ? s->attn_per_sm * s->num_sms / s->nkv : 1;
   if (s->splits > 256) s->splits = 256;  // the combine kernel holds up to 256 splits
   s->nq_max = s->G * kMaxRows;
   pp_status r;
@@ -1729,7 +1734,7 @@ pp_status pp_shard_set_sm_limit(pp_shard* s, uint32_t ctas) {
   const int n = ctas == 0 || (int)ctas > s->num_sms ? s->num_sms : (int)ctas;
   if (n < s->nkv) return fail(s, PP_E_INVALID, "an SM limit below n_kv_heads (%d)", s->nkv);
   s->max_grid = n;
-  s->splits = kAttnSplitsPerSm * n / s->nkv > 256 ? 256 : kAttnSplitsPerSm * n / s->nkv;  // buffers were sized for the whole GPU
+  s->splits = s->attn_per_sm * n / s->nkv > 256 ? 256 : s->attn_per_sm * n / s->nkv;  // buffers were sized for the whole GPU
   for (auto& e : s->exec)
     if (e) {
       cudaGraphExecDestroy(e);
