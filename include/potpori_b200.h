@@ -242,10 +242,28 @@ pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const fl
  * library holds until exit; it rejects larger sizes with PP_E_INVALID. The first call on a
  * device looks the array up with that device current and should come before any stream
  * capture. Every call shares the array and clears the counters it needs: calls that overlap
- * on the GPU (two streams at once) race on it. stream: a cudaStream_t (NULL = default). */
+ * on the GPU (two streams at once) race on it. *err (device memory, zero before the call, or
+ * NULL) gets status bits: 2 when x holds a non-finite value, 4 when a bounded wait on the
+ * device expired, in which case y is undefined (the call itself still returned PP_OK, since it
+ * only enqueues). stream: a cudaStream_t (NULL = default). */
 pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x, const float* norm_w,
                               float eps, uint32_t n, uint32_t k, uint32_t m, float* y,
-                              void* stream);
+                              uint32_t* err, void* stream);
+
+/* Tapped-layer outputs: TappedShards (src/node.rs:108-223) and LayerTap
+ * (src/transport.rs:148-179). After every step the output rows [m][hidden] of each layer in
+ * `layers` (model layer numbers inside the shard's range and below the model's last layer,
+ * which feeds the logits: src/node.rs:118-124) are kept on the device; duplicates are dropped,
+ * the order is ascending, n = 0 ends tapping. One shard taps any of its layers, where the
+ * reference cuts a node into one shard per tap. 1-row steps of a shard with the decode kernel
+ * run on the per-layer kernels while layers are tapped. */
+pp_status pp_shard_set_taps(pp_shard* shard, const uint32_t* layers, uint32_t n);
+/* The tapped layers (ascending) into layers[0..cap); returns their number. */
+uint32_t pp_shard_tap_layers(const pp_shard* shard, uint32_t* layers, uint32_t cap);
+/* The last step's tapped outputs for its m rows, [n_taps][m][hidden]: F32 into f32 and/or
+ * BF16 bits rounded to nearest even into bf16 (LayerTap::from_f32, the wire form); either may
+ * be NULL. Synchronises the shard's stream. */
+pp_status pp_shard_read_taps(pp_shard* shard, uint32_t m, float* f32, uint16_t* bf16);
 
 /* Message of the last error on the handle (or of the last failed create when NULL). */
 size_t pp_last_error(const pp_shard* shard, char* buf, size_t len);

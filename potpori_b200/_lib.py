@@ -32,7 +32,8 @@ EXPORTS = [
     "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
     "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
     "pp_shard_prefill", "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
-    "pp_rows_gemm_work_bytes", "pp_rows_gemm", "pp_norm_gemv_static", "pp_last_error", "pp_version",
+    "pp_rows_gemm_work_bytes", "pp_rows_gemm", "pp_norm_gemv_static", "pp_shard_set_taps",
+    "pp_shard_tap_layers", "pp_shard_read_taps", "pp_last_error", "pp_version",
 ]
 
 KERNEL_KINDS = ["begin", "embed", "qkv", "attn", "attn_combine", "o_proj", "gate_up", "down",
@@ -128,7 +129,10 @@ def load() -> ctypes.CDLL:
         "pp_shard_decode_greedy": (I32, [P, U32, I32, U32, pI32]),
         "pp_rows_gemm_work_bytes": (U64, [U32, U32]),
         "pp_rows_gemm": (I32, [P, U32, U32, P, U32, P, P, U64, P, P]),
-        "pp_norm_gemv_static": (I32, [P, P, P, F, U32, U32, U32, P, P]),
+        "pp_norm_gemv_static": (I32, [P, P, P, F, U32, U32, U32, P, P, P]),
+        "pp_shard_set_taps": (I32, [P, ctypes.POINTER(U32), U32]),
+        "pp_shard_tap_layers": (U32, [P, ctypes.POINTER(U32), U32]),
+        "pp_shard_read_taps": (I32, [P, U32, P, P]),
         "pp_last_error": (SZ, [P, ctypes.c_char_p, SZ]),
         "pp_version": (ctypes.c_char_p, []),
     }

@@ -19,11 +19,56 @@ from .target import NonFiniteLogits
 RING = 64
 
 
+class HandshakeError(RuntimeError):
+    """Two adjacent stages disagree on the session (src/transport.rs:299-358)."""
+
+
+def hello_mismatch(expected: dict, got: dict) -> str:
+    """Why `got` (the upstream stage's hello) does not fit `expected` (what this stage serves):
+    SessionHello::mismatch, src/transport.rs:256-291."""
+    diffs = []
+    if got["model"] != expected["model"]:
+        diffs.append(f"model {got['model']!r} (this node has {expected['model']!r})")
+    if got["next_layer"] != expected["next_layer"]:
+        diffs.append(f"next layer {got['next_layer']} (this node starts at {expected['next_layer']})")
+    if got["max_seq"] != expected["max_seq"]:
+        diffs.append(f"max_seq {got['max_seq']} (this node has {expected['max_seq']})")
+    if got["chunk"] != expected["chunk"]:
+        diffs.append(f"chunk {got['chunk']} (this node has {expected['chunk']})")
+    if got["taps"] != expected["taps"]:
+        diffs.append(f"tapped layers {got['taps']} (this node has {expected['taps']})")
+    return "upstream expects " + ", ".join(diffs)
+
+
+def check_link(up_range, up_hello: dict, down_range, down_hello: dict) -> None:
+    """receive_hello (src/transport.rs:339-358) for one link: the downstream stage accepts the
+    session only if the upstream hello equals its own; the error names the downstream node
+    and the settings that differ."""
+    if up_hello != down_hello:
+        raise HandshakeError(f"node [{down_range[0]}, {down_range[1]}): "
+                             f"{hello_mismatch(down_hello, up_hello)}")
+
+
+def session_taps(stages) -> List[int]:
+    """The session's tapped layers: every stage's, ascending (each node reports its own)."""
+    return sorted({l for s in stages for l in s.tap_layers()})
+
+
 class LocalChain:
     def __init__(self, stages: Sequence[Shard]):
-        assert stages and stages[0].first and stages[-1].last
+        assert stages and stages[0].first
         for a, b in zip(stages, stages[1:]):
             assert a.range()[1] == b.range()[0], "stages must be contiguous"
+        # The handshake of src/transport.rs:299-358 on every link: each stage's hello carries
+        # the session's tapped layers; the chain must end at the model's last layer (Ready).
+        taps = session_taps(stages)
+        for a, b in zip(stages, stages[1:]):
+            up = dict(a.hello(a.range()[1]), taps=taps)
+            down = dict(b.hello(b.range()[0]), taps=taps)
+            check_link(a.range(), up, b.range(), down)
+        if not stages[-1].last:
+            raise HandshakeError(f"the chain ends at layer {stages[-1].range()[1]}, but the "
+                                 f"model has {stages[-1].model_layers()}")
         self.stages = list(stages)
         self.chunk = stages[0].chunk_size() or 8
         self.inflight: deque = deque()

@@ -318,7 +318,7 @@ __device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const
 }
 
 template <int MT, int NT>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) pp_attn_split_kernel(const AttnArgs a) {
   extern __shared__ uint8_t attn_smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)attn_smem_raw + 127) & ~(uintptr_t)127);
   const AttnSmem L(a.head_dim, NT, kAttnStages);
@@ -387,7 +387,7 @@ __device__ __forceinline__ void combine_unit(const AttnArgs& a, int hq, int r, i
 
 // Grid (n_heads, m), block max(32, head_dim) threads.
 template <int MT>
-__global__ void attn_combine_kernel(const AttnArgs a) {
+__global__ void pp_attn_combine_kernel(const AttnArgs a) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(a.desc, a.capacity, MT)) return;
   pdl_wait();

@@ -56,7 +56,7 @@ struct StepResult {
 };
 
 // A malformed step header (one that did not come through the host checks) makes every
-// kernel of the step return before touching memory; step_begin_kernel reports it.
+// kernel of the step return before touching memory; pp_step_begin_kernel reports it.
 __device__ __forceinline__ bool bad_step(const StepDesc* d, int32_t capacity, int32_t max_rows) {
   const int32_t pos = d->pos, m = d->m;
   return pos < 0 || m < 1 || m > max_rows || (int64_t)pos + m > capacity;

@@ -582,7 +582,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
 }
 
 template <int G>  // query heads per KV head (a.G)
-__global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int NG = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
 
   if (bad_step(a.desc, a.capacity, 1)) return;
   const int pos = a.desc->pos, tok = a.desc->tokens[0];
-  if (tok < 0 || tok >= a.V) return;  // step_begin_kernel reports it
+  if (tok < 0 || tok >= a.V) return;  // pp_step_begin_kernel reports it
   if (tid == 0) {
     for (int i = 0; i < a.nslots; ++i) {
       mbar_init(&r.full[i], 1);
@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
   }
   if (!live || !a.final_norm) return;
   // The vocabulary head's operand: split(x * final_norm) and the sums of squares of x per
-  // 128 columns (the layout input_prep_kernel writes).
+  // 128 columns (the layout pp_input_prep_kernel writes).
   for (int t = b; t < a.ss_tiles; t += NG) {
     float v = 0.f;
     const int n = t * 128 + tid;
@@ -780,7 +780,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_step_kernel(const Deco
 // Row-major copies of the packed weights for the decode kernel: dst[r][c] = W[row(r)][c]
 // with row(r) = r (QKV, O, down) or, for the gate/up pairs (mode 1), gate row r/2 or up row
 // r/2 of the 64-row interleaved blocks.
-__global__ void untile_rows_kernel(uint16_t* dst, const uint16_t* src, int64_t rows, int64_t cols,
+__global__ void pp_untile_rows_kernel(uint16_t* dst, const uint16_t* src, int64_t rows, int64_t cols,
                                    int64_t kchunks, int32_t mode) {
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;

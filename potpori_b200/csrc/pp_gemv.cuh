@@ -73,6 +73,7 @@ struct GemvArgs {
   uint32_t* done_cnt;   // zero between launches
   const StepDesc* desc;  // step header; NULL for a standalone GEMV (m_rows gives the rows)
   StepResult* res;       // step result / status; may be NULL for a standalone GEMV
+  int32_t* status;       // standalone GEMV (res NULL): where the status bits go, or NULL
   int32_t m_rows;
   // Streamed normalised input: the operand is split(x * w_norm) and the sums of squares of
   // x come as per-tile partials [ss_tiles][kMaxRows]; the accumulator is scaled by
@@ -110,6 +111,14 @@ __device__ __forceinline__ int sk_start(uint32_t b, uint32_t T, uint32_t G) {
 }
 __device__ __forceinline__ int sk_owner(uint32_t i, uint32_t T, uint32_t G) {
   return (int)(((i + 1) * G + T - 1) / T) - 1;
+}
+
+// Records status bits (ST_*) of a launch: in the step result, or in the standalone status word.
+__device__ __forceinline__ void gemv_flag(const GemvArgs& a, int32_t bits) {
+  if (a.res)
+    atomicOr(&a.res->status, bits);
+  else if (a.status)
+    atomicOr(a.status, bits);
 }
 
 __device__ __forceinline__ void argrec_merge(float& b1, int32_t& i1, float& s1, float b2,
@@ -296,7 +305,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const GemvShared
       *(uint4*)(blk + R * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     consumer_sync();
-    if (tid == 0 && misc[1] && a.res) atomicOr(&a.res->status, misc[1]);
+    if (tid == 0 && misc[1]) gemv_flag(a, misc[1]);
   }
 
   // Lane roles for ldmatrix: A (weights) matrix mat = lane >> 3 covers rows (mat & 1) * 8 and
@@ -584,7 +593,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const GemvShared
   rp.s = cs;
   rp.phase = cphase;
   if (!ok) {
-    if (tid == 0 && a.res) atomicOr(&a.res->status, ST_TIMEOUT);
+    if (tid == 0) gemv_flag(a, ST_TIMEOUT);
     return false;
   }
 
@@ -650,7 +659,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvArgs& a, const GemvShared
 }
 
 template <int MT, int XM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) pp_gemv_kernel(const GemvArgs a) {
   using L = GemvSmem<MT, XM>;
   constexpr int XB = SplitRows<MT>::kBlock;
   extern __shared__ uint8_t smem_raw[];
@@ -731,7 +740,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         }
       }
       if (issued < n_it) {
-        if (a.res) atomicOr(&a.res->status, ST_TIMEOUT);
+        gemv_flag(a, ST_TIMEOUT);
         // Let the copies already issued land before the CTA's shared memory goes away.
         for (int j = (issued > ns ? issued - ns : 0); j < issued; ++j)
           mbar_wait(&full[j % ns], (uint32_t)(j / ns) & 1);

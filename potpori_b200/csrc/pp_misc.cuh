@@ -61,7 +61,7 @@ __device__ __forceinline__ void prep_unit(const PrepArgs& p, int tile, int r, in
 
 // Grid (ceil(hidden / 128), MT), 128 threads; rows past m are left alone.
 template <int MT>
-__global__ void __launch_bounds__(128) input_prep_kernel(const PrepArgs p, int32_t capacity) {
+__global__ void __launch_bounds__(128) pp_input_prep_kernel(const PrepArgs p, int32_t capacity) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(p.desc, capacity, MT)) return;
   pdl_wait();
@@ -98,7 +98,7 @@ struct RowMap {
 };
 
 // Fill a [rows][cols] logical matrix from the generator into the tiled layout.
-__global__ void gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int64_t kchunks,
+__global__ void pp_gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int64_t kchunks,
                                   RowMap map, uint64_t key, float scale) {
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -110,7 +110,7 @@ __global__ void gen_matrix_kernel(uint16_t* dst, int64_t rows, int64_t cols, int
 
 // Copy an uploaded [rows][cols] matrix (BF16 bits, or F32 rounded to BF16 as the reference's
 // loader does, src/qwen/hf.rs:248-253) into the packed layout.
-__global__ void pack_matrix_kernel(uint16_t* dst, const void* src, int32_t src_f32, int64_t rows,
+__global__ void pp_pack_matrix_kernel(uint16_t* dst, const void* src, int32_t src_f32, int64_t rows,
                                    int64_t cols, int64_t kchunks, RowMap map) {
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -121,7 +121,7 @@ __global__ void pack_matrix_kernel(uint16_t* dst, const void* src, int32_t src_f
   }
 }
 
-__global__ void fill_f32_kernel(float* dst, int64_t n, float v) {
+__global__ void pp_fill_f32_kernel(float* dst, int64_t n, float v) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     dst[i] = v;
@@ -129,7 +129,7 @@ __global__ void fill_f32_kernel(float* dst, int64_t n, float v) {
 
 // Seeded N(0,1) values (rounded through BF16) for KV rows [0, rows) of one layer: a warm
 // context for benchmarks; the oracle's or_shard_fill_kv writes the same values.
-__global__ void fill_kv_kernel(uint8_t* kc, uint8_t* vc, int64_t rows, int32_t kv_dim,
+__global__ void pp_fill_kv_kernel(uint8_t* kc, uint8_t* vc, int64_t rows, int32_t kv_dim,
                                int32_t n_kv, int32_t hd, int64_t capacity, uint64_t key) {
   const int64_t n = rows * kv_dim;
   const float scale = 1.0f / 65536.0f;

@@ -14,7 +14,7 @@
 namespace pp {
 
 // x[t][c] = embedding row of tokens[t] (BF16 decoded), c < h; grid (t), 256 threads.
-__global__ void pre_embed_kernel(const uint16_t* table, int32_t kchunks, const int32_t* tokens,
+__global__ void pp_pre_embed_kernel(const uint16_t* table, int32_t kchunks, const int32_t* tokens,
                                  int32_t h, float* x) {
   const int t = blockIdx.x, tok = tokens[t];
   for (int c = threadIdx.x; c < h; c += blockDim.x)
@@ -24,7 +24,7 @@ __global__ void pre_embed_kernel(const uint16_t* table, int32_t kchunks, const i
 // RMSNorm of row t, x[t][c] * (1 / sqrt(mean_c x[t][c]^2 + eps)) * w[c], written straight
 // into the projection's activation blocks (kchunks 64-column chunks, columns past h zero);
 // grid (t), 256 threads.
-__global__ void pre_norm_split_kernel(const float* x, const float* w, int32_t h, float eps,
+__global__ void pp_pre_norm_split_kernel(const float* x, const float* w, int32_t h, float eps,
                                       int32_t kchunks, uint8_t* xs) {
   __shared__ float red[8];
   const float* xr = x + (size_t)blockIdx.x * h;
@@ -52,7 +52,7 @@ __global__ void pre_norm_split_kernel(const float* x, const float* w, int32_t h,
 // Head size 128 (hd is checked by the caller). Grid (t, ceil((n_heads + 2 n_kv) / 4)), 256
 // threads: four heads per block, 64 threads per head, one per dim pair (i, i + 64).
 __global__ void __launch_bounds__(256)
-    pre_qkv_kernel(const float* qkv, int32_t t_rows, int32_t pos, int32_t nh, int32_t nkv,
+    pp_pre_qkv_kernel(const float* qkv, int32_t t_rows, int32_t pos, int32_t nh, int32_t nkv,
                    int32_t hd, float eps, const float* qn, const float* kn, const float2* rope,
                    uint8_t* kc, uint8_t* vc, int32_t capacity, float* q) {
   constexpr int HD = 128, HALF = 64;
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256)
 // act[t][j] = g / (1 + e^-g) * u for j < I, written straight into the down projection's
 // activation blocks (kchunks 64-column chunks, columns past I zero); one thread per row and 8
 // columns, grid-stride.
-__global__ void pre_swiglu_split_kernel(const float* gu, int32_t gu_rows, int32_t I,
+__global__ void pp_pre_swiglu_split_kernel(const float* gu, int32_t gu_rows, int32_t I,
                                         int32_t t_rows, int32_t kchunks, uint8_t* xs) {
   const int64_t per_row = (int64_t)kchunks * 8, n = (int64_t)t_rows * per_row;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
@@ -153,7 +153,7 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
 
 template <int NW, int NS>
 __global__ void __launch_bounds__(32 * NW, 256 / (32 * NW))
-    pre_flash_kernel(const float* q, const uint8_t* kc, const uint8_t* vc, int32_t capacity,
+    pp_pre_flash_kernel(const float* q, const uint8_t* kc, const uint8_t* vc, int32_t capacity,
                      int32_t nh, int32_t nkv, int32_t pos, int32_t t, float scale,
                      uint8_t* xs, StepResult* res) {
   constexpr int HD = kFlashHd, RB = kFlashRowB, TB = kFlashTileB, NT = 32 * NW, NQ = 16 * NW;

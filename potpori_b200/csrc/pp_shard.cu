@@ -16,6 +16,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -180,6 +181,11 @@ struct pp_shard {
     uint32_t* err = nullptr;
     int32_t* tokens = nullptr;
   } pf;
+  // Tapped layers (pp_shard_set_taps): model layer numbers, ascending, and their output rows
+  // [n_taps][kMaxRows][H] F32 written by every step.
+  std::vector<int> taps;
+  float* d_taps = nullptr;
+  int taps_cap = 0;  // taps the buffer holds
   uint32_t launches = 0;                 // kernels of the step being enqueued
   std::vector<cudaEvent_t>* prof_events = nullptr;  // kernel-by-kernel timing (profile mode)
   std::vector<int>* prof_kinds = nullptr;
@@ -189,6 +195,17 @@ struct pp_shard {
 };
 
 namespace {
+
+// Whether 1-row steps run on the persistent decode kernel (it does not write tapped outputs).
+inline bool use_decode(const pp_shard* s) { return s->dec_on && s->taps.empty(); }
+
+void drop_graphs(pp_shard* s) {
+  for (auto& e : s->exec)
+    if (e) {
+      cudaGraphExecDestroy(e);
+      e = nullptr;
+    }
+}
 
 pp_status fail(pp_shard* s, pp_status st, const char* fmt, ...) {
   char buf[512];
@@ -256,7 +273,7 @@ template <int MT, int XM, int EPI>
 pp_status launch_gemv(pp_shard* s, cudaStream_t st, const uint16_t* w, GemvArgs a) {
   a.w = w;
   using Lay = GemvSmem<MT, XM>;
-  auto kern = gemv_kernel<MT, XM, EPI>;
+  auto kern = pp_gemv_kernel<MT, XM, EPI>;
   const size_t budget = dyn_smem_limit(s, kern);
   a.nstages = gemv_stages<MT, XM>(a.kp, budget, s->gemv_max_stages);
   const size_t smem = Lay::total(a.nstages, a.kp);
@@ -303,7 +320,7 @@ pp_status launch_plain(pp_shard* s, cudaStream_t st, int kind, bool pdl, dim3 gr
 
 // Validates the step header on the device, clears the result and stops every later kernel
 // of a malformed step (a header that came from a peer instead of the host checks).
-__global__ void step_begin_kernel(const StepDesc* desc, StepResult* res, int32_t capacity,
+__global__ void pp_step_begin_kernel(const StepDesc* desc, StepResult* res, int32_t capacity,
                                   int32_t max_rows, int32_t vocab, int32_t first) {
   if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
@@ -330,7 +347,7 @@ __global__ void step_begin_kernel(const StepDesc* desc, StepResult* res, int32_t
 // and, if another step follows, make it the next step's token at the next position. Errors
 // of the step (status bits, a non-finite row) accumulate in out[kDecodeMax].
 constexpr int kDecodeMax = 64;
-__global__ void decode_feed_kernel(StepDesc* desc, const StepResult* res, int32_t* out,
+__global__ void pp_decode_feed_kernel(StepDesc* desc, const StepResult* res, int32_t* out,
                                    int32_t i, int32_t feed) {
   const int32_t t = res->argmax[0];
   out[i] = t;
@@ -374,7 +391,7 @@ template <int MT>
 pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
   s->launches = 0;
   pp_status r;
-  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
+  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, pp_step_begin_kernel, s->d_desc, s->d_res,
                         (int32_t)s->d.capacity, (int32_t)MT, (int32_t)s->V, (int32_t)s->first)))
     return r;
   {
@@ -393,7 +410,7 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
     pa.desc = s->d_desc;
     pa.res = s->d_res;
     if ((r = launch_plain(s, st, PP_K_EMBED, true, dim3(s->ss_tiles, MT), dim3(128), 0,
-                          input_prep_kernel<MT>, pa, (int32_t)s->d.capacity)))
+                          pp_input_prep_kernel<MT>, pa, (int32_t)s->d.capacity)))
       return r;
   }
   for (int l = 0; l < s->nl; ++l) {
@@ -453,14 +470,14 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
       const int qpw = (s->G * MT + 7) / 8;  // query tiles of 8 (G * MT query vectors)
       const size_t smem = attn_smem_bytes(s->hd, qpw);
       const dim3 grid(s->nkv, s->splits), block(kAttnThreads);
-      r = qpw <= 1   ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 1>, atq)
-          : qpw <= 2 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 2>, atq)
-          : qpw <= 4 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 4>, atq)
-                     : launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, attn_split_kernel<MT, 8>, atq);
+      r = qpw <= 1   ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, pp_attn_split_kernel<MT, 1>, atq)
+          : qpw <= 2 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, pp_attn_split_kernel<MT, 2>, atq)
+          : qpw <= 4 ? launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, pp_attn_split_kernel<MT, 4>, atq)
+                     : launch_plain(s, st, PP_K_ATTN, true, grid, block, smem, pp_attn_split_kernel<MT, 8>, atq);
       if (r) return r;
       const int tb = s->hd < 32 ? 32 : s->hd;
       if ((r = launch_plain(s, st, PP_K_ATTN_COMBINE, true, dim3(s->nh, MT), dim3(tb), 0,
-                            attn_combine_kernel<MT>, at)))
+                            pp_attn_combine_kernel<MT>, at)))
         return r;
     }
     // O projection + residual.
@@ -510,6 +527,11 @@ pp_status enqueue_step(pp_shard* s, cudaStream_t st) {
       dn.ss_out = s->ss_attn;
     }
     if ((r = launch_gemv<MT, X_STREAM, EPI_RESADD>(s, st, Ld.wd, dn))) return r;
+    // Tapped layer: keep its output rows (src/node.rs:152-157).
+    for (size_t ti = 0; ti < s->taps.size(); ++ti)
+      if (s->taps[ti] == (int)s->d.layer_begin + l)
+        CK(cudaMemcpy2DAsync(s->d_taps + ti * (size_t)kMaxRows * s->H, (size_t)s->H * 4, s->x,
+                             (size_t)s->Hp * 4, (size_t)s->H * 4, MT, cudaMemcpyDeviceToDevice, st));
   }
   if (s->last && (r = launch_head<MT>(s, st))) return r;
   return PP_OK;
@@ -554,10 +576,10 @@ pp_status decode_rebuild(pp_shard* s) {
   for (int l = 0; l < s->nl; ++l) {
     uint16_t** w = &s->dec_w[(size_t)l * 4];
     const LayerDev& Ld = s->L[l];
-    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, s->Hp / kChunkK, 0);
-    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, s->Qp / kChunkK, 0);
-    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, s->Hp / kChunkK, 1);
-    untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, s->Ip / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, s->Hp / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, s->Qp / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, s->Hp / kChunkK, 1);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, s->Ip / kChunkK, 0);
     CK(cudaGetLastError());
   }
   CK(cudaStreamSynchronize(s->stream));
@@ -570,7 +592,7 @@ pp_status decode_rebuild(pp_shard* s) {
 pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   s->launches = 0;
   pp_status r;
-  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, step_begin_kernel, s->d_desc, s->d_res,
+  if ((r = launch_plain(s, st, PP_K_BEGIN, false, dim3(1), dim3(32), 0, pp_step_begin_kernel, s->d_desc, s->d_res,
                         (int32_t)s->d.capacity, (int32_t)1, (int32_t)s->V, (int32_t)s->first)))
     return r;
   CK(cudaMemsetAsync(s->dec_sync, 0, (size_t)(2 + s->nkv) * 4, st));
@@ -619,10 +641,10 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   switch (s->G) {  // set_decode_kernel admits 1, 2, 4 or 8 query heads per KV head
-    case 1: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<1>, a)); break;
-    case 2: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<2>, a)); break;
-    case 4: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<4>, a)); break;
-    default: CK(cudaLaunchKernelEx(&cfg, decode_step_kernel<8>, a)); break;
+    case 1: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<1>, a)); break;
+    case 2: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<2>, a)); break;
+    case 4: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<4>, a)); break;
+    default: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<8>, a)); break;
   }
   if ((r = after_launch(s, st, PP_K_DECODE))) return r;
   return launch_head<1>(s, st);
@@ -683,36 +705,36 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   pp_status r;
   CK(cudaMemsetAsync(s->pf.err, 0, 4, st));
   CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
-  pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
+  pp_pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
   CK(cudaGetLastError());
   const int bq = (s->G <= 4 ? 64 : 128) / s->G;  // prompt rows per attention CTA
   const int64_t swiglu_units = (int64_t)t * kcI * 8;
   const int swiglu_grid = (int)((swiglu_units + 255) / 256 < 4096 ? (swiglu_units + 255) / 256 : 4096);
   for (int l = 0; l < s->nl; ++l) {
     LayerDev& Ld = s->L[l];
-    pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, kcH, xs);
+    pp_pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_ATTN], H, eps, kcH, xs);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wqkv, Q + 2 * KV, H, t, s->pf.qkv, Q + 2 * KV, false))) return r;
-    pre_qkv_kernel<<<dim3(t, (s->nh + 2 * s->nkv + 3) / 4), 256, 0, st>>>(
+    pp_pre_qkv_kernel<<<dim3(t, (s->nh + 2 * s->nkv + 3) / 4), 256, 0, st>>>(
         s->pf.qkv, t, (int32_t)pos, s->nh, s->nkv, hd, eps, Ld.norm[N_QN], Ld.norm[N_KN], s->rope,
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
     if (l + 1 == s->nl) break;
     const dim3 fgrid(s->nkv, (t + bq - 1) / bq);
     if (s->G <= 4)
-      pre_flash_kernel<4, 2><<<fgrid, 128, flash_smem_bytes(4, 2), st>>>(
+      pp_pre_flash_kernel<4, 2><<<fgrid, 128, flash_smem_bytes(4, 2), st>>>(
           s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
           sqrtf((float)hd), xs, s->d_res);
     else
-      pre_flash_kernel<8, 3><<<fgrid, 256, flash_smem_bytes(8, 3), st>>>(
+      pp_pre_flash_kernel<8, 3><<<fgrid, 256, flash_smem_bytes(8, 3), st>>>(
           s->pf.q, Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->nh, s->nkv, (int32_t)pos, t,
           sqrtf((float)hd), xs, s->d_res);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wo, H, Q, t, s->pf.x, H, true))) return r;
-    pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, kcH, xs);
+    pp_pre_norm_split_kernel<<<t, 256, 0, st>>>(s->pf.x, Ld.norm[N_FFN], H, eps, kcH, xs);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wgu, (int)s->gu_rows, H, t, s->pf.gu, (int)s->gu_rows, false))) return r;
-    pre_swiglu_split_kernel<<<swiglu_grid, 256, 0, st>>>(s->pf.gu, (int32_t)s->gu_rows, I, t, kcI, xs);
+    pp_pre_swiglu_split_kernel<<<swiglu_grid, 256, 0, st>>>(s->pf.gu, (int32_t)s->gu_rows, I, t, kcI, xs);
     CK(cudaGetLastError());
     if ((r = prefill_gemm(s, Ld.wd, H, I, t, s->pf.x, H, true))) return r;
   }
@@ -730,14 +752,14 @@ pp_status set_max_smem(pp_shard* s, K kern) {
 template <int MT>
 pp_status set_attrs_mt(pp_shard* s) {
   pp_status r;
-  if ((r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_QKV>)) ||
-      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_RESADD>)) ||
-      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_SWIGLU>)) ||
-      (r = set_max_smem(s, gemv_kernel<MT, X_STREAM, EPI_ARGMAX>)) ||
-      (r = set_max_smem(s, attn_split_kernel<MT, 1>)) ||
-      (r = set_max_smem(s, attn_split_kernel<MT, 2>)) ||
-      (r = set_max_smem(s, attn_split_kernel<MT, 4>)) ||
-      (r = set_max_smem(s, attn_split_kernel<MT, 8>)))
+  if ((r = set_max_smem(s, pp_gemv_kernel<MT, X_STREAM, EPI_QKV>)) ||
+      (r = set_max_smem(s, pp_gemv_kernel<MT, X_STREAM, EPI_RESADD>)) ||
+      (r = set_max_smem(s, pp_gemv_kernel<MT, X_STREAM, EPI_SWIGLU>)) ||
+      (r = set_max_smem(s, pp_gemv_kernel<MT, X_STREAM, EPI_ARGMAX>)) ||
+      (r = set_max_smem(s, pp_attn_split_kernel<MT, 1>)) ||
+      (r = set_max_smem(s, pp_attn_split_kernel<MT, 2>)) ||
+      (r = set_max_smem(s, pp_attn_split_kernel<MT, 4>)) ||
+      (r = set_max_smem(s, pp_attn_split_kernel<MT, 8>)))
     return r;
   return PP_OK;
 }
@@ -746,10 +768,10 @@ pp_status set_attrs(pp_shard* s) {
   pp_status r;
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
-      (r = set_max_smem(s, decode_step_kernel<1>)) || (r = set_max_smem(s, decode_step_kernel<2>)) ||
-      (r = set_max_smem(s, decode_step_kernel<4>)) || (r = set_max_smem(s, decode_step_kernel<8>)) ||
-      (r = set_max_smem(s, pre_flash_kernel<4, 2>)) ||
-      (r = set_max_smem(s, pre_flash_kernel<8, 3>)))
+      (r = set_max_smem(s, pp_decode_step_kernel<1>)) || (r = set_max_smem(s, pp_decode_step_kernel<2>)) ||
+      (r = set_max_smem(s, pp_decode_step_kernel<4>)) || (r = set_max_smem(s, pp_decode_step_kernel<8>)) ||
+      (r = set_max_smem(s, pp_pre_flash_kernel<4, 2>)) ||
+      (r = set_max_smem(s, pp_pre_flash_kernel<8, 3>)))
     return r;
   return PP_OK;
 }
@@ -757,7 +779,7 @@ pp_status set_attrs(pp_shard* s) {
 pp_status enqueue_variant(pp_shard* s, int vi, cudaStream_t st) {
   pp_status r;
   switch (vi) {
-    case 0: r = s->dec_on ? enqueue_decode_step(s, st) : enqueue_step<1>(s, st); break;
+    case 0: r = use_decode(s) ? enqueue_decode_step(s, st) : enqueue_step<1>(s, st); break;
     case 1: r = enqueue_step<2>(s, st); break;
     case 2: r = enqueue_step<4>(s, st); break;
     case 3: r = enqueue_step<8>(s, st); break;
@@ -772,11 +794,11 @@ pp_status run_step(pp_shard* s, int vi, cudaStream_t st) {
   if (pp_shard_missing(s, nullptr, 0))
     return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
   s->last_variant = vi;
-  if (vi == 0 && s->dec_on && s->dec_stale) {
+  const bool dec = vi == 0 && use_decode(s);
+  if (dec && s->dec_stale) {
     pp_status r = decode_rebuild(s);
     if (r) return r;
   }
-  const bool dec = vi == 0 && s->dec_on;
   if (!s->use_graphs || (dec && !s->dec_graph)) return enqueue_variant(s, vi, st);
   if (!s->exec[vi]) {
     cudaGraph_t g = nullptr;
@@ -1295,7 +1317,7 @@ pp_status pp_shard_set_tensor(pp_shard* s, const char* name, pp_dtype dtype, con
     CK(cudaMalloc(&tmp, elements * eb));
     cudaError_t e = cudaMemcpyAsync(tmp, data, elements * eb, cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) {
-      pack_matrix_kernel<<<1024, 256, 0, s->stream>>>(t.mat, tmp, dtype == PP_F32, t.rows, t.cols,
+      pp_pack_matrix_kernel<<<1024, 256, 0, s->stream>>>(t.mat, tmp, dtype == PP_F32, t.rows, t.cols,
                                                       t.kchunks, t.map);
       e = cudaGetLastError();
     }
@@ -1325,9 +1347,9 @@ pp_status pp_shard_init_random(pp_shard* s, uint64_t seed, float stdv) {
     pp_status r = resolve(s, nm.c_str(), t);
     if (r) return r;
     if (t.is_norm) {
-      fill_f32_kernel<<<64, 256, 0, s->stream>>>(t.norm, t.cols, 1.0f);
+      pp_fill_f32_kernel<<<64, 256, 0, s->stream>>>(t.norm, t.cols, 1.0f);
     } else {
-      gen_matrix_kernel<<<2048, 256, 0, s->stream>>>(t.mat, t.rows, t.cols, t.kchunks, t.map,
+      pp_gen_matrix_kernel<<<2048, 256, 0, s->stream>>>(t.mat, t.rows, t.cols, t.kchunks, t.map,
                                                      tensor_key(seed, nm.c_str()), scale);
     }
     CK(cudaGetLastError());
@@ -1373,6 +1395,14 @@ pp_status pp_shard_load_safetensors(pp_shard* s, const char* path) {
       continue;
     }
     if (!t.mine) continue;
+    // src/qwen/hf.rs:235: the stored shape must be the parameter's ([rows, cols], or [n] for a
+    // norm), not only its element count.
+    const std::vector<int64_t> want =
+        t.is_norm ? std::vector<int64_t>{t.cols} : std::vector<int64_t>{t.rows, t.cols};
+    if (en.shape != want) {
+      r = fail(s, PP_E_INVALID, "shape mismatch for %s", nm.c_str());
+      break;
+    }
     int64_t n = 1;
     for (int64_t v : en.shape) n *= v;
     if (en.begin < 0 || en.end < en.begin || (size_t)en.end > dsize) {
@@ -1481,7 +1511,7 @@ pp_status pp_shard_decode_greedy(pp_shard* s, uint32_t pos, int32_t token, uint3
   CK(cudaMemsetAsync(s->d_decode + kDecodeMax, 0, 4, s->stream));
   for (uint32_t i = 0; i < n; ++i) {
     if ((r = run_step(s, 0, s->stream))) return r;
-    decode_feed_kernel<<<1, 1, 0, s->stream>>>(s->d_desc, s->d_res, s->d_decode, (int32_t)i,
+    pp_decode_feed_kernel<<<1, 1, 0, s->stream>>>(s->d_desc, s->d_res, s->d_decode, (int32_t)i,
                                                 i + 1 < n ? 1 : 0);
     CK(cudaGetLastError());
   }
@@ -1592,7 +1622,7 @@ pp_status pp_shard_fill_kv(pp_shard* s, uint64_t seed, uint32_t rows) {
   CK(cudaSetDevice(s->dev));
   for (int l = 0; l < s->nl; ++l) {
     const uint64_t key = mix64h(seed * 0x9E3779B97F4A7C15ull ^ (uint64_t)(l + 1));
-    fill_kv_kernel<<<1024, 256, 0, s->stream>>>(s->L[l].kc, s->L[l].vc, rows, s->KV, s->nkv, s->hd,
+    pp_fill_kv_kernel<<<1024, 256, 0, s->stream>>>(s->L[l].kc, s->L[l].vc, rows, s->KV, s->nkv, s->hd,
                                                 s->d.capacity, key);
     CK(cudaGetLastError());
   }
@@ -1735,11 +1765,7 @@ pp_status pp_shard_set_sm_limit(pp_shard* s, uint32_t ctas) {
   if (n < s->nkv) return fail(s, PP_E_INVALID, "an SM limit below n_kv_heads (%d)", s->nkv);
   s->max_grid = n;
   s->splits = s->attn_per_sm * n / s->nkv > 256 ? 256 : s->attn_per_sm * n / s->nkv;  // buffers were sized for the whole GPU
-  for (auto& e : s->exec)
-    if (e) {
-      cudaGraphExecDestroy(e);
-      e = nullptr;
-    }
+  drop_graphs(s);
   return PP_OK;
 }
 uint32_t pp_shard_sm_limit(const pp_shard* s) { return s ? (uint32_t)s->max_grid : 0u; }
@@ -1755,9 +1781,9 @@ pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
         (s->G != 1 && s->G != 2 && s->G != 4 && s->G != 8))
       return fail(s, PP_E_UNSUPPORTED, "geometry outside the decode kernel's row and slot sizes");
     const int vec = decode_vec_floats(s->H, s->Q, s->I, s->hd, s->G);
-    size_t budget = dyn_smem_limit(s, decode_step_kernel<1>);
-    for (size_t b : {dyn_smem_limit(s, decode_step_kernel<2>), dyn_smem_limit(s, decode_step_kernel<4>),
-                     dyn_smem_limit(s, decode_step_kernel<8>)})
+    size_t budget = dyn_smem_limit(s, pp_decode_step_kernel<1>);
+    for (size_t b : {dyn_smem_limit(s, pp_decode_step_kernel<2>), dyn_smem_limit(s, pp_decode_step_kernel<4>),
+                     dyn_smem_limit(s, pp_decode_step_kernel<8>)})
       budget = b < budget ? b : budget;
     const size_t fixed = DecodeSmem(0, vec, decode_own_cap(s, s->nkv)).total();
     const int ns = budget > fixed ? (int)((budget - fixed) / kDecSlot) : 0;
@@ -1780,11 +1806,64 @@ int32_t pp_shard_decode_kernel(const pp_shard* s) { return s && s->dec_on ? 1 : 
 pp_status pp_shard_set_pdl(pp_shard* s, int32_t enabled) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
   s->use_pdl = enabled != 0;
-  for (auto& e : s->exec)
-    if (e) {
-      cudaGraphExecDestroy(e);
-      e = nullptr;
+  drop_graphs(s);
+  return PP_OK;
+}
+
+pp_status pp_shard_set_taps(pp_shard* s, const uint32_t* layers, uint32_t n) {
+  if (!s || (n && !layers)) return fail(s, PP_E_INVALID, "null argument");
+  std::vector<int> t(layers, layers + n);
+  std::sort(t.begin(), t.end());
+  t.erase(std::unique(t.begin(), t.end()), t.end());
+  for (int l : t) {
+    // src/node.rs:118-124: the model's last layer feeds the logits and cannot be tapped.
+    if (l + 1 >= (int)s->d.cfg.layers)
+      return fail(s, PP_E_INVALID, "tapped layer %d must be below the model's last layer (%u)", l,
+                  s->d.cfg.layers - 1);
+    if (l < (int)s->d.layer_begin || l >= (int)s->d.layer_end)
+      return fail(s, PP_E_INVALID, "tapped layer %d is outside the shard's layers [%u, %u)", l,
+                  s->d.layer_begin, s->d.layer_end);
+  }
+  CK(cudaSetDevice(s->dev));
+  if ((int)t.size() > s->taps_cap) {
+    pp_status r = dalloc(s, &s->d_taps, t.size() * (size_t)kMaxRows * s->H * 4);
+    if (r) return r;
+    CK(cudaStreamSynchronize(s->stream));
+    s->taps_cap = (int)t.size();
+  }
+  s->taps = t;
+  drop_graphs(s);
+  return PP_OK;
+}
+
+uint32_t pp_shard_tap_layers(const pp_shard* s, uint32_t* layers, uint32_t cap) {
+  if (!s) return 0;
+  for (size_t i = 0; i < s->taps.size() && i < cap; ++i) layers[i] = (uint32_t)s->taps[i];
+  return (uint32_t)s->taps.size();
+}
+
+pp_status pp_shard_read_taps(pp_shard* s, uint32_t m, float* f32, uint16_t* bf16) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (m == 0 || m > (uint32_t)kMaxRows) return fail(s, PP_E_INVALID, "m must be 1..%d", kMaxRows);
+  CK(cudaSetDevice(s->dev));
+  const size_t row = (size_t)m * s->H;
+  std::vector<float> tmp(f32 ? 0 : row);
+  for (size_t i = 0; i < s->taps.size(); ++i) {
+    float* dst = f32 ? f32 + i * row : tmp.data();
+    CK(cudaMemcpyAsync(dst, s->d_taps + i * (size_t)kMaxRows * s->H, row * 4,
+                       cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    if (bf16) {
+      // LayerTap::from_f32 (src/transport.rs:160-168): round to nearest even, NaN kept quiet.
+      for (size_t j = 0; j < row; ++j) {
+        uint32_t u;
+        memcpy(&u, &dst[j], 4);
+        bf16[i * row + j] = (u & 0x7fffffffu) > 0x7f800000u
+                                ? (uint16_t)((u >> 16) | 0x40)
+                                : (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+      }
     }
+  }
   return PP_OK;
 }
 

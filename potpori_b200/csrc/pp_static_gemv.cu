@@ -31,6 +31,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};  // device address of the array, per device
 int g_num_sms[kMaxDevices] = {};
+size_t g_smem_budget[kMaxDevices] = {};  // dynamic shared memory the kernel may use, per device
 
 // Messages go where pp_last_error(NULL, ...) reads them.
 pp_status static_fail(pp_status st, const char* msg) {
@@ -47,7 +48,7 @@ static __device__ __align__(256) uint8_t g_norm_gemv_scratch[kScratchBytes];
 
 extern "C" pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x,
                                          const float* norm_w, float eps, uint32_t n, uint32_t k,
-                                         uint32_t m, float* y, void* stream) {
+                                         uint32_t m, float* y, uint32_t* err, void* stream) {
   if (!w_tiled || !x || !norm_w || !y) return static_fail(PP_E_INVALID, "null argument");
   if (m < 1 || m > (uint32_t)kStaticRows)
     return static_fail(PP_E_INVALID, "m must be 1..8 rows");
@@ -60,7 +61,7 @@ extern "C" pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return static_fail(PP_E_CUDA, "no current CUDA device");
   using Kern = void (*)(GemvArgs);
-  Kern kern = gemv_kernel<kStaticRows, X_RESIDENT_NORM, EPI_STORE>;
+  Kern kern = pp_gemv_kernel<kStaticRows, X_RESIDENT_NORM, EPI_STORE>;
   {
     // Once per device, with that device current: the array's device address and the
     // kernel's shared-memory limit. Documented to run before any stream capture.
@@ -80,6 +81,7 @@ extern "C" pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x
                                optin - (int)fa.sharedSizeBytes) != cudaSuccess)
         return static_fail(PP_E_CUDA, "kernel set-up failed");
       g_num_sms[dev] = sms < kStaticMaxCtas ? sms : kStaticMaxCtas;
+      g_smem_budget[dev] = (size_t)optin - fa.sharedSizeBytes;
       g_scratch_ptr[dev] = p;
     }
   }
@@ -103,14 +105,13 @@ extern "C" pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x
   a.partials = (float*)scratch;
   a.tile_cnt = (uint32_t*)(scratch + kPartialBytes);
   a.m_rows = (int32_t)m;
+  // Non-finite x values and an expired bounded wait (ST_NONFINITE_IN, ST_TIMEOUT) are ORed
+  // into the caller's error word.
+  a.check_input = 1;
+  a.status = (int32_t*)err;
 
   using Lay = GemvSmem<kStaticRows, X_RESIDENT_NORM>;
-  cudaFuncAttributes fa;
-  int optin = 0;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
-      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-    return static_fail(PP_E_CUDA, "kernel query failed");
-  const size_t budget = (size_t)optin - fa.sharedSizeBytes;
+  const size_t budget = g_smem_budget[dev];
   int ns = 12;
   while (ns > 2 && Lay::total(ns, a.kp) > budget) --ns;
   if (Lay::total(ns, a.kp) > budget)

@@ -29,6 +29,7 @@ from typing import List, Tuple
 import torch
 import torch.distributed as dist
 
+from .chain import HandshakeError, check_link
 from .config import is_eos
 from .target import NonFiniteLogits
 
@@ -133,15 +134,26 @@ class CudaStageIO:
     def chunk_size(self) -> int:
         return self.shard.chunk_size()
 
+    def range(self) -> Tuple[int, int]:
+        return self.shard.range()
+
+    def model_layers(self) -> int:
+        return self.shard.model_layers()
+
+    def hello(self, next_layer: int) -> dict:
+        return self.shard.hello(next_layer)
+
 
 class HostStageIO:
     """The same interface over host tensors and a host `stage` object with `step(hdr, hid,
     res)`: runs the protocol under gloo without a GPU (tests of the multi-process logic)."""
 
     def __init__(self, stage, width: int, hidden: int, first: bool, last: bool,
-                 capacity: int = 4096, chunk: int = 8):
+                 capacity: int = 4096, chunk: int = 8, layer_range=(0, 1), model_layers=1,
+                 model: str = "host-stand-in"):
         self.stage, self.width = stage, width
         self.first, self.last = first, last
+        self._range, self._layers, self._model = tuple(layer_range), model_layers, model
         self.hid = torch.zeros(width * hidden, dtype=torch.float32)
         self.hdr = torch.zeros(HDR_INTS, dtype=torch.int32)
         self.res = torch.zeros(RES_INTS, dtype=torch.int32)
@@ -196,11 +208,49 @@ class HostStageIO:
     def chunk_size(self) -> int:
         return self._chunk
 
+    def range(self) -> Tuple[int, int]:
+        return self._range
+
+    def model_layers(self) -> int:
+        return self._layers
+
+    def hello(self, next_layer: int) -> dict:
+        return {"model": self._model, "next_layer": next_layer, "max_seq": self._cap,
+                "chunk": self._chunk, "taps": []}
+
+
+def negotiate(io, rank: int, world: int) -> None:
+    """The session handshake (src/transport.rs:299-358) before any frame moves: every rank
+    publishes the hello it sends downstream (its range end) and the one it expects from
+    upstream (its range start); every link is checked, and the chain must end at the model's
+    last layer (the head's Ready check). All ranks take this one collective step and raise the
+    same HandshakeError, so a mismatched session ends everywhere before the first chunk."""
+    a, b = io.range()
+    mine = {"range": (a, b), "down": io.hello(b), "up": io.hello(a),
+            "layers": io.model_layers()}
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    # Each hello carries the session's tapped layers: every stage's own, ascending.
+    taps = sorted({l for v in every for l in v["up"]["taps"]})
+    errors = []
+    for r in range(1, world):
+        try:
+            check_link(every[r - 1]["range"], dict(every[r - 1]["down"], taps=taps),
+                       every[r]["range"], dict(every[r]["up"], taps=taps))
+        except HandshakeError as e:
+            errors.append(str(e))
+    end, layers = every[-1]["range"][1], every[-1]["layers"]
+    if end != layers:
+        errors.append(f"the chain ends at layer {end}, but the model has {layers}")
+    if errors:
+        raise HandshakeError("; ".join(errors))
+
 
 def run_stage(shard, rank: int, world: int, width: int, links: Links, io=None) -> float:
     """Serve as stage `rank` (1 <= rank < world) until the session ends. Returns the time (ms)
     between the timed-window marks, measured on this stage's stream (0 without both marks)."""
     io = io or CudaStageIO(shard, width)
+    negotiate(io, rank, world)
     started = ended = False
     with io.ordered():
         while True:
@@ -239,6 +289,7 @@ class DistChain:
     def __init__(self, stage0, world: int, width: int, links: Links, io=None):
         self.io = io or CudaStageIO(stage0, width)
         assert self.io.first and not self.io.last and world > 1
+        negotiate(self.io, 0, world)
         self.world, self.width, self.links = world, width, links
         self.slots = self.io.result_slots(RING)
         self.inflight: deque = deque()

@@ -8,7 +8,7 @@ kernel of the step (graph replay, event per kernel) and reports latency and achi
 GB/s against the algorithmic bytes of that kernel. The tail (final norm + vocab projection
 + argmax over 151936 rows at hidden 2560) is timed the same way on a last-layer shard.
 
-    python -m potpori_b200.layer_sweep [--kv 128 512 2048 4096] [--m 1 4 8 16] [--json]
+    python bench.py --probe layer-sweep [--kv 128 512 2048 4096] [--m 1 4 8 16] [--json]
 """
 from __future__ import annotations
 
@@ -77,7 +77,7 @@ def sweep(kv_lens, ms, steps=3, iters=5, device=0, seed=4, tail=True):
     return rows, peak, src
 
 
-def main():
+def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--kv", type=int, nargs="+", default=[128, 512, 2048, 4096])
     ap.add_argument("--m", type=int, nargs="+", default=[1, 4, 8, 16])
@@ -85,7 +85,7 @@ def main():
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--no-tail", action="store_true")
     ap.add_argument("--json", action="store_true")
-    a = ap.parse_args()
+    a = ap.parse_args(argv)
     rows, peak, src = sweep(a.kv, a.m, a.steps, a.iters, tail=not a.no_tail)
     if a.json:
         for r in rows:

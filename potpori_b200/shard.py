@@ -62,6 +62,7 @@ class Shard:
         self._L = L
         self.device = device
         self._vo = _lib.VerifyOut()
+        self._last_m = 1
         self._am = np.zeros(16, np.int32)
         self._t1 = np.zeros(16, np.float32)
         self._t2 = np.zeros(16, np.float32)
@@ -158,9 +159,40 @@ class Shard:
         return int(self._L.pp_shard_chunk_size(self._h))
 
     def hello(self, next_layer: int) -> dict:
-        """SessionHello of src/qwen/shard.rs:89-105."""
+        """SessionHello of src/qwen/shard.rs:89-105 (with the tapped layers of
+        TappedShards::hello, src/node.rs:160-166)."""
         return {"model": self.cfg.hello_model(), "next_layer": next_layer,
-                "max_seq": self.capacity(), "chunk": self.chunk_size(), "taps": []}
+                "max_seq": self.capacity(), "chunk": self.chunk_size(),
+                "taps": self.tap_layers()}
+
+    # ---- tapped layers (TappedShards, src/node.rs:108-223) ----
+    def set_taps(self, layers: Sequence[int]) -> None:
+        """Keep the output rows of these model layers after every step (ascending, inside the
+        shard's range, below the model's last layer); [] ends tapping."""
+        arr = (ctypes.c_uint32 * max(len(layers), 1))(*[int(l) for l in layers])
+        check(self._L.pp_shard_set_taps(self._h, arr, len(layers)), self._h, "set_taps")
+
+    def tap_layers(self) -> List[int]:
+        """ShardEngine::tap_layers (src/node.rs:206-213): the tapped layers of this shard."""
+        buf = (ctypes.c_uint32 * 256)()
+        n = int(self._L.pp_shard_tap_layers(self._h, buf, 256))
+        return [int(buf[i]) for i in range(min(n, 256))]
+
+    def take_taps(self, m: Optional[int] = None, bf16: bool = False) -> List[np.ndarray]:
+        """ShardEngine::take_taps (src/node.rs:214-216): the last step's output of every tapped
+        layer, [m, hidden] each (F32, or the BF16 bits of the wire form LayerTap::from_f32)."""
+        m = int(m if m is not None else self._last_m)
+        layers = self.tap_layers()
+        if not layers:
+            return []
+        shape = (len(layers), m, self.cfg.hidden)
+        f = np.empty(shape, np.float32) if not bf16 else None
+        b = np.empty(shape, np.uint16) if bf16 else None
+        check(self._L.pp_shard_read_taps(self._h, m, f.ctypes.data if f is not None else None,
+                                         b.ctypes.data if b is not None else None),
+              self._h, "read_taps")
+        out = b if bf16 else f
+        return [out[i] for i in range(len(layers))]
 
     def reset(self) -> None:
         check(self._L.pp_shard_reset(self._h), self._h, "reset KV")
@@ -256,6 +288,7 @@ class Shard:
         else:
             hid = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32)).reshape(-1)
             m = hid.size // cfg.hidden
+        self._last_m = m
         out_h = None if self.last else np.empty((m, cfg.hidden), np.float32)
         logits = np.empty((m, cfg.vocab_size), np.float32) if (self.last and want_logits) else None
         vo = self._verify_struct(logits) if self.last else None
@@ -308,6 +341,7 @@ class Shard:
                  stream: int = 0, flags: int = 0) -> None:
         """Enqueue the step header. flags bit 0 (or want_logits) also writes the logits; other
         bits travel with the header to the next stages."""
+        self._last_m = m
         t = _i32(tokens) if tokens is not None else None
         d = _i32(drafts)
         check(self._L.pp_shard_set_step(

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this folder from the potpori reference checkout.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <potpori checkout>
 
 Source: the reference's own golden vectors in ``tests/fixtures/dspark_tiny`` (made by its
 ``tools/make_dspark_fixture.py`` with transformers): a 6-layer tiny Qwen3 target
@@ -31,7 +31,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the potpori repository checkout")
     args = ap.parse_args()
     src = os.path.join(args.reference, "tests", "fixtures", "dspark_tiny")
 

@@ -97,3 +97,38 @@ def tile_weights(w: np.ndarray) -> np.ndarray:
     off = ((((j // 128) * kc + c // 64) * 128 + j % 128) * 64) + ((((c % 64) // 8) ^ (j % 8)) * 8) + c % 8
     out[off] = w
     return out
+
+
+def random_weights(cfg: QwenConfig, seed: int, std: float = 0.02) -> dict:
+    """Every parameter of a whole-model graph: matrices N(0, std) as BF16 bits, norms
+    1 + 0.1 N(0, 1) as F32 (numpy's generator, not the shards' seeded one)."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in param_shapes(cfg):
+        if "norm" in name:
+            out[name] = (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32)
+        else:
+            out[name] = f32_to_bf16_bits((std * rng.standard_normal(shape)).astype(np.float32))
+    return out
+
+
+def write_prepared(path: str, cfg: QwenConfig, weights: dict, matrix_dtype: str = "bf16") -> None:
+    """A prepared weights file in the layout of src/qwen/hf.rs:20,85-91 (the
+    model_combined_bf16_v1.safetensors the reference writes): one safetensors file, matrices
+    BF16 (or F32 with matrix_dtype="f32", as a checkpoint used as published may store them),
+    norms F32, the tied embedding as model.embed_tokens.weight."""
+    import torch
+    from safetensors.torch import save_file
+
+    shapes = dict(param_shapes(cfg))
+    tensors = {}
+    for name, value in weights.items():
+        shape = shapes[name]
+        if "norm" in name:
+            tensors[name] = torch.from_numpy(np.asarray(value, np.float32).reshape(shape).copy())
+        elif matrix_dtype == "f32":
+            tensors[name] = torch.from_numpy(bf16_bits_to_f32(value).reshape(shape).copy())
+        else:
+            bits = np.asarray(value, np.uint16).reshape(shape).view(np.int16).copy()
+            tensors[name] = torch.from_numpy(bits).view(torch.bfloat16)
+    save_file(tensors, path)

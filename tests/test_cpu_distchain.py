@@ -52,7 +52,8 @@ def _worker(rank: int, world: int, port: int, q) -> None:
     try:
         links = Links(world)
         io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
-                         first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH)
+                         first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH,
+                         layer_range=(rank, rank + 1), model_layers=world)
         if rank != 0:
             q.put((rank, "ms", run_stage(None, rank, world, WIDTH, links, io=io)))
             return
@@ -114,3 +115,67 @@ def test_pipeline_protocol_over_gloo(world):
     # every stage saw both window marks
     for r in range(1, world):
         assert got[(r, "ms")] > 0.0
+
+
+def _hello_worker(rank: int, world: int, port: int, bad: str, q) -> None:
+    import torch.distributed as dist
+    from potpori_b200.chain import HandshakeError
+    from potpori_b200.distchain import DistChain, HostStageIO, Links, run_stage
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        links = Links(world)
+        cap, chunk, rng, layers = 256, WIDTH, (rank, rank + 1), world
+        if rank == world - 1:  # the last stage is set up differently
+            if bad == "chunk":
+                chunk = 4
+            elif bad == "max_seq":
+                cap = 512
+            elif bad == "boundary":
+                rng = (rank + 1, rank + 2)
+                layers = world + 1
+            elif bad == "short":
+                layers = world + 1
+        io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
+                         first=rank == 0, last=rank == world - 1, capacity=cap, chunk=chunk,
+                         layer_range=rng, model_layers=layers)
+        try:
+            if rank == 0:
+                DistChain(None, world, WIDTH, links, io=io)
+            else:
+                run_stage(None, rank, world, WIDTH, links, io=io)
+            q.put((rank, "refused", None))
+        except HandshakeError as e:
+            q.put((rank, "refused", str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bad,words", [("chunk", "chunk 8 (this node has 4)"),
+                                       ("max_seq", "max_seq 256 (this node has 512)"),
+                                       ("boundary", "next layer 2 (this node starts at 3)"),
+                                       ("short", "the chain ends at layer 3, but the model has 4")])
+def test_handshake_refuses_a_mismatched_session(bad, words):
+    """src/transport.rs:299-358: before any frame moves, every link compares the upstream
+    stage's hello with what the downstream stage serves, and a chain that stops short of the
+    model's last layer is refused; every rank gets the same error, naming what differs."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hello_worker, args=(r, world, port, bad, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    got = {}
+    while not q.empty():
+        r, k, v = q.get()
+        got[r] = v
+    assert sorted(got) == list(range(world)), got
+    for r in range(world):
+        assert got[r] is not None and words in got[r], (r, got[r])

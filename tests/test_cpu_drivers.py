@@ -179,3 +179,49 @@ def test_stepwise_driver_matches_the_loop():
     while d.step():
         steps += 1
     assert d.out == a and steps == d.traversals
+
+
+class _HelloStage:
+    """What LocalChain reads from a stage before the first chunk: range, role, hello."""
+
+    def __init__(self, a, b, layers=4, max_seq=768, chunk=8, model="qwen3:4:64:128:64:2:1",
+                 taps=()):
+        self._r, self._layers = (a, b), layers
+        self.first, self.last = a == 0, b == layers
+        self._hello = {"model": model, "max_seq": max_seq, "chunk": chunk}
+        self._taps = list(taps)
+
+    def range(self):
+        return self._r
+
+    def model_layers(self):
+        return self._layers
+
+    def chunk_size(self):
+        return self._hello["chunk"]
+
+    def tap_layers(self):
+        return self._taps
+
+    def hello(self, next_layer):
+        return dict(self._hello, next_layer=next_layer, taps=self._taps)
+
+
+def test_local_chain_handshake():
+    """src/transport.rs:299-358 on LocalChain's links: matching stages (with taps on some of
+    them) are accepted; a different model, max_seq or chunk on one link, or a chain that stops
+    before the model's last layer, is refused with the settings that differ."""
+    from potpori_b200.chain import HandshakeError, LocalChain
+
+    LocalChain([_HelloStage(0, 2, taps=[1]), _HelloStage(2, 4)])
+    cases = [
+        ([_HelloStage(0, 2), _HelloStage(2, 4, model="qwen3:4:64:128:64:4:1")], "model"),
+        ([_HelloStage(0, 2), _HelloStage(2, 4, max_seq=512)], "max_seq 768 (this node has 512)"),
+        ([_HelloStage(0, 1), _HelloStage(1, 3, chunk=4), _HelloStage(3, 4, chunk=4)],
+         "node [1, 3): upstream expects chunk 8 (this node has 4)"),
+        ([_HelloStage(0, 2), _HelloStage(2, 3)], "the chain ends at layer 3, but the model has 4"),
+    ]
+    for stages, words in cases:
+        with pytest.raises(HandshakeError) as e:
+            LocalChain(stages)
+        assert words in str(e.value)

@@ -6,7 +6,9 @@ allowed); it keeps its scratch in a static device array. Here it must reproduce 
 projection of a last shard, through the C ABI, on two calls in a row: the shard's one layer
 has all-zero matrices, so its output is its input and the shard's logits are exactly
 RMSNorm(x, model.norm) . embed^T, computed by the existing entry point
-(pp_shard_forward_hidden with logits requested). This file sorts last so that a run that
+(pp_shard_forward_hidden with logits requested). A ragged case (3 rows, k = 200, which
+pads to a fourth 64-column chunk) is checked against a float64 RMSNorm . W^T, and a
+non-finite input must set the caller's error word. This file sorts last so that a run that
 stops at the first failure has run every other test first.
 """
 import ctypes
@@ -68,21 +70,55 @@ def test_norm_gemv_static_matches_the_shard_head(gpu):
     x_t = torch.from_numpy(x).to(dev)
     n_t = torch.from_numpy(fnorm).to(dev)
     y_t = torch.empty((m, cfg.vocab_size), dtype=torch.float32, device=dev)
+    err_t = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
     for call in range(2):
         y_t.fill_(float("nan"))
         st = L.pp_norm_gemv_static(w_t.data_ptr(), x_t.data_ptr(), n_t.data_ptr(),
                                    ctypes.c_float(cfg.rms_norm_eps), cfg.vocab_size, cfg.hidden,
-                                   m, y_t.data_ptr(), ctypes.c_void_p(stream))
+                                   m, y_t.data_ptr(), err_t.data_ptr(), ctypes.c_void_p(stream))
         assert st == _lib.PP_OK, _lib.last_error(None)
         torch.cuda.synchronize(dev)
         got = y_t.cpu().numpy()
+        assert int(err_t.item()) == 0, f"call {call}: status {int(err_t.item())}"
         assert np.isfinite(got).all(), f"call {call}"
         assert rel_l2(got, want) <= 1e-3, f"call {call}"
         assert np.abs(got - want).max() <= 1e-4, f"call {call}"
 
+    # A ragged case: 3 of the 8 rows, k = 200 (a padded fourth 64-column chunk), 1000 outputs
+    # (a partial 128-row tile), against float64 RMSNorm(x) . W^T.
+    n2, k2, m2 = 1000, 200, 3
+    w2 = f32_to_bf16_bits((0.05 * rng.standard_normal((n2, k2))).astype(np.float32))
+    x2 = rng.standard_normal((m2, k2)).astype(np.float32)
+    g2 = (1 + 0.3 * rng.standard_normal(k2)).astype(np.float32)
+    w64 = (w2.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    x64 = x2.astype(np.float64)
+    xn = x64 / np.sqrt((x64 * x64).mean(axis=1, keepdims=True) + 1e-6) * g2.astype(np.float64)
+    want2 = xn @ w64.T
+    w2_t = torch.from_numpy(tile_bf16(w2).view(np.int16)).to(dev)
+    x2_t = torch.from_numpy(x2).to(dev)
+    g2_t = torch.from_numpy(g2).to(dev)
+    y2_t = torch.full((m2, n2), float("nan"), dtype=torch.float32, device=dev)
+    st = L.pp_norm_gemv_static(w2_t.data_ptr(), x2_t.data_ptr(), g2_t.data_ptr(),
+                               ctypes.c_float(1e-6), n2, k2, m2, y2_t.data_ptr(),
+                               err_t.data_ptr(), ctypes.c_void_p(stream))
+    assert st == _lib.PP_OK, _lib.last_error(None)
+    torch.cuda.synchronize(dev)
+    got2 = y2_t.cpu().numpy()
+    assert int(err_t.item()) == 0
+    assert rel_l2(got2, want2) <= 5e-5
+
+    # A non-finite input value is reported in the error word (status bit 2).
+    x2_t[1, 17] = float("inf")
+    st = L.pp_norm_gemv_static(w2_t.data_ptr(), x2_t.data_ptr(), g2_t.data_ptr(),
+                               ctypes.c_float(1e-6), n2, k2, m2, y2_t.data_ptr(),
+                               err_t.data_ptr(), ctypes.c_void_p(stream))
+    assert st == _lib.PP_OK
+    torch.cuda.synchronize(dev)
+    assert int(err_t.item()) & 2
+
     # Sizes past the static scratch are refused with a clear error.
     st = L.pp_norm_gemv_static(w_t.data_ptr(), x_t.data_ptr(), n_t.data_ptr(),
                                ctypes.c_float(1e-6), cfg.vocab_size, cfg.hidden, 9,
-                               y_t.data_ptr(), None)
+                               y_t.data_ptr(), None, None)
     assert st == _lib.PP_E_INVALID and "8" in _lib.last_error(None)
