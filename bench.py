@@ -651,6 +651,47 @@ def _probe_prefill_gemm(argv):
                       "issued_tflops": round(2 * flops / best / 1e9, 1)}))
 
 
+def _probe_verify_pass(argv):
+    """One whole verify pass of a Qwen3-4B shard (seed 3, the workload's target) on one GPU:
+    chunk rows over a seeded cache of --kv positions, the step graph replayed back to back
+    (CUDA events on the shard's stream), against the pass's algorithmic bytes."""
+    import torch
+
+    from potpori_b200.config import QWEN3_4B
+    from potpori_b200.shard import Shard
+    from potpori_b200.workload import verify_pass_bytes
+
+    ap = argparse.ArgumentParser(prog="bench.py --probe verify-pass")
+    ap.add_argument("--kv", type=int, default=2048)
+    ap.add_argument("--rows", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    cfg = QWEN3_4B
+    rng = (0, a.layers)
+    sh = Shard.random(cfg, rng, 4096, 8, seed=3)
+    sh.fill_kv(11, a.kv)
+    toks = list(range(100, 100 + a.rows))
+    st = torch.cuda.ExternalStream(sh.stream())
+    for _ in range(3):
+        sh.set_step(a.kv, a.rows, toks if sh.first else None, stream=sh.stream())
+        sh.step_device(a.rows, sh.stream())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(a.iters):
+        sh.step_device(a.rows, sh.stream())
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    b = verify_pass_bytes(cfg, rng, a.rows, a.kv + a.rows)
+    peak, src = peaks()
+    print(json.dumps({"layers": list(rng), "rows": a.rows, "kv": a.kv, "ms": round(ms, 4),
+                      "bytes": b, "gbs": round(b / ms / 1e6, 1),
+                      "frac": round(b / ms / 1e6 / peak, 4), "peak_source": src}))
+    sh.close()
+
+
 def _probe_layer_sweep(argv):
     """Config 4's single Qwen3-4B layer sweep (potpori_b200.layer_sweep)."""
     from potpori_b200 import layer_sweep
@@ -658,7 +699,8 @@ def _probe_layer_sweep(argv):
 
 
 PROBES = {"draft-step": _probe_draft_step, "prefill-step": _probe_prefill_step,
-          "prefill-gemm": _probe_prefill_gemm, "layer-sweep": _probe_layer_sweep}
+          "prefill-gemm": _probe_prefill_gemm, "layer-sweep": _probe_layer_sweep,
+          "verify-pass": _probe_verify_pass}
 
 
 def main():
