@@ -21,6 +21,13 @@
 //    -> gate/up with the post-attention norm and SwiGLU -> down + residual. After the last
 //    layer the CTAs write the vocabulary head's operand split(x * final_norm) and the
 //    per-128-column sums of squares, which the stream-K head kernel consumes.
+//  * In a GEMV slot the K dimension is split over the eight warps: a lane holds its slice of
+//    the input vector in registers for the whole phase and reads each weight byte once from
+//    shared memory (the weight rows are stored with a per-row swizzle of their 16-byte units,
+//    so the lanes of a warp hit distinct bank groups); the warps' partial sums meet in a small
+//    double-buffered table.
+//  * In the attention a key is eight lanes (16 head dims each): a warp walks four keys at a
+//    time, each lane group with its own running max, sum and output, merged at the end.
 //
 // Arithmetic is the reference's F32 (src/qwen/model.rs:166-183, tiny.rs:20-115): BF16
 // weights decoded exactly to F32, F32 products and sums (packed FFMA2), RMSNorm as
@@ -33,12 +40,29 @@ namespace pp {
 constexpr int kDecSlot = 32768;           // bytes per ring slot
 constexpr int kDecKvHalf = kDecSlot / 2;  // K rows at 0, V rows at 16 KB of a K/V slot
 constexpr uint64_t kDecBarrierNs = 200ull * 1000 * 1000;  // grid barrier time limit
+constexpr int kDecKAlign = 512;           // K of the weight copies: a multiple of 8 warps x 64
+constexpr int kDecHd = 128;               // head size the attention takes
+
+// K of a decode weight copy (zero columns past K).
+__host__ __device__ inline int dec_kpad(int k) { return (k + kDecKAlign - 1) / kDecKAlign * kDecKAlign; }
+// Rows per weight slot for rows of kp columns: the largest power of two <= 16 that fits.
+__host__ __device__ inline int dec_slot_rows(int kp) {
+  int r = 16;
+  while (r > 1 && r * kp * 2 > kDecSlot) r >>= 1;
+  return r;
+}
+// Element offset of (row r, column c) in a decode weight copy of kp columns per row: the
+// 16-byte unit c / 8 of row r sits at (c / 8) ^ (r & 7), inside its 128-byte group, so the
+// lanes reading one unit of eight consecutive rows hit eight different bank groups.
+__host__ __device__ inline int64_t dec_w_offset(int64_t r, int64_t c, int64_t kp) {
+  return r * kp + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7);
+}
 
 struct DecodeLayer {
-  const uint16_t* wqkv;  // [Q + 2 KV][H] row-major BF16 (q rows, k rows, v rows)
-  const uint16_t* wo;    // [H][Q]
-  const uint16_t* wgu;   // [I][2][H]: gate row j then up row j
-  const uint16_t* wd;    // [H][I]
+  const uint16_t* wqkv;  // [Q + 2 KV][kH] (q rows, k rows, v rows), dec_w_offset layout
+  const uint16_t* wo;    // [H][kQ]
+  const uint16_t* wgu;   // [I][2][kH]: gate row j then up row j
+  const uint16_t* wd;    // [H][kI]
   const float* n_attn;
   const float* n_q;
   const float* n_k;
@@ -50,6 +74,7 @@ struct DecodeLayer {
 struct DecodeArgs {
   const DecodeLayer* layers;  // [nl]
   int32_t nl, H, Q, KV, I, hd, nh, nkv, G, V, capacity, embed_kchunks, splits, ss_tiles, nslots;
+  int32_t kH, kQ, kI;  // K of the weight copies (dec_kpad of H, Q, I)
   int32_t vec_floats;  // floats of the staged-vector region
   float eps, inv_scale;
   const uint16_t* embed;    // tiled embedding table (tiled_offset layout)
@@ -67,30 +92,40 @@ struct DecodeArgs {
   StepResult* res;
 };
 
-// Shared memory (from a 1024-aligned base): ring slots | staged vector (xa, xb: float4 units
-// of 8 floats split in halves, or the attention scratch) | own residual rows | reduction |
-// flags | mbarriers.
+// Shared memory (from a 1024-aligned base): ring slots | staged vector (the phase's input,
+// padded, or the attention scratch) | own residual rows | warp partials [rows][8] |
+// reduction | flags | mbarriers.
 struct DecodeSmem {
-  int ns, vec_floats, own;
-  __host__ __device__ DecodeSmem(int ns_, int vf, int own_) : ns(ns_), vec_floats(vf), own(own_) {}
+  int ns, vec_floats, own, prow;
+  __host__ __device__ DecodeSmem(int ns_, int vf, int own_, int prow_)
+      : ns(ns_), vec_floats(vf), own(own_), prow(prow_) {}
   __host__ __device__ size_t vec_off() const { return (size_t)ns * kDecSlot; }
   __host__ __device__ size_t own_off() const { return vec_off() + (size_t)vec_floats * 4; }
-  __host__ __device__ size_t red_off() const { return own_off() + (((size_t)own * 4 + 15) & ~(size_t)15); }
+  __host__ __device__ size_t part_off() const { return own_off() + (((size_t)own * 4 + 15) & ~(size_t)15); }
+  __host__ __device__ size_t red_off() const { return part_off() + (size_t)prow * kConsumerWarps * 4; }
   __host__ __device__ size_t bar_off() const { return red_off() + 64; }
   __host__ __device__ size_t total() const { return bar_off() + 16 * (size_t)ns + 1024; }
 };
 
-// Floats of the staged-vector region: the widest GEMV input (two float4 halves per 8 columns)
-// or the attention scratch (queries, new key and value, per-warp partials).
+// Floats of the staged-vector region: the widest padded GEMV input (a pad of 4 floats per
+// slice, a slice at least 4 units) or the attention scratch (queries, new key and value,
+// per-warp partials; the merge of a head's splits reuses it).
 __host__ __device__ inline int decode_vec_floats(int H, int Q, int I, int hd, int G) {
-  int k = H > Q ? H : Q;
-  k = k > I ? k : I;
+  int k = dec_kpad(H) > dec_kpad(Q) ? dec_kpad(H) : dec_kpad(Q);
+  k = k > dec_kpad(I) ? k : dec_kpad(I);
+  k += k / 8;
   const int att = (G + 2) * hd + kConsumerWarps * G * (hd + 4);
   return k > att ? k : att;
 }
 
 // Balanced contiguous share [lo(b), lo(b+1)) of n items over g CTAs.
 __device__ __forceinline__ int dec_lo(int n, int b, int g) { return (int)((int64_t)n * b / g); }
+
+// Rows of the partial table: the most rows of one GEMV phase a CTA of a g-CTA grid gets.
+__host__ __device__ inline int decode_part_rows(int H, int Q, int KV, int I, int g) {
+  const int a = (Q + 2 * KV + g - 1) / g, b = (2 * I + 2 * g - 1) / g, c = (H + g - 1) / g;
+  return (a > b ? (a > c ? a : c) : (b > c ? b : c)) + 2;
+}
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
@@ -157,10 +192,10 @@ __device__ __forceinline__ DecPlan dec_plan(const DecodeArgs& a, int b, int g, i
     p.pe = p1 < pos ? p1 : pos;
     if (p.pe < p.p0) p.pe = p.p0;
   }
-  p.rps_qkv = kDecSlot / (a.H * 2);
-  p.rps_o = kDecSlot / (a.Q * 2);
-  p.rps_gu = (kDecSlot / (a.H * 2)) & ~1;
-  p.rps_d = kDecSlot / (a.I * 2);
+  p.rps_qkv = dec_slot_rows(a.kH);
+  p.rps_o = dec_slot_rows(a.kQ);
+  p.rps_gu = dec_slot_rows(a.kH);  // an even number: gate/up pairs never straddle two slots
+  p.rps_d = dec_slot_rows(a.kI);
   p.rowb = kv_row_bytes(a.hd);
   p.kvps = kDecKvHalf / p.rowb;
   return p;
@@ -215,64 +250,47 @@ __device__ __forceinline__ void dec_release(DecRing& r, int lane) {
   r.advance();
 }
 
-// Dot products of the `rows` rows of one weight slot (units 16-byte units each) with the
-// staged vector; warp w takes the row pairs (2p, 2p + 1), p = w, w + 8, ..., and lane 0 calls
-// epi(row, value0, has_second, value1).
-template <typename Epi>
-__device__ __forceinline__ void dec_dot_slot(const uint8_t* slot, int rows, int units,
-                                             const float4* xa, const float4* xb, int warp,
-                                             int lane, Epi&& epi) {
-  for (int p = warp; 2 * p < rows; p += kConsumerWarps) {
-    const int r0 = 2 * p;
-    const bool two = r0 + 1 < rows;
-    const uint4* w0 = (const uint4*)(slot + (size_t)r0 * units * 16);
-    const uint4* w1 = w0 + units;
-    float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
-#pragma unroll 4
-    for (int u = lane; u < units; u += 32) {
-      const float4 x0 = xa[u], x1 = xb[u];
-      const uint4 v = w0[u];
-      ffma2(a0, make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x0.x, x0.y));
-      ffma2(a1, make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x0.z, x0.w));
-      ffma2(a0, make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x1.x, x1.y));
-      ffma2(a1, make_float2(bf16lo(v.w), bf16hi(v.w)), make_float2(x1.z, x1.w));
-      if (two) {
-        const uint4 t = w1[u];
-        ffma2(b0, make_float2(bf16lo(t.x), bf16hi(t.x)), make_float2(x0.x, x0.y));
-        ffma2(b1, make_float2(bf16lo(t.y), bf16hi(t.y)), make_float2(x0.z, x0.w));
-        ffma2(b0, make_float2(bf16lo(t.z), bf16hi(t.z)), make_float2(x1.x, x1.y));
-        ffma2(b1, make_float2(bf16lo(t.w), bf16hi(t.w)), make_float2(x1.z, x1.w));
-      }
-    }
-    const float s0 = warp_sum((a0.x + a0.y) + (a1.x + a1.y));
-    const float s1 = two ? warp_sum((b0.x + b0.y) + (b1.x + b1.y)) : 0.f;
-    if (lane == 0) epi(r0, s0, two, s1);
+// A lane's part of one GEMV phase: slots of R rows of kp columns; the lanes of a warp take the
+// rows (lpr = 32 / R lanes per row), and warp w the columns [w kp / 8, (w + 1) kp / 8), of
+// which the lane takes upl consecutive 16-byte units starting at unit u0 (of the whole row).
+struct DecLane {
+  int lpr, upl, row, sub, u0;
+};
+
+__device__ __forceinline__ DecLane dec_lane(int kp, int R, int warp, int lane) {
+  DecLane d;
+  d.lpr = 32 / R;
+  d.upl = (kp >> 6) / d.lpr;
+  d.row = lane / d.lpr;
+  d.sub = lane - d.row * d.lpr;
+  d.u0 = warp * (kp >> 6) + d.sub * d.upl;
+  return d;
+}
+
+// Staged input vectors are padded: 16 bytes after every upl units (8 floats per unit), so the
+// slices that the lanes of one row read at the same time start in different bank groups.
+// Float index of column c (upl units per slice):
+__device__ __forceinline__ int dec_vpad(int c, int upl) { return c + 4 * ((c >> 3) / upl); }
+
+// The lane's slice of the staged input vector, 8 floats per unit, held for the whole phase.
+__device__ __forceinline__ void dec_load_x(const float* vec, const DecLane& d, float4 (&x)[16]) {
+  const float4* v4 = (const float4*)(vec + dec_vpad(8 * d.u0, d.upl));  // a slice is contiguous
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const bool in = t < d.upl;
+    x[2 * t] = in ? v4[2 * t] : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[2 * t + 1] = in ? v4[2 * t + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
-// Consumes one weight segment of `rows` rows; `live` false only releases the slots.
-template <typename Epi>
-__device__ __forceinline__ bool dec_rows(DecRing& r, bool live, int rows, int rowbytes, int rps,
-                                         const float4* xa, const float4* xb, int warp, int lane,
-                                         Epi&& epi) {
-  for (int i = 0; i < rows; i += rps) {
-    const int n = rows - i < rps ? rows - i : rps;
-    if (!dec_take(r)) return false;
-    if (live)
-      dec_dot_slot(r.cur(), n, rowbytes >> 4, xa, xb, warp, lane,
-                   [&](int rr, float s0, bool two, float s1) { epi(i + rr, s0, two, s1); });
-    dec_release(r, lane);
-  }
-  return true;
-}
-
-// Stages K floats of src (times w when given) into the unit-split vector; returns the sum of
-// squares of src, reduced in the same order in every CTA.
-__device__ __forceinline__ float dec_stage_vec(const float* src, const float* w, int K, float4* xa,
-                                               float4* xb, float* red, int tid) {
+// Stages K floats of src (times w when given) into vec in the padded layout of kp columns in
+// slices of upl units (zeros past K); returns the sum of squares of src, reduced in the same
+// order in every CTA.
+__device__ __forceinline__ float dec_stage_vec(const float* src, const float* w, int K, int kp,
+                                               int upl, float* vec, float* red, int tid) {
   constexpr int T = kConsumerWarps * 32, B = 4;  // float4s per thread per batch of loads
   float ss = 0.f;
-  for (int q0 = 0; q0 < (K >> 2); q0 += B * T) {
+  for (int q0 = 0; q0 < (kp >> 2); q0 += B * T) {
     float4 v[B], ww[B];
 #pragma unroll
     for (int k = 0; k < B; ++k) {  // every load of the batch in flight together
@@ -284,7 +302,7 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* w,
 #pragma unroll
     for (int k = 0; k < B; ++k) {
       const int q = q0 + tid + k * T;
-      if (q < (K >> 2)) {
+      if (q < (kp >> 2)) {
         float4 x = v[k];
         ss += (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
         if (w) {
@@ -293,7 +311,7 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* w,
           x.z *= ww[k].z;
           x.w *= ww[k].w;
         }
-        ((q & 1) ? xb : xa)[q >> 1] = x;
+        *(float4*)(vec + dec_vpad(4 * q, upl)) = x;
       }
     }
   }
@@ -305,6 +323,65 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* w,
   for (int i = 0; i < kConsumerWarps; ++i) t += red[i];
   consumer_sync();  // red is free again
   return t;
+}
+
+// One slot of a GEMV phase: rows [i, i + n) of the phase, whose first row is row g0 of the
+// weight copy (the key of its unit swizzle). Each lane dots its units of its row, the lanes of
+// a row are summed, and the warp's sum of row i + j goes to part[(i + j) * 8 + warp].
+__device__ __forceinline__ void dec_slot(const uint8_t* slot, int n, int i, int g0, int kp,
+                                         const DecLane& d, const float4 (&x)[16], float* part,
+                                         int warp) {
+  const bool mine = d.row < n;
+  const int rr = mine ? d.row : 0;  // a lane without a row reads row 0 and drops the sum
+  const uint8_t* row = slot + (size_t)rr * kp * 2;
+  const int key = (g0 + i + rr) & 7;
+  float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if (t < d.upl) {
+      const uint4 v = *(const uint4*)(row + (((d.u0 + t) ^ key) << 4));
+      ffma2(a0, make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x[2 * t].x, x[2 * t].y));
+      ffma2(a1, make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x[2 * t].z, x[2 * t].w));
+      ffma2(a0, make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x[2 * t + 1].x, x[2 * t + 1].y));
+      ffma2(a1, make_float2(bf16lo(v.w), bf16hi(v.w)), make_float2(x[2 * t + 1].z, x[2 * t + 1].w));
+    }
+  }
+  float s = (a0.x + a0.y) + (a1.x + a1.y);
+  for (int o = d.lpr >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (mine && d.sub == 0) part[(i + d.row) * kConsumerWarps + warp] = s;
+}
+
+// Consumes one weight segment of `rows` rows (from row g0 of the weight copy) in slots of R,
+// then sums the warps' partials of every row (in warp order) and runs epi(row, value, -) for
+// every row — or, with pairs, epi(row, gate, up) for each gate/up pair (row, row + 1) — one
+// row per thread. `live` false only releases the slots.
+// `x` holds the lane's slice of the phase's input (dec_load_x), and `part` room for rows x 8
+// floats.
+template <typename Epi>
+__device__ __forceinline__ bool dec_rows(DecRing& r, bool live, int rows, int g0, int kp, int R,
+                                         const DecLane& d, const float4 (&x)[16], float* part,
+                                         int warp, int lane, int tid, bool pairs, Epi&& epi) {
+  for (int i = 0; i < rows; i += R) {
+    const int n = rows - i < R ? rows - i : R;
+    if (!dec_take(r)) return false;
+    if (live) dec_slot(r.cur(), n, i, g0, kp, d, x, part, warp);
+    dec_release(r, lane);  // this warp's reads of the slot are done (the sums depend on them)
+  }
+  if (!live) return true;
+  consumer_sync();
+  const int outs = pairs ? rows >> 1 : rows;
+  for (int t = tid; t < outs; t += kConsumerWarps * 32) {
+    const float4* p = (const float4*)(part + (size_t)(pairs ? 2 * t : t) * kConsumerWarps);
+    const float4 a0 = p[0], a1 = p[1];
+    const float v0 = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
+    float v1 = 0.f;
+    if (pairs) {
+      const float4 b0 = p[2], b1 = p[3];
+      v1 = ((b0.x + b0.y) + (b0.z + b0.w)) + ((b1.x + b1.y) + (b1.z + b1.w));
+    }
+    epi(pairs ? 2 * t : t, v0, v1);
+  }
+  return true;
 }
 
 // Grid barrier among the consumers of all CTAs (the producers never wait on it): barrier
@@ -337,17 +414,61 @@ __device__ __forceinline__ bool dec_grid_sync(const DecodeArgs& a, uint32_t targ
   return *flag != 0;
 }
 
+// Online-softmax state of one lane group over its keys for G query heads: running max and
+// sum, and the unnormalised output on the lane's 16 head dims.
+template <int G>
+struct DecAttnState {
+  float m[G], l[G], o[G][16];
+};
+
+// One key for the lane's group: k/v are the lane's 16 dims, q its 16 dims of each query head;
+// the eight lanes of the group hold the rest. `valid` false: the state does not change (the
+// lanes still take part in the group's shuffles).
+template <int G>
+__device__ __forceinline__ void dec_attn_key(DecAttnState<G>& st, const float (&q)[G][16],
+                                             const float (&k)[16], const float (&v)[16], bool valid,
+                                             float inv_scale) {
+  float sc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int e = 0; e < 16; e += 2)
+      ffma2(acc, make_float2(q[g][e], q[g][e + 1]), make_float2(k[e], k[e + 1]));
+    sc[g] = acc.x + acc.y;
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+    for (int g = 0; g < G; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+  if (!valid) return;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float s = sc[g] * inv_scale;
+    const float mn = fmaxf(st.m[g], s);
+    const float al = __expf(st.m[g] - mn);  // 0 for the first key (m = -inf)
+    const float p = __expf(s - mn);
+    st.l[g] = st.l[g] * al + p;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) st.o[g][e] = st.o[g][e] * al + p * v[e];
+    st.m[g] = mn;
+  }
+}
+
 // Attention unit (KV head h, split s) for the single query position pos: QK-RMSNorm + RoPE
 // of the G query heads and of the new key (tiny.rs:24-37), the new K/V row written by the
 // unit that holds pos, online softmax over the streamed cached rows (tiny.rs:77-101), the
 // unit's partial (max, sum, output) per query head, and the merge of the head's splits by
-// the last unit to finish.
+// the last unit to finish. A key is taken by eight lanes: lane group kg = lane / 8 of warp w
+// takes the keys 4 w + kg of each 32-key slot, lane q8 = lane % 8 the head dims of 16-byte
+// units q8 and q8 + 8 (dims 8 q8 .. 8 q8 + 7 and 64 + 8 q8 .. 64 + 8 q8 + 7).
 template <int G>  // query heads per KV head (a.G)
 __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeLayer& L,
                                               const DecPlan& P, DecRing& r, bool live, int pos,
                                               int layer, float* vec, int* flag, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
-  const int hd = a.hd, half = hd >> 1, h = P.h;
+  constexpr int hd = kDecHd, half = hd / 2;
+  const int h = P.h;
   float* qs = vec;             // [G][hd]
   float* kn = qs + G * hd;     // [hd]
   float* vn = kn + hd;         // [hd]
@@ -362,18 +483,17 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
       const float* w = isq ? L.n_q : L.n_k;
       const float2* rp = a.rope + (size_t)pos * half;
       // One batch of loads per lane: its raw values, norm weights and (cos, sin) pairs for
-      // dims i and i + half, i = lane + 32 t (head_dim <= 128).
+      // dims i and i + half, i = lane + 32 t.
       float x0[2], x1[2], w0[2], w1[2];
       float2 cs[2];
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int i = lane + 32 * t;
-        const bool in = i < half;
-        x0[t] = in ? __ldcg(src + i) : 0.f;
-        x1[t] = in ? __ldcg(src + i + half) : 0.f;
-        w0[t] = in ? w[i] : 0.f;
-        w1[t] = in ? w[i + half] : 0.f;
-        cs[t] = in ? rp[i] : make_float2(0.f, 0.f);
+        x0[t] = __ldcg(src + i);
+        x1[t] = __ldcg(src + i + half);
+        w0[t] = w[i];
+        w1[t] = w[i + half];
+        cs[t] = rp[i];
       }
       const float ssq = warp_sum((x0[0] * x0[0] + x1[0] * x1[0]) + (x0[1] * x0[1] + x1[1] * x1[1]));
       const float rms = sqrtf(ssq / (float)hd + a.eps);
@@ -381,11 +501,9 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int i = lane + 32 * t;
-        if (i < half) {
-          const float y0 = x0[t] / rms * w0[t], y1 = x1[t] / rms * w1[t];
-          dst[i] = y0 * cs[t].x - y1 * cs[t].y;
-          dst[i + half] = y1 * cs[t].x + y0 * cs[t].y;
-        }
+        const float y0 = x0[t] / rms * w0[t], y1 = x1[t] / rms * w1[t];
+        dst[i] = y0 * cs[t].x - y1 * cs[t].y;
+        dst[i + half] = y1 * cs[t].x + y0 * cs[t].y;
       }
     }
     if (P.has_new && tid < hd) vn[tid] = vnew;
@@ -398,75 +516,38 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
       }
     }
   }
-  // Lane l holds dims 4l..4l+3 of every query head and of the running outputs.
-  const bool act = 4 * lane < hd;
-  const int d0 = 4 * lane;
-  float q[G][4], o[G][4], m[G], l[G];
+  const int kg = lane >> 3, q8 = lane & 7;
+  // The lane's dims of every query head, and the group's state.
+  float q[G][16];
+  DecAttnState<G> st;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+    st.m[g] = -INFINITY;
+    st.l[g] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      o[g][j] = 0.f;
-      q[g][j] = (live && act) ? qs[g * hd + d0 + j] : 0.f;
+    for (int e = 0; e < 16; ++e) {
+      st.o[g][e] = 0.f;
+      const int d = (e < 8 ? 8 * q8 : half + 8 * q8) + (e & 7);
+      q[g][e] = live ? qs[g * hd + d] : 0.f;
     }
   }
-  // Online softmax over one or two keys (B valid when vb): the dot products of both keys are
-  // reduced together so their shuffle chains overlap, then the state takes A, then B.
-  auto visit2 = [&](const float (&ka)[4], const float (&va)[4], bool vb, const float (&kb)[4],
-                    const float (&vb4)[4]) {
-    float sa[G], sb[G];
+  // The lane's 16 dims of one cache row j (hi + lo parts, kv_offset layout).
+  auto load_row = [&](const uint8_t* row, int j, float (&out)[16]) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      sa[g] = (q[g][0] * ka[0] + q[g][1] * ka[1]) + (q[g][2] * ka[2] + q[g][3] * ka[3]);
-      sb[g] = (q[g][0] * kb[0] + q[g][1] * kb[1]) + (q[g][2] * kb[2] + q[g][3] * kb[3]);
+    for (int hu = 0; hu < 2; ++hu) {
+      const int u = (q8 + 8 * hu) ^ (j & 7);
+      const uint4 hi = *(const uint4*)(row + (u << 4));
+      const uint4 lo = *(const uint4*)(row + 2 * hd + (u << 4));
+      float* o = out + 8 * hu;
+      o[0] = bf16lo(hi.x) + bf16lo(lo.x);
+      o[1] = bf16hi(hi.x) + bf16hi(lo.x);
+      o[2] = bf16lo(hi.y) + bf16lo(lo.y);
+      o[3] = bf16hi(hi.y) + bf16hi(lo.y);
+      o[4] = bf16lo(hi.z) + bf16lo(lo.z);
+      o[5] = bf16hi(hi.z) + bf16hi(lo.z);
+      o[6] = bf16lo(hi.w) + bf16lo(lo.w);
+      o[7] = bf16hi(hi.w) + bf16hi(lo.w);
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        sa[g] += __shfl_xor_sync(0xffffffffu, sa[g], off);
-        sb[g] += __shfl_xor_sync(0xffffffffu, sb[g], off);
-      }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float sc = sa[g] * a.inv_scale;
-      float mn = fmaxf(m[g], sc);
-      float al = __expf(m[g] - mn);  // 0 for the first key (m = -inf)
-      float pr = __expf(sc - mn);
-      l[g] = l[g] * al + pr;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[g][j] = o[g][j] * al + pr * va[j];
-      m[g] = mn;
-      if (vb) {
-        sc = sb[g] * a.inv_scale;
-        mn = fmaxf(m[g], sc);
-        al = __expf(m[g] - mn);
-        pr = __expf(sc - mn);
-        l[g] = l[g] * al + pr;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[g][j] = o[g][j] * al + pr * vb4[j];
-        m[g] = mn;
-      }
-    }
-  };
-  auto load_kv = [&](const uint8_t* ks, const uint8_t* vs, int i, int j, float (&k)[4],
-                     float (&v)[4]) {
-    const uint8_t* kr = ks + (size_t)i * P.rowb;
-    const uint8_t* vr = vs + (size_t)i * P.rowb;
-    const uint2 kh = *(const uint2*)(kr + kv_offset(j, d0, 0, hd));
-    const uint2 kl = *(const uint2*)(kr + kv_offset(j, d0, 1, hd));
-    const uint2 vh = *(const uint2*)(vr + kv_offset(j, d0, 0, hd));
-    const uint2 vl = *(const uint2*)(vr + kv_offset(j, d0, 1, hd));
-    k[0] = bf16lo(kh.x) + bf16lo(kl.x);
-    k[1] = bf16hi(kh.x) + bf16hi(kl.x);
-    k[2] = bf16lo(kh.y) + bf16lo(kl.y);
-    k[3] = bf16hi(kh.y) + bf16hi(kl.y);
-    v[0] = bf16lo(vh.x) + bf16lo(vl.x);
-    v[1] = bf16hi(vh.x) + bf16hi(vl.x);
-    v[2] = bf16lo(vh.y) + bf16lo(vl.y);
-    v[3] = bf16hi(vh.y) + bf16hi(vl.y);
   };
   const int npos = P.pe - P.p0;
   for (int i0 = 0; i0 < npos; i0 += P.kvps) {
@@ -475,43 +556,62 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
     if (live) {
       const uint8_t* ks = r.cur();
       const uint8_t* vs = ks + kDecKvHalf;
-      for (int i = warp; i < n; i += 2 * kConsumerWarps) {
-        const int ib = i + kConsumerWarps;
-        const bool vb = ib < n;
-        float ka[4] = {0.f, 0.f, 0.f, 0.f}, va[4] = {0.f, 0.f, 0.f, 0.f};
-        float kb[4] = {0.f, 0.f, 0.f, 0.f}, vbv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (act) {
-          load_kv(ks, vs, i, P.p0 + i0 + i, ka, va);
-          if (vb) load_kv(ks, vs, ib, P.p0 + i0 + ib, kb, vbv);
-        }
-        visit2(ka, va, vb, kb, vbv);
+      for (int kk = 4 * warp + kg; kk - kg < n; kk += 4 * kConsumerWarps) {
+        const bool valid = kk < n;
+        const int ki = valid ? kk : 0;
+        const int j = P.p0 + i0 + ki;  // absolute position (the swizzle key)
+        float k[16], v[16];
+        load_row(ks + (size_t)ki * P.rowb, j, k);
+        load_row(vs + (size_t)ki * P.rowb, j, v);
+        dec_attn_key<G>(st, q, k, v, valid, a.inv_scale);
       }
     }
     dec_release(r, lane);
   }
   if (!live) return true;
-  if (P.has_new && warp == (npos % kConsumerWarps)) {
-    float k[4] = {0.f, 0.f, 0.f, 0.f}, v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (act)
+  if (P.has_new && warp == 0) {
+    // The step's own key and value (F32, from the prologue), taken by lane group 0.
+    float k[16], v[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        k[j] = kn[d0 + j];
-        v[j] = vn[d0 + j];
-      }
-    visit2(k, v, false, k, v);
-  }
-  // Merge the warps' partials: thread t handles (head g, dim d) of the unit's record.
-  const int stride = hd + 4;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float* mw = mrg + (size_t)(warp * G + g) * stride;
-    if (lane == 0) {
-      mw[0] = m[g];
-      mw[1] = l[g];
+    for (int e = 0; e < 16; ++e) {
+      const int d = (e < 8 ? 8 * q8 : half + 8 * q8) + (e & 7);
+      k[e] = kn[d];
+      v[e] = vn[d];
     }
-    if (act)
+    dec_attn_key<G>(st, q, k, v, kg == 0, a.inv_scale);
+  }
+  // Merge the four lane groups of the warp (lanes q8, q8 + 8, q8 + 16, q8 + 24 hold the same
+  // dims), then the warps' partials in shared memory.
 #pragma unroll
-      for (int j = 0; j < 4; ++j) mw[4 + d0 + j] = o[g][j];
+  for (int o = 8; o < 32; o <<= 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mo = __shfl_xor_sync(0xffffffffu, st.m[g], o);
+      const float lo = __shfl_xor_sync(0xffffffffu, st.l[g], o);
+      const float M = fmaxf(st.m[g], mo);
+      const float fa = st.m[g] == -INFINITY ? 0.f : __expf(st.m[g] - M);
+      const float fb = mo == -INFINITY ? 0.f : __expf(mo - M);
+      st.l[g] = st.l[g] * fa + lo * fb;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float oo = __shfl_xor_sync(0xffffffffu, st.o[g][e], o);
+        st.o[g][e] = st.o[g][e] * fa + oo * fb;
+      }
+      st.m[g] = M;
+    }
+  }
+  const int stride = hd + 4;
+  if (kg == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float* mw = mrg + (size_t)(warp * G + g) * stride;
+      if (q8 == 0) {
+        mw[0] = st.m[g];
+        mw[1] = st.l[g];
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) mw[4 + (e < 8 ? 8 * q8 : half + 8 * q8) + (e & 7)] = st.o[g][e];
+    }
   }
   consumer_sync();
   const int S = a.splits;
@@ -588,7 +688,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   const int NG = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int own_cap = (a.H + NG - 1) / NG + 1;
-  const DecodeSmem lay(a.nslots, a.vec_floats, own_cap);
+  const DecodeSmem lay(a.nslots, a.vec_floats, own_cap, decode_part_rows(a.H, a.Q, a.KV, a.I, NG));
   DecRing r;
   r.base = smem;
   r.full = (uint64_t*)(smem + lay.bar_off());
@@ -598,9 +698,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   r.phase = 0;
   r.n = 0;
   float* vec = (float*)(smem + lay.vec_off());
-  float4* xa = (float4*)vec;
-  float4* xb = xa + (a.vec_floats >> 3);
   float* xown = (float*)(smem + lay.own_off());
+  float* part = (float*)(smem + lay.part_off());
   float* red = (float*)(smem + lay.red_off());
   int* flag = (int*)(red + kConsumerWarps);
 
@@ -623,14 +722,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
     bool ok = true;
     for (int l = 0; l < a.nl && ok; ++l) {
       const DecodeLayer& L = a.layers[l];
-      ok = dec_issue_rows(r, L.wqkv + (size_t)P.q0 * a.H, P.q1 - P.q0, a.H * 2, P.rps_qkv);
+      ok = dec_issue_rows(r, L.wqkv + (size_t)P.q0 * a.kH, P.q1 - P.q0, a.kH * 2, P.rps_qkv);
       if (ok && P.h >= 0) {
         const size_t off = ((size_t)P.h * a.capacity + P.p0) * P.rowb;
         ok = dec_issue_kv(r, L.kc + off, L.vc + off, P.pe - P.p0, P.rowb, P.kvps);
       }
-      ok = ok && dec_issue_rows(r, L.wo + (size_t)P.o0 * a.Q, P.o1 - P.o0, a.Q * 2, P.rps_o);
-      ok = ok && dec_issue_rows(r, L.wgu + (size_t)2 * P.j0 * a.H, 2 * (P.j1 - P.j0), a.H * 2, P.rps_gu);
-      ok = ok && dec_issue_rows(r, L.wd + (size_t)P.o0 * a.I, P.o1 - P.o0, a.I * 2, P.rps_d);
+      ok = ok && dec_issue_rows(r, L.wo + (size_t)P.o0 * a.kQ, P.o1 - P.o0, a.kQ * 2, P.rps_o);
+      ok = ok && dec_issue_rows(r, L.wgu + (size_t)2 * P.j0 * a.kH, 2 * (P.j1 - P.j0), a.kH * 2, P.rps_gu);
+      ok = ok && dec_issue_rows(r, L.wd + (size_t)P.o0 * a.kI, P.o1 - P.o0, a.kI * 2, P.rps_d);
     }
     if (!ok) {
       atomicOr(&a.res->status, ST_TIMEOUT);
@@ -644,113 +743,92 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   }
 
   // ------------------------------------------------------------------ consumer warps
+  // The four GEMV phases of a layer run through one copy of the GEMV code (a loop over the
+  // phase; the epilogue switches on it), so the per-layer code stays in the instruction cache:
+  // 0 QKV with the input RMSNorm, then the attention; 1 O + residual; 2 gate/up with the
+  // post-attention RMSNorm and SwiGLU; 3 down + residual.
   bool live = true, lost = false;  // lost: a ring slot never landed
   uint32_t nb = 0;
   for (int l = 0; l < a.nl && !lost; ++l) {
     const DecodeLayer& L = a.layers[l];
-    // QKV with the input RMSNorm; layer 0 gathers the token's embedding row
-    // (src/qwen/model.rs:239-241).
-    float rinv = 0.f;
-    if (live) {
-      float ss;
-      if (l == 0) {
-        float t = 0.f;
-        for (int q = tid; q < (a.H >> 2); q += kConsumerWarps * 32) {
-          float4 v;
-          v.x = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 0, a.embed_kchunks)] << 16);
-          v.y = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 1, a.embed_kchunks)] << 16);
-          v.z = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 2, a.embed_kchunks)] << 16);
-          v.w = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 3, a.embed_kchunks)] << 16);
-          const int n0 = 4 * q;
-          if (n0 + 3 >= P.o0 && n0 < P.o1) {
-            if (n0 + 0 >= P.o0 && n0 + 0 < P.o1) xown[n0 + 0 - P.o0] = v.x;
-            if (n0 + 1 >= P.o0 && n0 + 1 < P.o1) xown[n0 + 1 - P.o0] = v.y;
-            if (n0 + 2 >= P.o0 && n0 + 2 < P.o1) xown[n0 + 2 - P.o0] = v.z;
-            if (n0 + 3 >= P.o0 && n0 + 3 < P.o1) xown[n0 + 3 - P.o0] = v.w;
+#pragma unroll 1
+    for (int ph = 0; ph < 4 && !lost; ++ph) {
+      const int kp = ph == 1 ? a.kQ : ph == 3 ? a.kI : a.kH;
+      const int R = ph == 0 ? P.rps_qkv : ph == 1 ? P.rps_o : ph == 2 ? P.rps_gu : P.rps_d;
+      const DecLane d = dec_lane(kp, R, warp, lane);
+      float rinv = 1.f;
+      if (live) {
+        float ss;
+        if (ph == 0 && l == 0) {
+          // The token's embedding row (src/qwen/model.rs:239-241), also the first residual.
+          float t = 0.f;
+          for (int q = tid; q < (kp >> 2); q += kConsumerWarps * 32) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (q < (a.H >> 2)) {
+              v.x = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 0, a.embed_kchunks)] << 16);
+              v.y = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 1, a.embed_kchunks)] << 16);
+              v.z = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 2, a.embed_kchunks)] << 16);
+              v.w = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 3, a.embed_kchunks)] << 16);
+              const int n0 = 4 * q;
+              if (n0 + 3 >= P.o0 && n0 < P.o1) {
+                if (n0 + 0 >= P.o0 && n0 + 0 < P.o1) xown[n0 + 0 - P.o0] = v.x;
+                if (n0 + 1 >= P.o0 && n0 + 1 < P.o1) xown[n0 + 1 - P.o0] = v.y;
+                if (n0 + 2 >= P.o0 && n0 + 2 < P.o1) xown[n0 + 2 - P.o0] = v.z;
+                if (n0 + 3 >= P.o0 && n0 + 3 < P.o1) xown[n0 + 3 - P.o0] = v.w;
+              }
+              t += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+              const float4 ww = ((const float4*)L.n_attn)[q];
+              v.x *= ww.x;
+              v.y *= ww.y;
+              v.z *= ww.z;
+              v.w *= ww.w;
+            }
+            *(float4*)(vec + dec_vpad(4 * q, d.upl)) = v;
           }
-          t += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-          const float4 ww = ((const float4*)L.n_attn)[q];
-          v.x *= ww.x;
-          v.y *= ww.y;
-          v.z *= ww.z;
-          v.w *= ww.w;
-          ((q & 1) ? xb : xa)[q >> 1] = v;
-        }
-        t = warp_sum(t);
-        if (lane == 0) red[warp] = t;
-        consumer_sync();
-        ss = 0.f;
+          t = warp_sum(t);
+          if (lane == 0) red[warp] = t;
+          consumer_sync();
+          ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < kConsumerWarps; ++i) ss += red[i];
-        consumer_sync();
-      } else {
-        ss = dec_stage_vec(a.x, L.n_attn, a.H, xa, xb, red, tid);
+          for (int i = 0; i < kConsumerWarps; ++i) ss += red[i];
+          consumer_sync();
+        } else {
+          const float* src = ph == 1 ? a.attn : ph == 3 ? a.act : a.x;
+          const float* w = ph == 0 ? L.n_attn : ph == 2 ? L.n_ffn : nullptr;
+          const int K = ph == 1 ? a.Q : ph == 3 ? a.I : a.H;
+          ss = dec_stage_vec(src, w, K, kp, d.upl, vec, red, tid);
+        }
+        if (ph == 0 || ph == 2) rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
-      rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+      float4 x[16];
+      dec_load_x(vec, d, x);
+      const int rows = ph == 0 ? P.q1 - P.q0 : ph == 2 ? 2 * (P.j1 - P.j0) : P.o1 - P.o0;
+      const int g0 = ph == 0 ? P.q0 : ph == 2 ? 2 * P.j0 : P.o0;
+      if (!dec_rows(r, live, rows, g0, kp, R, d, x, part, warp, lane, tid, ph == 2,
+                    [&](int rr, float v0, float v1) {
+                      if (ph == 0) {
+                        a.qkv[P.q0 + rr] = v0 * rinv;
+                      } else if (ph == 2) {  // tiny.rs:111-115
+                        const float g = v0 * rinv, u = v1 * rinv;
+                        a.act[P.j0 + (rr >> 1)] = g / (1.0f + expf(-g)) * u;
+                      } else {  // O and down add to the residual (src/qwen/model.rs:304-306)
+                        const float v = xown[rr] + v0;
+                        xown[rr] = v;
+                        a.x[P.o0 + rr] = v;
+                      }
+                    })) {
+        lost = true;
+        break;
+      }
+      live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+      if (ph == 0) {
+        if (P.h >= 0 && !dec_attention<G>(a, L, P, r, live, pos, l, vec, flag, tid)) {
+          lost = true;
+          break;
+        }
+        live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+      }
     }
-    if (!dec_rows(r, live, P.q1 - P.q0, a.H * 2, P.rps_qkv, xa, xb, warp, lane,
-                  [&](int rr, float s0, bool two, float s1) {
-                    a.qkv[P.q0 + rr] = s0 * rinv;
-                    if (two) a.qkv[P.q0 + rr + 1] = s1 * rinv;
-                  })) {
-      lost = true;
-      break;
-    }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
-    // Attention.
-    if (P.h >= 0 && !dec_attention<G>(a, L, P, r, live, pos, l, vec, flag, tid)) {
-      lost = true;
-      break;
-    }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
-    // O projection + residual (src/qwen/model.rs:304-306).
-    if (live) dec_stage_vec(a.attn, nullptr, a.Q, xa, xb, red, tid);
-    if (!dec_rows(r, live, P.o1 - P.o0, a.Q * 2, P.rps_o, xa, xb, warp, lane,
-                  [&](int rr, float s0, bool two, float s1) {
-                    float v = xown[rr] + s0;
-                    xown[rr] = v;
-                    a.x[P.o0 + rr] = v;
-                    if (two) {
-                      v = xown[rr + 1] + s1;
-                      xown[rr + 1] = v;
-                      a.x[P.o0 + rr + 1] = v;
-                    }
-                  })) {
-      lost = true;
-      break;
-    }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
-    // gate/up with the post-attention RMSNorm, SwiGLU (tiny.rs:111-115).
-    if (live) {
-      const float ss = dec_stage_vec(a.x, L.n_ffn, a.H, xa, xb, red, tid);
-      rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
-    }
-    if (!dec_rows(r, live, 2 * (P.j1 - P.j0), a.H * 2, P.rps_gu, xa, xb, warp, lane,
-                  [&](int rr, float s0, bool, float s1) {
-                    const float g = s0 * rinv, u = s1 * rinv;
-                    a.act[P.j0 + (rr >> 1)] = g / (1.0f + expf(-g)) * u;
-                  })) {
-      lost = true;
-      break;
-    }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
-    // down + residual.
-    if (live) dec_stage_vec(a.act, nullptr, a.I, xa, xb, red, tid);
-    if (!dec_rows(r, live, P.o1 - P.o0, a.I * 2, P.rps_d, xa, xb, warp, lane,
-                  [&](int rr, float s0, bool two, float s1) {
-                    float v = xown[rr] + s0;
-                    xown[rr] = v;
-                    a.x[P.o0 + rr] = v;
-                    if (two) {
-                      v = xown[rr + 1] + s1;
-                      xown[rr + 1] = v;
-                      a.x[P.o0 + rr + 1] = v;
-                    }
-                  })) {
-      lost = true;
-      break;
-    }
-    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
   }
   if (lost) {
     if (tid == 0) {
@@ -777,21 +855,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   }
 }
 
-// Row-major copies of the packed weights for the decode kernel: dst[r][c] = W[row(r)][c]
-// with row(r) = r (QKV, O, down) or, for the gate/up pairs (mode 1), gate row r/2 or up row
-// r/2 of the 64-row interleaved blocks.
+// Decode weight copies of the packed weights: dst row r of kp columns (dec_w_offset layout,
+// zero past `cols`) = W[row(r)] with row(r) = r (QKV, O, down) or, for the gate/up pairs
+// (mode 1), gate row r/2 or up row r/2 of the 64-row interleaved blocks.
 __global__ void pp_untile_rows_kernel(uint16_t* dst, const uint16_t* src, int64_t rows, int64_t cols,
-                                   int64_t kchunks, int32_t mode) {
-  const int64_t n = rows * cols;
+                                      int64_t kp, int64_t kchunks, int32_t mode) {
+  const int64_t n = rows * kp;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t r = i / kp, c = i - r * kp;
     int64_t pr = r;
     if (mode == 1) {
       const int64_t j = r >> 1;
       pr = (j / (kTileRows / 2)) * kTileRows + (j % (kTileRows / 2)) + (r & 1) * (kTileRows / 2);
     }
-    dst[i] = src[tiled_offset(pr, c, kchunks)];
+    dst[dec_w_offset(r, c, kp)] = c < cols ? src[tiled_offset(pr, c, kchunks)] : (uint16_t)0;
   }
 }
 

@@ -547,12 +547,13 @@ pp_status decode_alloc(pp_shard* s) {
   const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
   s->dec_w.assign((size_t)s->nl * 4, nullptr);
   std::vector<DecodeLayer> tab(s->nl);
+  const int64_t kH = dec_kpad(s->H), kQ = dec_kpad(s->Q), kI = dec_kpad(s->I);
   for (int l = 0; l < s->nl; ++l) {
     uint16_t** w = &s->dec_w[(size_t)l * 4];
-    if ((r = dalloc(s, &w[0], (size_t)(Q + 2 * KV) * H * 2))) return r;
-    if ((r = dalloc(s, &w[1], (size_t)H * Q * 2))) return r;
-    if ((r = dalloc(s, &w[2], (size_t)2 * I * H * 2))) return r;
-    if ((r = dalloc(s, &w[3], (size_t)H * I * 2))) return r;
+    if ((r = dalloc(s, &w[0], (size_t)(Q + 2 * KV) * kH * 2))) return r;
+    if ((r = dalloc(s, &w[1], (size_t)H * kQ * 2))) return r;
+    if ((r = dalloc(s, &w[2], (size_t)2 * I * kH * 2))) return r;
+    if ((r = dalloc(s, &w[3], (size_t)H * kI * 2))) return r;
     const LayerDev& Ld = s->L[l];
     tab[l] = DecodeLayer{w[0], w[1], w[2], w[3], Ld.norm[N_ATTN], Ld.norm[N_QN], Ld.norm[N_KN],
                          Ld.norm[N_FFN], Ld.kc, Ld.vc};
@@ -573,13 +574,14 @@ pp_status decode_alloc(pp_shard* s) {
 // Row-major copies of the packed weights (after any weight upload).
 pp_status decode_rebuild(pp_shard* s) {
   const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
+  const int64_t kH = dec_kpad(s->H), kQ = dec_kpad(s->Q), kI = dec_kpad(s->I);
   for (int l = 0; l < s->nl; ++l) {
     uint16_t** w = &s->dec_w[(size_t)l * 4];
     const LayerDev& Ld = s->L[l];
-    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, s->Hp / kChunkK, 0);
-    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, s->Qp / kChunkK, 0);
-    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, s->Hp / kChunkK, 1);
-    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, s->Ip / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, kH, s->Hp / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, kQ, s->Qp / kChunkK, 0);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, kH, s->Hp / kChunkK, 1);
+    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, kI, s->Ip / kChunkK, 0);
     CK(cudaGetLastError());
   }
   CK(cudaStreamSynchronize(s->stream));
@@ -614,6 +616,9 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   a.splits = grid / s->nkv;
   a.ss_tiles = s->ss_tiles;
   a.nslots = s->dec_ns;
+  a.kH = dec_kpad(s->H);
+  a.kQ = dec_kpad(s->Q);
+  a.kI = dec_kpad(s->I);
   a.vec_floats = s->dec_vec;
   a.eps = s->d.cfg.rms_norm_eps;
   a.inv_scale = 1.0f / sqrtf((float)s->hd);
@@ -633,18 +638,19 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGemvThreads);
-  cfg.dynamicSmemBytes = DecodeSmem(s->dec_ns, s->dec_vec, decode_own_cap(s, grid)).total();
+  cfg.dynamicSmemBytes =
+      DecodeSmem(s->dec_ns, s->dec_vec, decode_own_cap(s, grid),
+                 decode_part_rows(s->H, s->Q, s->KV, s->I, grid)).total();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: they meet at grid barriers
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  switch (s->G) {  // set_decode_kernel admits 1, 2, 4 or 8 query heads per KV head
+  switch (s->G) {  // set_decode_kernel admits 1, 2 or 4 query heads per KV head
     case 1: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<1>, a)); break;
     case 2: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<2>, a)); break;
-    case 4: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<4>, a)); break;
-    default: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<8>, a)); break;
+    default: CK(cudaLaunchKernelEx(&cfg, pp_decode_step_kernel<4>, a)); break;
   }
   if ((r = after_launch(s, st, PP_K_DECODE))) return r;
   return launch_head<1>(s, st);
@@ -769,7 +775,7 @@ pp_status set_attrs(pp_shard* s) {
   if ((r = set_attrs_mt<1>(s)) || (r = set_attrs_mt<2>(s)) || (r = set_attrs_mt<4>(s)) ||
       (r = set_attrs_mt<8>(s)) || (r = set_attrs_mt<16>(s)) ||
       (r = set_max_smem(s, pp_decode_step_kernel<1>)) || (r = set_max_smem(s, pp_decode_step_kernel<2>)) ||
-      (r = set_max_smem(s, pp_decode_step_kernel<4>)) || (r = set_max_smem(s, pp_decode_step_kernel<8>)) ||
+      (r = set_max_smem(s, pp_decode_step_kernel<4>)) ||
       (r = set_max_smem(s, pp_pre_flash_kernel<4, 2>)) ||
       (r = set_max_smem(s, pp_pre_flash_kernel<8, 3>)))
     return r;
@@ -1776,16 +1782,20 @@ pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
   if (enabled && !s->dec_on) {
     if (!(s->first && s->last))
       return fail(s, PP_E_UNSUPPORTED, "the decode kernel runs shards that hold every layer");
-    if (s->H % 8 || s->Q % 8 || s->I % 8 || 4 * s->H > kDecSlot || 2 * s->Q > kDecSlot ||
-        2 * s->I > kDecSlot || kv_row_bytes(s->hd) > kDecKvHalf ||
-        (s->G != 1 && s->G != 2 && s->G != 4 && s->G != 8))
+    // A gate/up pair of rows (two rows of the padded H) and a row of the padded Q and I must
+    // fit one ring slot; the attention takes head size 128 and up to 4 query heads per KV head.
+    if (s->H % 8 || s->Q % 8 || s->I % 8 || 4 * dec_kpad(s->H) > kDecSlot ||
+        2 * dec_kpad(s->Q) > kDecSlot || 2 * dec_kpad(s->I) > kDecSlot || s->hd != kDecHd ||
+        (s->G != 1 && s->G != 2 && s->G != 4))
       return fail(s, PP_E_UNSUPPORTED, "geometry outside the decode kernel's row and slot sizes");
     const int vec = decode_vec_floats(s->H, s->Q, s->I, s->hd, s->G);
     size_t budget = dyn_smem_limit(s, pp_decode_step_kernel<1>);
-    for (size_t b : {dyn_smem_limit(s, pp_decode_step_kernel<2>), dyn_smem_limit(s, pp_decode_step_kernel<4>),
-                     dyn_smem_limit(s, pp_decode_step_kernel<8>)})
+    for (size_t b : {dyn_smem_limit(s, pp_decode_step_kernel<2>), dyn_smem_limit(s, pp_decode_step_kernel<4>)})
       budget = b < budget ? b : budget;
-    const size_t fixed = DecodeSmem(0, vec, decode_own_cap(s, s->nkv)).total();
+    // The fixed part at the smallest grid an SM limit allows (n_kv CTAs).
+    const size_t fixed =
+        DecodeSmem(0, vec, decode_own_cap(s, s->nkv), decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv))
+            .total();
     const int ns = budget > fixed ? (int)((budget - fixed) / kDecSlot) : 0;
     if (ns < 2) return fail(s, PP_E_UNSUPPORTED, "the decode kernel's ring does not fit");
     pp_status r = decode_alloc(s);
