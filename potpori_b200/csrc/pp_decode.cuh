@@ -45,9 +45,10 @@ constexpr int kDecHd = 128;               // head size the attention takes
 
 // K of a decode weight copy (zero columns past K).
 __host__ __device__ inline int dec_kpad(int k) { return (k + kDecKAlign - 1) / kDecKAlign * kDecKAlign; }
-// Rows per weight slot for rows of kp columns: the largest power of two <= 16 that fits.
+// Rows per weight slot for rows of kp columns: the largest power of two <= 32 that fits (a lane
+// per row at 32, so at most 32).
 __host__ __device__ inline int dec_slot_rows(int kp) {
-  int r = 16;
+  int r = 32;
   while (r > 1 && r * kp * 2 > kDecSlot) r >>= 1;
   return r;
 }
@@ -60,7 +61,7 @@ __host__ __device__ inline int64_t dec_w_offset(int64_t r, int64_t c, int64_t kp
 
 struct DecodeLayer {
   const uint16_t* wqkv;  // [Q + 2 KV][kH] (q rows, k rows, v rows), dec_w_offset layout
-  const uint16_t* wo;    // [H][kQ]
+  const uint16_t* wo;    // [n_kv][H][kO]: per KV head, its G query heads' columns of O
   const uint16_t* wgu;   // [I][2][kH]: gate row j then up row j
   const uint16_t* wd;    // [H][kI]
   const float* n_attn;
@@ -75,6 +76,7 @@ struct DecodeArgs {
   const DecodeLayer* layers;  // [nl]
   int32_t nl, H, Q, KV, I, hd, nh, nkv, G, V, capacity, embed_kchunks, splits, ss_tiles, nslots;
   int32_t kH, kQ, kI;  // K of the weight copies (dec_kpad of H, Q, I)
+  int32_t kO;          // K of the per-head O copy: G * head_dim
   int32_t vec_floats;  // floats of the staged-vector region
   float eps, inv_scale;
   const uint16_t* embed;    // tiled embedding table (tiled_offset layout)
@@ -82,10 +84,11 @@ struct DecodeArgs {
   const float2* rope;       // [capacity][hd / 2] (cos, sin)
   float* qkv;               // [Q + 2 KV] projections before QK-norm / RoPE
   float* x;                 // [H] residual stream
-  float* attn;              // [Q] attention output
+  float* attn;              // [Q] attention output (unused: each head's stays on chip)
+  float* opart;             // [n_kv][H] O projection of each KV head's query heads
   float* act;               // [I] SwiGLU output
   float* part;              // [nh][splits][hd + 4]: max, sum, -, -, unnormalised output
-  uint32_t* sync;           // [0] barrier arrivals, [1] abort, [2 + h] finished units of head h
+  uint32_t* sync;           // [0] barrier arrivals, [1] abort, [2 + h] units of head h done
   uint8_t* xw_out;          // split(x * final_norm) (split_offset<1> layout)
   float* ss_out;            // [ss_tiles][kMaxRows] sums of squares of x per 128 columns
   const StepDesc* desc;
@@ -110,21 +113,31 @@ struct DecodeSmem {
 // Floats of the staged-vector region: the widest padded GEMV input (a pad of 4 floats per
 // slice, a slice at least 4 units) or the attention scratch (queries, new key and value,
 // per-warp partials; the merge of a head's splits reuses it).
+__host__ __device__ inline int decode_att_floats(int hd, int G) {
+  return (G + 2) * hd + kConsumerWarps * G * (hd + 4);
+}
 __host__ __device__ inline int decode_vec_floats(int H, int Q, int I, int hd, int G) {
   int k = dec_kpad(H) > dec_kpad(Q) ? dec_kpad(H) : dec_kpad(Q);
   k = k > dec_kpad(I) ? k : dec_kpad(I);
   k += k / 8;
-  const int att = (G + 2) * hd + kConsumerWarps * G * (hd + 4);
+  // The attention scratch, then the head's merged output for its O rows (padded, at least one
+  // unit per slice: 4 floats of pad per 8).
+  const int att = decode_att_floats(hd, G) + G * hd * 3 / 2 + 16;
   return k > att ? k : att;
 }
 
 // Balanced contiguous share [lo(b), lo(b+1)) of n items over g CTAs.
 __device__ __forceinline__ int dec_lo(int n, int b, int g) { return (int)((int64_t)n * b / g); }
 
-// Rows of the partial table: the most rows of one GEMV phase a CTA of a g-CTA grid gets.
-__host__ __device__ inline int decode_part_rows(int H, int Q, int KV, int I, int g) {
+// Rows of the partial table: the most rows of one GEMV phase a CTA of a g-CTA grid gets
+// (QKV rows, gate/up rows, down rows, or an attention unit's rows of its head's O block).
+__host__ __device__ inline int decode_part_rows(int H, int Q, int KV, int I, int nkv, int g) {
+  const int S = g / nkv > 0 ? g / nkv : 1;
   const int a = (Q + 2 * KV + g - 1) / g, b = (2 * I + 2 * g - 1) / g, c = (H + g - 1) / g;
-  return (a > b ? (a > c ? a : c) : (b > c ? b : c)) + 2;
+  const int o = (H + S - 1) / S;
+  int m = a > b ? a : b;
+  m = m > c ? m : c;
+  return (m > o ? m : o) + 2;
 }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -166,7 +179,8 @@ struct DecPlan {
   int h, s;       // attention unit (KV head, split); h < 0: none
   int p0, pe;     // cached positions [p0, pe) streamed for the unit
   bool has_new;   // the unit holds the step's own position
-  int rps_qkv, rps_o, rps_gu, rps_d, kvps, rowb;
+  int r0, r1;     // the unit's rows of its head's O block
+  int rps_qkv, rps_oh, rps_gu, rps_d, kvps, rowb;
 };
 
 __device__ __forceinline__ DecPlan dec_plan(const DecodeArgs& a, int b, int g, int pos) {
@@ -182,9 +196,12 @@ __device__ __forceinline__ DecPlan dec_plan(const DecodeArgs& a, int b, int g, i
   p.s = 0;
   p.p0 = p.pe = 0;
   p.has_new = false;
+  p.r0 = p.r1 = 0;
   if (b < a.nkv * S) {
     p.h = b / S;
     p.s = b - p.h * S;
+    p.r0 = dec_lo(a.H, p.s, S);
+    p.r1 = dec_lo(a.H, p.s + 1, S);
     const int c = pos + 1;
     p.p0 = dec_lo(c, p.s, S);
     const int p1 = dec_lo(c, p.s + 1, S);
@@ -193,7 +210,7 @@ __device__ __forceinline__ DecPlan dec_plan(const DecodeArgs& a, int b, int g, i
     if (p.pe < p.p0) p.pe = p.p0;
   }
   p.rps_qkv = dec_slot_rows(a.kH);
-  p.rps_o = dec_slot_rows(a.kQ);
+  p.rps_oh = dec_slot_rows(a.kO);
   p.rps_gu = dec_slot_rows(a.kH);  // an even number: gate/up pairs never straddle two slots
   p.rps_d = dec_slot_rows(a.kI);
   p.rowb = kv_row_bytes(a.hd);
@@ -283,11 +300,14 @@ __device__ __forceinline__ void dec_load_x(const float* vec, const DecLane& d, f
   }
 }
 
-// Stages K floats of src (times w when given) into vec in the padded layout of kp columns in
-// slices of upl units (zeros past K); returns the sum of squares of src, reduced in the same
-// order in every CTA.
-__device__ __forceinline__ float dec_stage_vec(const float* src, const float* w, int K, int kp,
-                                               int upl, float* vec, float* red, int tid) {
+// Stages K floats of src plus, when given, the `nadd` vectors add[j][0..K) (the heads' shares
+// of O, summed in head order), times w when given, into vec in the padded layout of kp columns
+// in slices of upl units (zeros past K); the CTA's own rows [o0, o1) of the sum also go to
+// xown when given. Returns the sum of squares of the sum, reduced in the same order in every
+// CTA.
+__device__ __forceinline__ float dec_stage_vec(const float* src, const float* add, int nadd,
+                                               const float* w, int K, int kp, int upl, float* vec,
+                                               float* red, int tid, float* xown, int o0, int o1) {
   constexpr int T = kConsumerWarps * 32, B = 4;  // float4s per thread per batch of loads
   float ss = 0.f;
   for (int q0 = 0; q0 < (kp >> 2); q0 += B * T) {
@@ -299,11 +319,35 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* w,
       v[k] = in ? __ldcg((const float4*)src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       ww[k] = (in && w) ? ((const float4*)w)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
     }
+    if (add) {
+      for (int j = 0; j < nadd; ++j) {
+        float4 t[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+          const int q = q0 + tid + k * T;
+          t[k] = q < (K >> 2) ? __ldcg((const float4*)(add + (size_t)j * K) + q)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+          v[k].x += t[k].x;
+          v[k].y += t[k].y;
+          v[k].z += t[k].z;
+          v[k].w += t[k].w;
+        }
+      }
+    }
 #pragma unroll
     for (int k = 0; k < B; ++k) {
       const int q = q0 + tid + k * T;
       if (q < (kp >> 2)) {
         float4 x = v[k];
+        if (xown && 4 * q + 3 >= o0 && 4 * q < o1) {
+          const float e[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (4 * q + c >= o0 && 4 * q + c < o1) xown[4 * q + c - o0] = e[c];
+        }
         ss += (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
         if (w) {
           x.x *= ww[k].x;
@@ -458,14 +502,16 @@ __device__ __forceinline__ void dec_attn_key(DecAttnState<G>& st, const float (&
 // Attention unit (KV head h, split s) for the single query position pos: QK-RMSNorm + RoPE
 // of the G query heads and of the new key (tiny.rs:24-37), the new K/V row written by the
 // unit that holds pos, online softmax over the streamed cached rows (tiny.rs:77-101), the
-// unit's partial (max, sum, output) per query head, and the merge of the head's splits by
-// the last unit to finish. A key is taken by eight lanes: lane group kg = lane / 8 of warp w
-// takes the keys 4 w + kg of each 32-key slot, lane q8 = lane % 8 the head dims of 16-byte
-// units q8 and q8 + 8 (dims 8 q8 .. 8 q8 + 7 and 64 + 8 q8 .. 64 + 8 q8 + 7).
+// unit's partial (max, sum, output) per query head, and the merge of the head's S splits by
+// every unit of the head once all are in. A key is taken by eight lanes: lane group
+// kg = lane / 8 of warp w takes the keys 4 w + kg of each 32-key slot, lane q8 = lane % 8 the
+// head dims of 16-byte units q8 and q8 + 8 (dims 8 q8 .. 8 q8 + 7 and 64 + 8 q8 .. 64 + 8 q8 + 7).
+// Returns false when a ring slot never landed; *live_out false when the step was aborted.
 template <int G>  // query heads per KV head (a.G)
 __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeLayer& L,
                                               const DecPlan& P, DecRing& r, bool live, int pos,
-                                              int layer, float* vec, int* flag, int tid) {
+                                              int layer, float* vec, float* ah, int upl_o,
+                                              int* flag, bool* live_out, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   constexpr int hd = kDecHd, half = hd / 2;
   const int h = P.h;
@@ -635,49 +681,72 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
     rec[4 + d] = O;
   }
   consumer_sync();
-  // The head's counter counts the units of every layer so far: the last of this layer's S.
-  if (tid == 0)
-    *flag = atom_add_acq_rel_gpu(&a.sync[2 + h], 1u) == (uint32_t)((layer + 1) * S - 1);
-  consumer_sync();
-  if (*flag) {
-    // Last unit of head h: merge the S splits (exp(max_s - max) weights, split order). The
-    // splits' maxima and sums come in one batch of loads, then each thread's S outputs.
-    float* Ms = mrg;           // [G][S] (the warps' partials are no longer needed)
-    float* Ss = mrg + G * S;   // [G][S]
-    for (int e = tid; e < G * S; e += kConsumerWarps * 32) {
-      const int g = e / S, sp = e - g * S;
-      const float2 ml = __ldcg((const float2*)(a.part + ((size_t)(h * G + g) * S + sp) * stride));
-      Ms[e] = ml.x;
-      Ss[e] = ml.y;
-    }
-    consumer_sync();
-    for (int e = tid; e < G * hd; e += kConsumerWarps * 32) {
-      const int g = e / hd, d = e - g * hd;
-      const float* col = a.part + (size_t)(h * G + g) * S * stride + 4 + d;
-      float pv[32];
-#pragma unroll
-      for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
-      float M = -INFINITY;
-      for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
-      float Ls = 0.f, O = 0.f;
-#pragma unroll
-      for (int sp = 0; sp < 32; ++sp) {
-        if (sp < S) {
-          const float ms = Ms[g * S + sp];
-          const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-          Ls += Ss[g * S + sp] * f;
-          O += pv[sp] * f;
+  // Every unit of the head waits for the head's S partials of this layer (the counter counts
+  // the units of every layer so far), then merges all of them itself: exp(max_s - max)
+  // weights in split order. The merged output (G query heads x head_dim) goes to `ah`, in
+  // the padded slices of the O rows' phase (`upl_o` units per slice).
+  if (tid == 0) {
+    int ok = 1;
+    red_release_gpu(&a.sync[2 + h], 1u);
+    const uint32_t target = (uint32_t)((layer + 1) * S);
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t n = 1; ld_acquire_gpu(&a.sync[2 + h]) < target; ++n) {
+      if ((n & 63) == 0) {
+        if (ld_acquire_gpu(&a.sync[1])) {
+          ok = 0;
+          break;
+        }
+        if (global_timer_ns() - t0 > kDecBarrierNs) {
+          atomicOr(&a.res->status, ST_TIMEOUT);
+          atomicExch(&a.sync[1], 1u);
+          ok = 0;
+          break;
         }
       }
-      for (int sp = 32; sp < S; ++sp) {
+    }
+    *flag = ok;
+  }
+  consumer_sync();
+  if (!*flag) {
+    *live_out = false;
+    return true;
+  }
+  float* Ms = mrg;           // [G][S] (the warps' partials are no longer needed)
+  float* Ss = mrg + G * S;   // [G][S]
+  for (int e = tid; e < G * S; e += kConsumerWarps * 32) {
+    const int g = e / S, sp = e - g * S;
+    const float2 ml = __ldcg((const float2*)(a.part + ((size_t)(h * G + g) * S + sp) * stride));
+    Ms[e] = ml.x;
+    Ss[e] = ml.y;
+  }
+  consumer_sync();
+  for (int e = tid; e < G * hd; e += kConsumerWarps * 32) {
+    const int g = e / hd, d = e - g * hd;
+    const float* col = a.part + (size_t)(h * G + g) * S * stride + 4 + d;
+    float pv[32];
+#pragma unroll
+    for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
+    float M = -INFINITY;
+    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
+    float Ls = 0.f, O = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < 32; ++sp) {
+      if (sp < S) {
         const float ms = Ms[g * S + sp];
         const float f = ms == -INFINITY ? 0.f : expf(ms - M);
         Ls += Ss[g * S + sp] * f;
-        O += __ldcg(col + (size_t)sp * stride) * f;
+        O += pv[sp] * f;
       }
-      a.attn[(h * G + g) * hd + d] = O / Ls;
     }
+    for (int sp = 32; sp < S; ++sp) {
+      const float ms = Ms[g * S + sp];
+      const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+      Ls += Ss[g * S + sp] * f;
+      O += __ldcg(col + (size_t)sp * stride) * f;
+    }
+    ah[dec_vpad(e, upl_o)] = O / Ls;
   }
+  consumer_sync();
   return true;
 }
 
@@ -688,7 +757,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   const int NG = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int own_cap = (a.H + NG - 1) / NG + 1;
-  const DecodeSmem lay(a.nslots, a.vec_floats, own_cap, decode_part_rows(a.H, a.Q, a.KV, a.I, NG));
+  const DecodeSmem lay(a.nslots, a.vec_floats, own_cap,
+                       decode_part_rows(a.H, a.Q, a.KV, a.I, a.nkv, NG));
   DecRing r;
   r.base = smem;
   r.full = (uint64_t*)(smem + lay.bar_off());
@@ -727,7 +797,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
         const size_t off = ((size_t)P.h * a.capacity + P.p0) * P.rowb;
         ok = dec_issue_kv(r, L.kc + off, L.vc + off, P.pe - P.p0, P.rowb, P.kvps);
       }
-      ok = ok && dec_issue_rows(r, L.wo + (size_t)P.o0 * a.kQ, P.o1 - P.o0, a.kQ * 2, P.rps_o);
+      if (ok && P.h >= 0)
+        ok = dec_issue_rows(r, L.wo + ((size_t)P.h * a.H + P.r0) * a.kO, P.r1 - P.r0, a.kO * 2,
+                            P.rps_oh);
       ok = ok && dec_issue_rows(r, L.wgu + (size_t)2 * P.j0 * a.kH, 2 * (P.j1 - P.j0), a.kH * 2, P.rps_gu);
       ok = ok && dec_issue_rows(r, L.wd + (size_t)P.o0 * a.kI, P.o1 - P.o0, a.kI * 2, P.rps_d);
     }
@@ -743,26 +815,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   }
 
   // ------------------------------------------------------------------ consumer warps
-  // The four GEMV phases of a layer run through one copy of the GEMV code (a loop over the
-  // phase; the epilogue switches on it), so the per-layer code stays in the instruction cache:
-  // 0 QKV with the input RMSNorm, then the attention; 1 O + residual; 2 gate/up with the
-  // post-attention RMSNorm and SwiGLU; 3 down + residual.
+  // Per layer, four grid barriers and one barrier among the units of each KV head:
+  //   QKV (input RMSNorm) | attention: each unit's partial, the head's units meet, every unit
+  //   merges the head's splits and computes its rows of the head's share of O | gate/up (the
+  //   residual plus every head's share of O, the post-attention RMSNorm, SwiGLU) | down +
+  //   residual |
   bool live = true, lost = false;  // lost: a ring slot never landed
   uint32_t nb = 0;
+  float* ah = vec + decode_att_floats(a.hd, G);  // a head's merged attention output
   for (int l = 0; l < a.nl && !lost; ++l) {
     const DecodeLayer& L = a.layers[l];
-#pragma unroll 1
-    for (int ph = 0; ph < 4 && !lost; ++ph) {
-      const int kp = ph == 1 ? a.kQ : ph == 3 ? a.kI : a.kH;
-      const int R = ph == 0 ? P.rps_qkv : ph == 1 ? P.rps_o : ph == 2 ? P.rps_gu : P.rps_d;
-      const DecLane d = dec_lane(kp, R, warp, lane);
+    // ---- QKV with the input RMSNorm; layer 0 gathers the token's embedding row
+    // (src/qwen/model.rs:239-241), also the first residual.
+    {
+      const DecLane d = dec_lane(a.kH, P.rps_qkv, warp, lane);
       float rinv = 1.f;
       if (live) {
         float ss;
-        if (ph == 0 && l == 0) {
-          // The token's embedding row (src/qwen/model.rs:239-241), also the first residual.
+        if (l == 0) {
           float t = 0.f;
-          for (int q = tid; q < (kp >> 2); q += kConsumerWarps * 32) {
+          for (int q = tid; q < (a.kH >> 2); q += kConsumerWarps * 32) {
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (q < (a.H >> 2)) {
               v.x = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 0, a.embed_kchunks)] << 16);
@@ -770,11 +842,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
               v.z = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 2, a.embed_kchunks)] << 16);
               v.w = __uint_as_float((uint32_t)a.embed[tiled_offset(tok, 4 * q + 3, a.embed_kchunks)] << 16);
               const int n0 = 4 * q;
-              if (n0 + 3 >= P.o0 && n0 < P.o1) {
-                if (n0 + 0 >= P.o0 && n0 + 0 < P.o1) xown[n0 + 0 - P.o0] = v.x;
-                if (n0 + 1 >= P.o0 && n0 + 1 < P.o1) xown[n0 + 1 - P.o0] = v.y;
-                if (n0 + 2 >= P.o0 && n0 + 2 < P.o1) xown[n0 + 2 - P.o0] = v.z;
-                if (n0 + 3 >= P.o0 && n0 + 3 < P.o1) xown[n0 + 3 - P.o0] = v.w;
+              if (n0 + 3 >= P.o0 && n0 < P.o1) {  // the residual of this CTA's rows
+                const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                  if (n0 + c >= P.o0 && n0 + c < P.o1) a.x[n0 + c] = e[c];
               }
               t += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
               const float4 ww = ((const float4*)L.n_attn)[q];
@@ -793,42 +865,78 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
           for (int i = 0; i < kConsumerWarps; ++i) ss += red[i];
           consumer_sync();
         } else {
-          const float* src = ph == 1 ? a.attn : ph == 3 ? a.act : a.x;
-          const float* w = ph == 0 ? L.n_attn : ph == 2 ? L.n_ffn : nullptr;
-          const int K = ph == 1 ? a.Q : ph == 3 ? a.I : a.H;
-          ss = dec_stage_vec(src, w, K, kp, d.upl, vec, red, tid);
+          ss = dec_stage_vec(a.x, nullptr, 0, L.n_attn, a.H, a.kH, d.upl, vec, red, tid, nullptr, 0, 0);
         }
-        if (ph == 0 || ph == 2) rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+        rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
       float4 x[16];
       dec_load_x(vec, d, x);
-      const int rows = ph == 0 ? P.q1 - P.q0 : ph == 2 ? 2 * (P.j1 - P.j0) : P.o1 - P.o0;
-      const int g0 = ph == 0 ? P.q0 : ph == 2 ? 2 * P.j0 : P.o0;
-      if (!dec_rows(r, live, rows, g0, kp, R, d, x, part, warp, lane, tid, ph == 2,
-                    [&](int rr, float v0, float v1) {
-                      if (ph == 0) {
-                        a.qkv[P.q0 + rr] = v0 * rinv;
-                      } else if (ph == 2) {  // tiny.rs:111-115
-                        const float g = v0 * rinv, u = v1 * rinv;
-                        a.act[P.j0 + (rr >> 1)] = g / (1.0f + expf(-g)) * u;
-                      } else {  // O and down add to the residual (src/qwen/model.rs:304-306)
-                        const float v = xown[rr] + v0;
-                        xown[rr] = v;
-                        a.x[P.o0 + rr] = v;
-                      }
+      if (!dec_rows(r, live, P.q1 - P.q0, P.q0, a.kH, P.rps_qkv, d, x, part, warp, lane, tid,
+                    false, [&](int rr, float v, float) { a.qkv[P.q0 + rr] = v * rinv; })) {
+        lost = true;
+        break;
+      }
+    }
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+    // ---- attention, then this unit's rows of its head's share of O (src/qwen/model.rs:304).
+    if (P.h >= 0) {
+      const DecLane d = dec_lane(a.kO, P.rps_oh, warp, lane);
+      bool hlive = live;
+      if (!dec_attention<G>(a, L, P, r, live, pos, l, vec, ah, d.upl, flag, &hlive, tid)) {
+        lost = true;
+        break;
+      }
+      live = hlive;
+      float4 x[16];
+      dec_load_x(ah, d, x);
+      float* op = a.opart + (size_t)P.h * a.H + P.r0;
+      if (!dec_rows(r, live, P.r1 - P.r0, P.r0, a.kO, P.rps_oh, d, x, part, warp, lane, tid,
+                    false, [&](int rr, float v, float) { op[rr] = v; })) {
+        lost = true;
+        break;
+      }
+    }
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+    // ---- gate/up: the residual after the attention (x plus every head's share of O; this
+    // CTA keeps its own rows), the post-attention RMSNorm, SwiGLU (tiny.rs:111-115).
+    {
+      const DecLane d = dec_lane(a.kH, P.rps_gu, warp, lane);
+      float rinv = 1.f;
+      if (live) {
+        const float ss = dec_stage_vec(a.x, a.opart, a.nkv, L.n_ffn, a.H, a.kH, d.upl, vec, red,
+                                       tid, xown, P.o0, P.o1);
+        rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+      }
+      float4 x[16];
+      dec_load_x(vec, d, x);
+      if (!dec_rows(r, live, 2 * (P.j1 - P.j0), 2 * P.j0, a.kH, P.rps_gu, d, x, part, warp, lane,
+                    tid, true, [&](int rr, float g, float u) {
+                      g *= rinv;
+                      u *= rinv;
+                      a.act[P.j0 + (rr >> 1)] = g / (1.0f + expf(-g)) * u;
                     })) {
         lost = true;
         break;
       }
-      live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
-      if (ph == 0) {
-        if (P.h >= 0 && !dec_attention<G>(a, L, P, r, live, pos, l, vec, flag, tid)) {
-          lost = true;
-          break;
-        }
-        live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+    }
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
+    // ---- down + residual.
+    {
+      const DecLane d = dec_lane(a.kI, P.rps_d, warp, lane);
+      if (live) dec_stage_vec(a.act, nullptr, 0, nullptr, a.I, a.kI, d.upl, vec, red, tid, nullptr, 0, 0);
+      float4 x[16];
+      dec_load_x(vec, d, x);
+      if (!dec_rows(r, live, P.o1 - P.o0, P.o0, a.kI, P.rps_d, d, x, part, warp, lane, tid, false,
+                    [&](int rr, float v, float) {
+                      v += xown[rr];
+                      xown[rr] = v;
+                      a.x[P.o0 + rr] = v;
+                    })) {
+        lost = true;
+        break;
       }
     }
+    live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
   }
   if (lost) {
     if (tid == 0) {
@@ -852,6 +960,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
     consumer_sync();
     if (tid == 0) a.ss_out[t * kMaxRows] = (red[0] + red[1]) + (red[2] + red[3]);
     consumer_sync();
+  }
+}
+
+// The O projection regrouped per KV head for the decode kernel: block h is [H][kO] (the head's
+// G query heads' kO = G * head_dim columns of W_o), dec_w_offset layout.
+__global__ void pp_untile_o_heads_kernel(uint16_t* dst, const uint16_t* src, int64_t H, int64_t kO,
+                                         int64_t nkv, int64_t kchunks) {
+  const int64_t per = H * kO, n = nkv * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t h = i / per, rem = i - h * per, r = rem / kO, c = rem - r * kO;
+    dst[h * per + dec_w_offset(r, c, kO)] = src[tiled_offset(r, h * kO + c, kchunks)];
   }
 }
 

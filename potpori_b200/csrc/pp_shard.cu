@@ -170,8 +170,10 @@ struct pp_shard {
   std::vector<uint16_t*> dec_w;  // [nl][4]: QKV, O, gate/up pairs, down
   DecodeLayer* dec_layers = nullptr;
   float *dec_qkv = nullptr, *dec_attn = nullptr, *dec_act = nullptr, *dec_part = nullptr;
+  float* dec_opart = nullptr;  // [n_kv][H] each KV head's share of the O projection
   uint32_t* dec_sync = nullptr;
-  int dec_ns = 0, dec_vec = 0;
+  int dec_vec = 0;
+  size_t dec_budget = 0;  // dynamic shared memory the decode kernel may use
   // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the
   // projections' activation blocks (work) and error word, the prompt's tokens.
   struct {
@@ -547,11 +549,11 @@ pp_status decode_alloc(pp_shard* s) {
   const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
   s->dec_w.assign((size_t)s->nl * 4, nullptr);
   std::vector<DecodeLayer> tab(s->nl);
-  const int64_t kH = dec_kpad(s->H), kQ = dec_kpad(s->Q), kI = dec_kpad(s->I);
+  const int64_t kH = dec_kpad(s->H), kI = dec_kpad(s->I);
   for (int l = 0; l < s->nl; ++l) {
     uint16_t** w = &s->dec_w[(size_t)l * 4];
     if ((r = dalloc(s, &w[0], (size_t)(Q + 2 * KV) * kH * 2))) return r;
-    if ((r = dalloc(s, &w[1], (size_t)H * kQ * 2))) return r;
+    if ((r = dalloc(s, &w[1], (size_t)s->nkv * H * s->G * s->hd * 2))) return r;
     if ((r = dalloc(s, &w[2], (size_t)2 * I * kH * 2))) return r;
     if ((r = dalloc(s, &w[3], (size_t)H * kI * 2))) return r;
     const LayerDev& Ld = s->L[l];
@@ -565,6 +567,7 @@ pp_status decode_alloc(pp_shard* s) {
   if ((r = dalloc(s, &s->dec_qkv, (size_t)(Q + 2 * KV) * 4))) return r;
   if ((r = dalloc(s, &s->dec_attn, (size_t)Q * 4))) return r;
   if ((r = dalloc(s, &s->dec_act, (size_t)I * 4))) return r;
+  if ((r = dalloc(s, &s->dec_opart, (size_t)s->nkv * H * 4))) return r;
   if ((r = dalloc(s, &s->dec_part, (size_t)s->nh * max_splits * (s->hd + 4) * 4))) return r;
   if ((r = dalloc(s, &s->dec_sync, (size_t)(2 + s->nkv) * 4))) return r;
   CK(cudaStreamSynchronize(s->stream));
@@ -574,12 +577,13 @@ pp_status decode_alloc(pp_shard* s) {
 // Row-major copies of the packed weights (after any weight upload).
 pp_status decode_rebuild(pp_shard* s) {
   const int64_t H = s->H, Q = s->Q, KV = s->KV, I = s->I;
-  const int64_t kH = dec_kpad(s->H), kQ = dec_kpad(s->Q), kI = dec_kpad(s->I);
+  const int64_t kH = dec_kpad(s->H), kI = dec_kpad(s->I);
   for (int l = 0; l < s->nl; ++l) {
     uint16_t** w = &s->dec_w[(size_t)l * 4];
     const LayerDev& Ld = s->L[l];
     pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[0], Ld.wqkv, Q + 2 * KV, H, kH, s->Hp / kChunkK, 0);
-    pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, Q, kQ, s->Qp / kChunkK, 0);
+    pp_untile_o_heads_kernel<<<1024, 256, 0, s->stream>>>(w[1], Ld.wo, H, (int64_t)s->G * s->hd,
+                                                          s->nkv, s->Qp / kChunkK);
     pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[2], Ld.wgu, 2 * I, H, kH, s->Hp / kChunkK, 1);
     pp_untile_rows_kernel<<<1024, 256, 0, s->stream>>>(w[3], Ld.wd, H, I, kI, s->Ip / kChunkK, 0);
     CK(cudaGetLastError());
@@ -599,6 +603,13 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
     return r;
   CK(cudaMemsetAsync(s->dec_sync, 0, (size_t)(2 + s->nkv) * 4, st));
   const int grid = s->max_grid;
+  // Ring slots: what the shared memory holds beside this grid's fixed part (at most 8).
+  const size_t fixed = DecodeSmem(0, s->dec_vec, decode_own_cap(s, grid),
+                                  decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv, grid))
+                           .total();
+  int ns = s->dec_budget > fixed ? (int)((s->dec_budget - fixed) / kDecSlot) : 0;
+  ns = ns > 8 ? 8 : ns;
+  if (ns < 2) return fail(s, PP_E_UNSUPPORTED, "the decode kernel's ring does not fit");
   DecodeArgs a = {};
   a.layers = s->dec_layers;
   a.nl = s->nl;
@@ -615,10 +626,11 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   a.embed_kchunks = (int32_t)(s->Hp / kChunkK);
   a.splits = grid / s->nkv;
   a.ss_tiles = s->ss_tiles;
-  a.nslots = s->dec_ns;
+  a.nslots = ns;
   a.kH = dec_kpad(s->H);
   a.kQ = dec_kpad(s->Q);
   a.kI = dec_kpad(s->I);
+  a.kO = s->G * s->hd;
   a.vec_floats = s->dec_vec;
   a.eps = s->d.cfg.rms_norm_eps;
   a.inv_scale = 1.0f / sqrtf((float)s->hd);
@@ -629,6 +641,7 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   a.x = s->x;
   a.attn = s->dec_attn;
   a.act = s->dec_act;
+  a.opart = s->dec_opart;
   a.part = s->dec_part;
   a.sync = s->dec_sync;
   a.xw_out = s->xw_attn;
@@ -639,8 +652,8 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes =
-      DecodeSmem(s->dec_ns, s->dec_vec, decode_own_cap(s, grid),
-                 decode_part_rows(s->H, s->Q, s->KV, s->I, grid)).total();
+      DecodeSmem(ns, s->dec_vec, decode_own_cap(s, grid),
+                 decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv, grid)).total();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: they meet at grid barriers
@@ -1794,13 +1807,13 @@ pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
       budget = b < budget ? b : budget;
     // The fixed part at the smallest grid an SM limit allows (n_kv CTAs).
     const size_t fixed =
-        DecodeSmem(0, vec, decode_own_cap(s, s->nkv), decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv))
+        DecodeSmem(0, vec, decode_own_cap(s, s->nkv), decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv, s->nkv))
             .total();
     const int ns = budget > fixed ? (int)((budget - fixed) / kDecSlot) : 0;
     if (ns < 2) return fail(s, PP_E_UNSUPPORTED, "the decode kernel's ring does not fit");
     pp_status r = decode_alloc(s);
     if (r) return r;
-    s->dec_ns = ns > 8 ? 8 : ns;
+    s->dec_budget = budget;
     s->dec_vec = vec;
     s->dec_stale = true;
   }
