@@ -5,8 +5,9 @@ Workload (default ``qwen3-4b-8stage``): Qwen3-4B target with seeded random BF16 
 (seed 3), Qwen3-0.6B draft (seed 0), gamma 7 (verify chunks of 8 rows), the depth-8
 pipelined driver of src/specpipe.rs, KV capacity 4096, a 2048-token seeded random prompt.
 With N GPUs the target is split into N contiguous layer ranges (1: 0-36, 2: 18+18, 4: 9x4,
-8: 5,5,5,5,4,4,4,4), one process per GPU, stages joined by NCCL point-to-point transfers;
-rank 0 also runs the draft model and the driver.
+8: 5,5,5,5,4,4,4,4), one process per GPU, stages joined by CUDA IPC copies on the copy
+engines with mailboxes in shared host memory; rank 0 also runs the draft model and the
+driver.
 
 A step is the run of driver iterations — FILL (draft and submit chunks until `depth` are in
 flight) and READ (take the oldest chunk's verified picks; commit, or drain a stale chunk) —
@@ -41,8 +42,6 @@ if ROOT not in sys.path:
 
 METRIC = "Qwen3-4B committed tok/s at 1/2/4/8 B200; verify-pass HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
-NCCL_SMS = 4  # SMs left free for NCCL's transfer kernels on every rank of a multi-GPU run
-DRAFT_SLACK = 8  # with N > 1, SMs of rank 0's budget the draft's decode kernel leaves free
 
 
 def parse_args():
@@ -56,17 +55,9 @@ def parse_args():
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
-    ap.add_argument("--draft-kernel", default="auto", choices=["auto", "decode", "layers"],
+    ap.add_argument("--draft-kernel", default="decode", choices=["decode", "layers"],
                     help="1-row draft steps: one persistent decode kernel, or six kernels per "
-                         "layer; auto = the decode kernel, with N > 1 on DRAFT_SLACK fewer SMs "
-                         "than rank 0's budget (its cooperative launch must find them free "
-                         "while NCCL's transfer kernels hold some)")
-    ap.add_argument("--draft-sms", type=int, default=0,
-                    help="one GPU: run the draft on this many SMs and the target on the rest, "
-                         "so draft steps and verify passes overlap; N > 1: the draft's grid on "
-                         "rank 0 only (0: every SM of the budget)")
-    ap.add_argument("--nccl-sms", type=int, default=None,
-                    help="SMs left to NCCL's transfer kernels on every rank when N > 1")
+                         "layer")
     return ap.parse_args()
 
 
@@ -265,25 +256,18 @@ def run_ours(args):
         import datetime
 
         import torch.distributed as dist
-        # The stage-to-stage messages are 144 B headers and 80 KiB hidden rows: two NCCL
-        # channels carry them, and fewer channels hold fewer SMs (see NCCL_SMS).
-        os.environ.setdefault("NCCL_MAX_NCHANNELS", "2")
+        # NCCL carries the setup and the final timing reduction only; the stages' chunks move
+        # by CUDA IPC copies on the copy engines (potpori_b200/distchain.py).
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     stage = Shard.random(wl.target, ranges[rank], wl.max_seq, wl.chunk, wl.target_seed,
                          device=local)
-    # With N > 1 the NCCL kernels that serve the stage-to-stage transfers hold a few SMs;
-    # the shards' kernels use the rest (their CTAs must all be resident at once).
-    n_sms = torch.cuda.get_device_properties(local).multi_processor_count
-    reserve = (NCCL_SMS if args.nccl_sms is None else args.nccl_sms) if world > 1 else 0
-    sm_budget = n_sms - reserve if reserve else 0
-    stage.set_sm_limit(sm_budget)
     width = wl.chunk
     if world > 1:
         dist.barrier()
     if rank != 0:
-        from potpori_b200.distchain import Links, run_stage
-        ms = run_stage(stage, rank, world, width, Links(world))
+        from potpori_b200.distchain import run_stage
+        ms = run_stage(stage, rank, world, width)
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
@@ -294,23 +278,14 @@ def run_ours(args):
 
     dmodel = QwenTarget(stage) if wl.draft_is_target and world == 1 else \
         QwenTarget.random(wl.draft, wl.max_seq, wl.chunk, wl.draft_seed, device=local)
-    dmodel.shard.set_sm_limit(sm_budget)
-    if args.draft_sms and dmodel.shard is not stage:
-        dmodel.shard.set_sm_limit(args.draft_sms)
-        if world == 1:  # disjoint budgets; with N > 1 only the draft's grid shrinks
-            stage.set_sm_limit(n_sms - args.draft_sms)
-    if args.draft_kernel in ("decode", "auto"):
+    if args.draft_kernel == "decode":
         dmodel.shard.set_decode_kernel(True)
-        if world > 1 and not args.draft_sms:
-            # The cooperative grid must find its SMs free while NCCL's transfer kernels and
-            # the stage's kernels come and go on rank 0: leave it DRAFT_SLACK more SMs.
-            dmodel.shard.set_sm_limit(sm_budget - DRAFT_SLACK)
     draft = IncrementalDraft(dmodel, wl.chunk)
     if world == 1:
         chain = LocalChain([stage])
     else:
-        from potpori_b200.distchain import FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain, Links
-        chain = DistChain(stage, world, width, Links(world))
+        from potpori_b200.distchain import FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain
+        chain = DistChain(stage, world, width)
     prompt = wl.prompt()
     drv = PipelinedDriver(draft, chain, prompt, SpecConfig(wl.gamma, wl.max_new), wl.depth)
     stream = torch.cuda.ExternalStream(stage.stream())

@@ -136,6 +136,29 @@ pp_status pp_shard_result_enqueue(pp_shard* shard, uint32_t slot);
 /* Wait for result slot `slot` and fill `verify` (m rows); the status of that step. */
 pp_status pp_shard_result_wait(pp_shard* shard, uint32_t slot, uint32_t m, pp_verify_out* verify);
 
+/* Cross-process stage link inside one box: the hop between the nodes of a chain
+ * (ChainLink::send_chunk and serve_middle/serve_tail, src/node.rs:242-342,466-535; the frames
+ * of src/transport.rs:425-489) when consecutive stages run in different processes, one per
+ * GPU. The receiving stage exports an inbox of `slots` chunk slots (step header + hidden rows)
+ * in its device memory as a 64-byte CUDA IPC handle; the sending stage opens it and, after
+ * its step, copies the chunk's header and hidden rows into slot seq % slots on the copy
+ * engines (NVLink), then writes the slot's two mailbox words (mail[1] = info, then
+ * mail[0] = seq + 1) with stream-ordered writes into host memory that both processes share
+ * (registered with pp_host_register). No SM takes part in a transfer. The receiving process
+ * waits for mail[0] on the host, then pp_shard_recv copies the slot into the shard's input
+ * and header buffers, ordered before its next step. m = 0 sends only the mailbox words (the
+ * end of a session). */
+pp_status pp_shard_inbox_export(pp_shard* shard, uint32_t slots, void* handle);
+pp_status pp_shard_outbox_open(pp_shard* shard, const void* handle, uint32_t slots);
+pp_status pp_shard_send(pp_shard* shard, uint32_t seq, uint32_t m, uint32_t* mail, uint32_t info);
+pp_status pp_shard_recv(pp_shard* shard, uint32_t seq, uint32_t m);
+/* Last stage: copy the step result into host memory (registered, shared with the head's
+ * process: the direct return of the result to the head) and then write `value` into *mail. */
+pp_status pp_shard_send_result(pp_shard* shard, void* host_result, uint32_t* mail, uint32_t value);
+/* Page-lock and map host memory for the device (a shared-memory segment of the chain). */
+pp_status pp_host_register(void* ptr, size_t bytes);
+pp_status pp_host_unregister(void* ptr);
+
 /* ShardEngine::reset (src/qwen/runtime/cuda.rs:181-189): KV cache back to zeros. */
 pp_status pp_shard_reset(pp_shard* shard);
 /* Seeded N(0,1) KV rows [0, rows) in every layer (benchmark warm context; the oracle's

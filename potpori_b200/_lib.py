@@ -33,7 +33,9 @@ EXPORTS = [
     "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
     "pp_shard_prefill", "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
     "pp_rows_gemm_work_bytes", "pp_rows_gemm", "pp_norm_gemv_static", "pp_shard_set_taps",
-    "pp_shard_tap_layers", "pp_shard_read_taps", "pp_last_error", "pp_version",
+    "pp_shard_tap_layers", "pp_shard_read_taps", "pp_shard_inbox_export", "pp_shard_outbox_open",
+    "pp_shard_send", "pp_shard_recv", "pp_shard_send_result", "pp_host_register",
+    "pp_host_unregister", "pp_last_error", "pp_version",
 ]
 
 KERNEL_KINDS = ["begin", "embed", "qkv", "attn", "attn_combine", "o_proj", "gate_up", "down",
@@ -133,6 +135,13 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_taps": (I32, [P, ctypes.POINTER(U32), U32]),
         "pp_shard_tap_layers": (U32, [P, ctypes.POINTER(U32), U32]),
         "pp_shard_read_taps": (I32, [P, U32, P, P]),
+        "pp_shard_inbox_export": (I32, [P, U32, P]),
+        "pp_shard_outbox_open": (I32, [P, P, U32]),
+        "pp_shard_send": (I32, [P, U32, U32, P, U32]),
+        "pp_shard_recv": (I32, [P, U32, U32]),
+        "pp_shard_send_result": (I32, [P, P, P, U32]),
+        "pp_host_register": (I32, [P, SZ]),
+        "pp_host_unregister": (I32, [P]),
         "pp_last_error": (SZ, [P, ctypes.c_char_p, SZ]),
         "pp_version": (ctypes.c_char_p, []),
     }

@@ -60,6 +60,23 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+typedef CUresult (*StreamWriteValue32Fn)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+StreamWriteValue32Fn write_value_fn() {
+  static StreamWriteValue32Fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (StreamWriteValue32Fn)p;
+  }
+  return fn;
+}
+
+// Bytes of one inbox slot: the step header (padded to 256) and kMaxRows hidden rows.
+inline size_t inbox_slot_bytes(int64_t Hp) { return 256 + (size_t)kMaxRows * Hp * 4; }
+
 inline float bits_to_float(uint32_t u) {
   float f;
   memcpy(&f, &u, 4);
@@ -152,6 +169,13 @@ struct pp_shard {
   cudaEvent_t desc_ev[kRing] = {};
   cudaEvent_t slot_ev[kRing] = {};
   cudaEvent_t handoff_ev = nullptr, handoff_done_ev = nullptr;
+  // Cross-process link (pp_shard_inbox_export / pp_shard_outbox_open): this shard's inbox of
+  // chunk slots (header + hidden rows) that the previous stage's process writes, and the next
+  // stage's inbox opened through CUDA IPC.
+  uint8_t* inbox = nullptr;
+  uint32_t inbox_slots = 0;
+  uint8_t* outbox = nullptr;
+  uint32_t outbox_slots = 0;
   uint32_t desc_next = 0;
   float* h_stage = nullptr;  // pinned [kMaxRows][H]
   int splits = 1, nq_max = 1;
@@ -1060,6 +1084,8 @@ void pp_shard_destroy(pp_shard* s) {
   if (s->stream) cudaStreamSynchronize(s->stream);
   for (auto& e : s->exec)
     if (e) cudaGraphExecDestroy(e);
+  if (s->outbox) cudaIpcCloseMemHandle(s->outbox);
+  if (s->inbox) cudaFree(s->inbox);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_desc) cudaFreeHost(s->h_desc);
   if (s->h_res) cudaFreeHost(s->h_res);
@@ -1730,6 +1756,106 @@ pp_status pp_shard_handoff(pp_shard* from, pp_shard* to, uint32_t m) {
   CK(cudaEventRecord(to->handoff_done_ev, to->stream));
   CK(cudaSetDevice(from->dev));
   CK(cudaStreamWaitEvent(from->stream, to->handoff_done_ev, 0));
+  return PP_OK;
+}
+
+pp_status pp_shard_inbox_export(pp_shard* s, uint32_t slots, void* handle) {
+  if (!s || !handle) return fail(s, PP_E_INVALID, "null argument");
+  if (slots == 0 || slots > 4096) return fail(s, PP_E_INVALID, "slots must be 1..4096");
+  if (s->first) return fail(s, PP_E_INVALID, "the first stage has no inbox");
+  CK(cudaSetDevice(s->dev));
+  if (s->inbox && s->inbox_slots != slots) return fail(s, PP_E_INVALID, "inbox already exported");
+  if (!s->inbox) {
+    // Its own allocation: an IPC handle names the start of one.
+    CK(cudaMalloc(&s->inbox, slots * inbox_slot_bytes(s->Hp)));
+    s->inbox_slots = slots;
+    s->bytes += slots * inbox_slot_bytes(s->Hp);
+  }
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, s->inbox));
+  memcpy(handle, &h, sizeof h);
+  return PP_OK;
+}
+
+pp_status pp_shard_outbox_open(pp_shard* s, const void* handle, uint32_t slots) {
+  if (!s || !handle) return fail(s, PP_E_INVALID, "null argument");
+  if (s->last) return fail(s, PP_E_INVALID, "the last stage sends results, not hidden rows");
+  if (slots == 0 || slots > 4096) return fail(s, PP_E_INVALID, "slots must be 1..4096");
+  if (s->outbox) return fail(s, PP_E_INVALID, "outbox already open");
+  CK(cudaSetDevice(s->dev));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  void* p = nullptr;
+  CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  s->outbox = (uint8_t*)p;
+  s->outbox_slots = slots;
+  return PP_OK;
+}
+
+// The stream-ordered write of `value` into a word of registered host memory.
+static pp_status write_word(pp_shard* s, uint32_t* host_word, uint32_t value) {
+  StreamWriteValue32Fn fn = write_value_fn();
+  if (!fn) return fail(s, PP_E_CUDA, "cuStreamWriteValue32 is not available");
+  void* dp = nullptr;
+  CK(cudaHostGetDevicePointer(&dp, host_word, 0));
+  if (fn((CUstream)s->stream, (CUdeviceptr)dp, value, 0) != CUDA_SUCCESS)
+    return fail(s, PP_E_CUDA, "cuStreamWriteValue32 failed");
+  return PP_OK;
+}
+
+pp_status pp_shard_send(pp_shard* s, uint32_t seq, uint32_t m, uint32_t* mail, uint32_t info) {
+  if (!s || !mail) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->outbox) return fail(s, PP_E_INVALID, "no outbox: pp_shard_outbox_open first");
+  if (m > (uint32_t)kMaxRows) return fail(s, PP_E_INVALID, "bad row count");
+  CK(cudaSetDevice(s->dev));
+  uint8_t* slot = s->outbox + (size_t)(seq % s->outbox_slots) * inbox_slot_bytes(s->Hp);
+  if (m) {
+    // Header and hidden rows over NVLink on the copy engines, ordered after the step.
+    CK(cudaMemcpyAsync(slot, s->d_desc, sizeof(StepDesc), cudaMemcpyDeviceToDevice, s->stream));
+    CK(cudaMemcpyAsync(slot + 256, s->x, (size_t)m * s->Hp * 4, cudaMemcpyDeviceToDevice, s->stream));
+  }
+  pp_status r;
+  if ((r = write_word(s, mail + 1, info))) return r;
+  return write_word(s, mail, seq + 1);
+}
+
+pp_status pp_shard_recv(pp_shard* s, uint32_t seq, uint32_t m) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (!s->inbox) return fail(s, PP_E_INVALID, "no inbox: pp_shard_inbox_export first");
+  if (m == 0 || m > (uint32_t)kMaxRows) return fail(s, PP_E_INVALID, "bad row count");
+  CK(cudaSetDevice(s->dev));
+  const uint8_t* slot = s->inbox + (size_t)(seq % s->inbox_slots) * inbox_slot_bytes(s->Hp);
+  CK(cudaMemcpyAsync(s->d_desc, slot, sizeof(StepDesc), cudaMemcpyDeviceToDevice, s->stream));
+  CK(cudaMemcpyAsync(s->x, slot + 256, (size_t)m * s->Hp * 4, cudaMemcpyDeviceToDevice, s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_send_result(pp_shard* s, void* host_result, uint32_t* mail, uint32_t value) {
+  if (!s || !host_result || !mail) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->last) return fail(s, PP_E_INVALID, "only the last stage has results");
+  CK(cudaSetDevice(s->dev));
+  CK(cudaMemcpyAsync(host_result, s->d_res, sizeof(StepResult), cudaMemcpyDeviceToHost, s->stream));
+  return write_word(s, mail, value);
+}
+
+pp_status pp_host_register(void* p, size_t bytes) {
+  if (!p || !bytes) {
+    pp::set_global_error("null argument");
+    return PP_E_INVALID;
+  }
+  cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
+  if (e != cudaSuccess) {
+    pp::set_global_error(cudaGetErrorString(e));
+    return PP_E_CUDA;
+  }
+  return PP_OK;
+}
+
+pp_status pp_host_unregister(void* p) {
+  if (cudaHostUnregister(p) != cudaSuccess) {
+    pp::set_global_error("cudaHostUnregister failed");
+    return PP_E_CUDA;
+  }
   return PP_OK;
 }
 

@@ -1,31 +1,42 @@
-"""Pipeline stages in separate processes, one per GPU, joined by NCCL point-to-point transfers
-of the shards' own device buffers (torch.distributed is the plumbing).
+"""Pipeline stages in separate processes, one per GPU, joined by CUDA IPC copies on the copy
+engines and mailbox words in host memory that the processes share.
 
 This replaces the reference's chain over QUIC (head ChainLink::send_chunk -> relay_middle ->
 serve_tail -> VerifyResult back, src/node.rs:242-342,466-535, src/transport.rs:425-489):
  * rank 0 (the head) runs the draft model, stage 0 and the driver; every chunk it submits
-   travels as two messages, the 144-byte step header (position, rows, tokens, drafts) and
-   the chunk's F32 hidden rows, from rank r to rank r+1, device buffer to device buffer;
- * every other rank loops: receive header + hidden into its shard's input buffers, run the
-   step (graph replay, no host involvement), forward to the next rank;
- * the last rank computes the greedy picks and the accept compare on the device and sends
-   the 208-byte result straight back to rank 0 (a direct return instead of a relay).
-Ordering is by streams only: NCCL transfers are enqueued on each shard's stream (via
-torch.cuda.ExternalStream), so nothing waits on the host except the head's poll and each
-stage's look at the header it just received (to notice the end of the session).
-A header with m = 0 ends the session; flag bits mark the benchmark's timed window.
+   travels as the step header (position, rows, tokens, drafts) and the chunk's F32 hidden rows
+   from rank r to rank r+1: after its step, rank r's stream copies them into slot k of rank
+   r+1's inbox (device memory opened through CUDA IPC; the copy engines move it over NVLink)
+   and then writes the slot's two mailbox words (info, then k + 1) into the shared host
+   memory with stream-ordered writes;
+ * every other rank loops: wait on the host for chunk k's mailbox word, copy the inbox slot
+   into its shard's input and header buffers (stream-ordered), run the step (graph replay)
+   and send it on;
+ * the last rank computes the greedy picks and the accept compare on the device and copies
+   the 208-byte result straight into the head's result ring in the shared host memory (a
+   direct return instead of the reference's relay), then its mailbox word.
+No SM takes part in a transfer: the copies run on the copy engines and the mailbox words are
+stream memory writes, so the stages' kernels, and the draft's cooperative decode kernel on
+rank 0, keep every SM. torch.distributed carries only the setup (the handshake of
+src/transport.rs:299-358, the IPC handles and the shared memory's name) and the final timing
+reduction. A chunk with m = 0 ends the session; flag bits mark the benchmark's timed window.
 
 The protocol (run_stage, DistChain) talks to its stage through a small I/O object:
-CudaStageIO (a Shard's device buffers and stream: the product path) or any object with the
-same methods, such as a host-memory stand-in that lets the protocol run under gloo on CPU.
+CudaStageIO (a Shard's device buffers and stream: the product path) or HostStageIO, a
+host-memory stand-in whose inbox lives in the shared memory too, so the protocol runs under
+gloo on CPU.
 """
 from __future__ import annotations
 
-import contextlib
+import ctypes
+import mmap
+import os
 import time
+import uuid
 from collections import deque
 from typing import List, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -36,69 +47,131 @@ from .target import NonFiniteLogits
 HDR_INTS = 36   # StepDesc: pos, m, n_drafts, flags, tokens[16], drafts[16]
 RES_INTS = 52   # StepResult: argmax[16], top1[16], top2[16], nonfinite_rows, n_acc, corr, status
 RES_NONFINITE, RES_STATUS = 48, 51
-RING = 64
+RES_SLOT = 256  # bytes per result slot
+RING = 64       # chunk slots of every inbox and of the result ring
 FLAG_WINDOW_START = 2
 FLAG_WINDOW_END = 4
+WAIT_S = 120.0  # a stage that hears nothing for this long ends the session with an error
 
 
-class Links:
-    """One process group per link, so transfers on different links never queue behind each
-    other: NCCL runs the ops of one communicator in order, so with a single group the head's
-    receive of chunk k's result (posted first, completing only after the whole traversal)
-    would hold back the send of chunk k+1, and the chunks could not overlap in the pipeline.
-    fwd[r]: rank r -> r + 1; ret: the last rank -> rank 0. Every rank must build it, in the
-    same order (dist.new_group is collective)."""
-
-    def __init__(self, world: int):
-        self.fwd = [dist.new_group([r, r + 1]) for r in range(world - 1)]
-        self.ret = dist.new_group([0, world - 1])
+class ChainError(RuntimeError):
+    pass
 
 
-class _DevArray:
-    def __init__(self, ptr: int, n: int, typestr: str):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
-                                         "data": (int(ptr), False), "version": 3}
+class ChainMemory:
+    """The chain's shared host memory, one file in /dev/shm made by rank 0: for every link
+    r -> r+1 a ring of RING mailbox word pairs (k + 1, info), the result ring (a word pair and
+    a result slot per chunk) and, when `data_bytes` is given, the inbox data of host stand-ins
+    (RING slots of data_bytes per link). info = rows | flags << 8."""
 
+    def __init__(self, world: int, path: str, create: bool, data_bytes: int = 0):
+        self.world, self.path, self.data_bytes = world, path, data_bytes
+        self.n_words = world * RING * 2  # world - 1 links + the result ring
+        self.res_off = self.n_words * 4
+        self.data_off = self.res_off + RING * RES_SLOT
+        self.size = self.data_off + (world - 1) * RING * data_bytes
+        fd = os.open(path, os.O_RDWR | (os.O_CREAT if create else 0), 0o600)
+        try:
+            if create:
+                os.ftruncate(fd, self.size)
+            self.mm = mmap.mmap(fd, self.size)
+        finally:
+            os.close(fd)
+        self.words = np.ndarray((self.n_words,), np.uint32, self.mm)
+        if create:
+            self.words[:] = 0
+        self._anchor = ctypes.c_char.from_buffer(self.mm)
+        self.base = ctypes.addressof(self._anchor)
+        self.registered = False
 
-def device_tensor(ptr: int, n: int, dtype, device: int) -> torch.Tensor:
-    ts = {torch.float32: "<f4", torch.int32: "<i4"}[dtype]
-    return torch.as_tensor(_DevArray(ptr, n, ts), device=torch.device("cuda", device))
+    def mail(self, link: int, k: int) -> int:
+        """Word index of chunk k's mailbox on link `link` (link world - 1: the results)."""
+        return (link * RING + k % RING) * 2
+
+    def result_ints(self, k: int) -> np.ndarray:
+        return np.ndarray((RES_INTS,), np.int32, self.mm, self.res_off + (k % RING) * RES_SLOT)
+
+    def wait(self, link: int, k: int, timeout: float = WAIT_S) -> int:
+        """Wait for chunk k on `link`; its info word."""
+        i = self.mail(link, k)
+        want = (k + 1) & 0xFFFFFFFF
+        t0 = time.monotonic()
+        n = 0
+        while int(self.words[i]) != want:
+            n += 1
+            if (n & 1023) == 0:
+                if time.monotonic() - t0 > timeout:
+                    raise ChainError(f"no chunk {k} on link {link} within {timeout:.0f} s")
+                time.sleep(0)
+        return int(self.words[i + 1])
+
+    def register(self, lib) -> None:
+        from ._lib import check
+        check(lib.pp_host_register(self.base, self.size), None, "register the chain memory")
+        self.registered = True
+
+    def close(self, lib=None) -> None:
+        if self.registered and lib is not None:
+            lib.pp_host_unregister(self.base)
+            self.registered = False
+        self.words = None
+        self._anchor = None
+        self.base = 0
+        try:
+            self.mm.close()
+        except BufferError:  # a view still alive: the mapping goes with the process
+            pass
 
 
 class CudaStageIO:
-    """A shard's resident buffers (hidden rows, step header, step result) as tensors, its
-    stream as the ordering of every transfer, and events for the timed window."""
+    """A shard's resident buffers and stream, the inbox it exports and the outbox it opened;
+    events for the timed window."""
 
     def __init__(self, shard, width: int):
-        hid, hdr, res = shard.buffers()
-        dev = shard.device
-        self.shard, self.width, self.device = shard, width, dev
+        self.shard, self.width, self.device = shard, width, shard.device
         self.first, self.last = shard.first, shard.last
-        self.hid = device_tensor(hid, width * shard.cfg.hidden, torch.float32, dev)
-        self.hdr = device_tensor(hdr, HDR_INTS, torch.int32, dev)
-        self.res = device_tensor(res, RES_INTS, torch.int32, dev)
-        self.stream = torch.cuda.ExternalStream(shard.stream(), device=torch.device("cuda", dev))
-        self._host_hdr = torch.empty(HDR_INTS, dtype=torch.int32, pin_memory=True)
-        self._host_res = torch.empty(RES_INTS, dtype=torch.int32, pin_memory=True)
-        self._seen = torch.cuda.Event()
+        self.stream = torch.cuda.ExternalStream(shard.stream(),
+                                                device=torch.device("cuda", self.device))
         self._t0 = torch.cuda.Event(enable_timing=True)
         self._t1 = torch.cuda.Event(enable_timing=True)
+        self.mem = None
+        self.rank = 0
 
-    def ordered(self):
-        return torch.cuda.stream(self.stream)
+    def data_bytes(self) -> int:
+        return 0
 
-    def read_header(self) -> Tuple[int, int]:
-        """(rows, flags) of the header that just arrived (waits for it on the host)."""
-        self._host_hdr.copy_(self.hdr, non_blocking=True)
-        self._seen.record(self.stream)
-        self._seen.synchronize()
-        return int(self._host_hdr[1]), int(self._host_hdr[3])
+    def export_inbox(self) -> bytes:
+        return self.shard.inbox_export(RING)
+
+    def open_outbox(self, handle: bytes) -> None:
+        self.shard.outbox_open(handle, RING)
+
+    def attach(self, mem: ChainMemory) -> None:
+        from . import _lib
+        self.mem = mem
+        mem.register(_lib.load())
+
+    def detach(self) -> None:
+        from . import _lib
+        self.mem.close(_lib.load())
 
     def set_step(self, pos: int, m: int, tokens, drafts, flags: int) -> None:
         self.shard.set_step(pos, m, tokens=tokens, drafts=drafts, flags=flags)
 
     def step(self) -> None:
-        self.shard.step_device(self.width, stream=self.shard.stream())
+        self.shard.step_device(self.width)
+
+    def recv(self, k: int, m: int) -> None:
+        self.shard.recv(k, m)
+
+    def send(self, link: int, k: int, m: int, info: int) -> None:
+        mem = self.mem
+        self.shard.send(k, m, mem.base + mem.mail(link, k) * 4, info)
+
+    def send_result(self, k: int) -> None:
+        mem = self.mem
+        self.shard.send_result(mem.base + mem.res_off + (k % RING) * RES_SLOT,
+                               mem.base + mem.mail(mem.world - 1, k) * 4, k + 1)
 
     def mark_start(self) -> None:
         self._t0.record(self.stream)
@@ -111,22 +184,6 @@ class CudaStageIO:
 
     def finish(self) -> None:
         torch.cuda.synchronize(self.device)
-
-    def result_slots(self, n: int) -> torch.Tensor:
-        return torch.zeros((n, RES_INTS), dtype=torch.int32, device=torch.device("cuda", self.device))
-
-    def fetch(self, slot_row: torch.Tensor) -> List[int]:
-        self._host_res.copy_(slot_row, non_blocking=True)
-        self.stream.synchronize()
-        return self._host_res.tolist()
-
-    def stop_header(self, flags: int) -> torch.Tensor:
-        stop = torch.zeros(HDR_INTS, dtype=torch.int32, device=torch.device("cuda", self.device))
-        stop[3] = flags
-        return stop
-
-    def drain(self) -> None:
-        self.stream.synchronize()
 
     def capacity(self) -> int:
         return self.shard.capacity()
@@ -146,12 +203,13 @@ class CudaStageIO:
 
 class HostStageIO:
     """The same interface over host tensors and a host `stage` object with `step(hdr, hid,
-    res)`: runs the protocol under gloo without a GPU (tests of the multi-process logic)."""
+    res)`; its inbox is a region of the shared memory. Runs the protocol under gloo without a
+    GPU (tests of the multi-process logic)."""
 
     def __init__(self, stage, width: int, hidden: int, first: bool, last: bool,
                  capacity: int = 4096, chunk: int = 8, layer_range=(0, 1), model_layers=1,
                  model: str = "host-stand-in"):
-        self.stage, self.width = stage, width
+        self.stage, self.width, self.hidden = stage, width, hidden
         self.first, self.last = first, last
         self._range, self._layers, self._model = tuple(layer_range), model_layers, model
         self.hid = torch.zeros(width * hidden, dtype=torch.float32)
@@ -159,12 +217,30 @@ class HostStageIO:
         self.res = torch.zeros(RES_INTS, dtype=torch.int32)
         self._cap, self._chunk = capacity, chunk
         self._t0 = self._t1 = 0.0
+        self.mem = None
+        self.rank = 0
 
-    def ordered(self):
-        return contextlib.nullcontext()
+    def data_bytes(self) -> int:
+        return HDR_INTS * 4 + self.width * self.hidden * 4
 
-    def read_header(self) -> Tuple[int, int]:
-        return int(self.hdr[1]), int(self.hdr[3])
+    def export_inbox(self) -> bytes:
+        return b""
+
+    def open_outbox(self, handle: bytes) -> None:
+        pass
+
+    def attach(self, mem: ChainMemory) -> None:
+        self.mem = mem
+
+    def detach(self) -> None:
+        self.mem.close()
+
+    def _slot(self, link: int, k: int) -> Tuple[np.ndarray, np.ndarray]:
+        mem = self.mem
+        off = mem.data_off + (link * RING + k % RING) * mem.data_bytes
+        hdr = np.ndarray((HDR_INTS,), np.int32, mem.mm, off)
+        hid = np.ndarray((self.width * self.hidden,), np.float32, mem.mm, off + HDR_INTS * 4)
+        return hdr, hid
 
     def set_step(self, pos: int, m: int, tokens, drafts, flags: int) -> None:
         self.hdr.zero_()
@@ -176,6 +252,26 @@ class HostStageIO:
     def step(self) -> None:
         self.stage.step(self.hdr, self.hid, self.res)
 
+    def recv(self, k: int, m: int) -> None:
+        hdr, hid = self._slot(self.rank - 1, k)
+        self.hdr.copy_(torch.from_numpy(hdr.copy()))
+        self.hid.copy_(torch.from_numpy(hid.copy()))
+
+    def send(self, link: int, k: int, m: int, info: int) -> None:
+        mem = self.mem
+        if m:
+            hdr, hid = self._slot(link, k)
+            hdr[:] = self.hdr.numpy()
+            hid[:] = self.hid.numpy()
+        i = mem.mail(link, k)
+        mem.words[i + 1] = info
+        mem.words[i] = (k + 1) & 0xFFFFFFFF
+
+    def send_result(self, k: int) -> None:
+        mem = self.mem
+        mem.result_ints(k)[:] = self.res.numpy()
+        mem.words[mem.mail(mem.world - 1, k)] = (k + 1) & 0xFFFFFFFF
+
     def mark_start(self) -> None:
         self._t0 = time.perf_counter()
 
@@ -186,20 +282,6 @@ class HostStageIO:
         return (self._t1 - self._t0) * 1e3
 
     def finish(self) -> None:
-        pass
-
-    def result_slots(self, n: int) -> torch.Tensor:
-        return torch.zeros((n, RES_INTS), dtype=torch.int32)
-
-    def fetch(self, slot_row: torch.Tensor) -> List[int]:
-        return slot_row.tolist()
-
-    def stop_header(self, flags: int) -> torch.Tensor:
-        stop = torch.zeros(HDR_INTS, dtype=torch.int32)
-        stop[3] = flags
-        return stop
-
-    def drain(self) -> None:
         pass
 
     def capacity(self) -> int:
@@ -246,88 +328,111 @@ def negotiate(io, rank: int, world: int) -> None:
         raise HandshakeError("; ".join(errors))
 
 
-def run_stage(shard, rank: int, world: int, width: int, links: Links, io=None) -> float:
+def connect(io, rank: int, world: int) -> ChainMemory:
+    """Set up the links (collective: every rank, in the same order): the handshake, the shared
+    memory (made by rank 0; its name and the inbox handles gathered), and each stage's outbox
+    opened on the next stage's inbox."""
+    negotiate(io, rank, world)
+    io.rank = rank
+    mine = {"inbox": io.export_inbox() if rank > 0 else b"", "data": io.data_bytes(),
+            "path": f"/dev/shm/potpori_chain_{uuid.uuid4().hex}" if rank == 0 else ""}
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    path = every[0]["path"]
+    data = max(v["data"] for v in every)
+    mem = ChainMemory(world, path, True, data) if rank == 0 else None
+    dist.barrier()
+    if rank != 0:
+        mem = ChainMemory(world, path, False, data)
+    io.attach(mem)
+    if rank + 1 < world:
+        io.open_outbox(every[rank + 1]["inbox"])
+    dist.barrier()
+    if rank == 0:  # every rank has mapped it: the name can go
+        os.unlink(path)
+    return mem
+
+
+def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
     """Serve as stage `rank` (1 <= rank < world) until the session ends. Returns the time (ms)
     between the timed-window marks, measured on this stage's stream (0 without both marks)."""
     io = io or CudaStageIO(shard, width)
-    negotiate(io, rank, world)
+    mem = connect(io, rank, world)
     started = ended = False
-    with io.ordered():
+    k = 0
+    try:
         while True:
-            w1 = dist.irecv(io.hdr, rank - 1, group=links.fwd[rank - 1])
-            w2 = dist.irecv(io.hid, rank - 1, group=links.fwd[rank - 1])
-            w1.wait()
-            w2.wait()
-            m, flags = io.read_header()
+            info = mem.wait(rank - 1, k)
+            m, flags = info & 0xFF, info >> 8
             if flags & FLAG_WINDOW_START and not started:
                 io.mark_start()
                 started = True
             if flags & FLAG_WINDOW_END and started and not ended:
                 io.mark_end()
                 ended = True
-            if m > 0:
-                io.step()
+            if m == 0:
+                if not io.last:
+                    io.send(rank, k, 0, info)
+                break
+            io.recv(k, m)
+            io.step()
             if io.last:
-                if m == 0:
-                    break
-                w = dist.isend(io.res, 0, group=links.ret)
-                w.wait()
+                io.send_result(k)
             else:
-                w1 = dist.isend(io.hdr, rank + 1, group=links.fwd[rank])
-                w2 = dist.isend(io.hid, rank + 1, group=links.fwd[rank])
-                w1.wait()
-                w2.wait()
-                if m == 0:
-                    break
-    io.finish()
+                io.send(rank, k, m, info)
+            k += 1
+        io.finish()
+    finally:
+        io.detach()
     return io.elapsed_ms() if (started and ended) else 0.0
 
 
 class DistChain:
     """The head's view of the multi-process chain (PipelinedChain / TargetChain)."""
 
-    def __init__(self, stage0, world: int, width: int, links: Links, io=None):
+    def __init__(self, stage0, world: int, width: int, io=None):
         self.io = io or CudaStageIO(stage0, width)
         assert self.io.first and not self.io.last and world > 1
-        negotiate(self.io, 0, world)
-        self.world, self.width, self.links = world, width, links
-        self.slots = self.io.result_slots(RING)
+        self.world, self.width = world, width
+        self.mem = connect(self.io, 0, world)
         self.inflight: deque = deque()
-        self.slot = 0
+        self.seq = 0    # next chunk to send
+        self.done = 0   # next chunk whose result is read
         self.capacity_ = self.io.capacity()
         self.chunk = self.io.chunk_size() or width
         self.pending_flags = 0
         self.submitted = 0
+        self.closed = False
 
     def capacity(self) -> int:
         return self.capacity_
 
     def mark(self, flags: int) -> None:
-        """Put flag bits on the next header sent (timed-window marks)."""
+        """Put flag bits on the next chunk sent (timed-window marks)."""
         self.pending_flags |= flags
 
     def submit(self, pos: int, cur: int, drafts: List[int]) -> None:
+        # A slot of every inbox is reused RING chunks later; with at most RING / 2 chunks
+        # between the head and its results, every stage has long read it by then.
+        if self.seq - self.done >= RING // 2:
+            raise ChainError("too many chunks in flight")
         tokens = [cur] + list(drafts)
         m = len(tokens)
         io = self.io
-        with io.ordered():
-            io.set_step(pos, m, tokens, list(drafts), self.pending_flags)
-            self.pending_flags = 0
-            io.step()
-            w1 = dist.isend(io.hdr, 1, group=self.links.fwd[0])
-            w2 = dist.isend(io.hid, 1, group=self.links.fwd[0])
-            w1.wait()
-            w2.wait()
-            wr = dist.irecv(self.slots[self.slot], self.world - 1, group=self.links.ret)
-        self.inflight.append((self.slot, m, wr))
-        self.slot = (self.slot + 1) % RING
+        io.set_step(pos, m, tokens, list(drafts), self.pending_flags)
+        io.step()
+        io.send(0, self.seq, m, m | (self.pending_flags << 8))
+        self.pending_flags = 0
+        self.inflight.append(m)
+        self.seq += 1
         self.submitted += 1
 
     def poll(self) -> List[int]:
-        slot, m, wr = self.inflight.popleft()
-        with self.io.ordered():
-            wr.wait()
-            r = self.io.fetch(self.slots[slot])
+        m = self.inflight.popleft()
+        k = self.done
+        self.mem.wait(self.world - 1, k)
+        r = self.mem.result_ints(k).tolist()
+        self.done += 1
         if r[RES_NONFINITE] or r[RES_STATUS] & 8:
             raise NonFiniteLogits("the shard produced missing or non-finite logits")
         if r[RES_STATUS] & 5:
@@ -341,7 +446,7 @@ class DistChain:
             piece = prompt[pos:pos + take]
             self.submit(pos, piece[0], piece[1:])
             pos += take
-            while len(self.inflight) > RING // 2:
+            while len(self.inflight) >= RING // 2:
                 self.poll()
         last = 0
         while self.inflight:
@@ -356,15 +461,13 @@ class DistChain:
         return is_eos(t)
 
     def stop(self) -> None:
-        """End the session on every stage (a header with m = 0 carries any pending marks)."""
+        """End the session on every stage (a chunk with m = 0 carries any pending marks)."""
+        if self.closed:
+            return
         while self.inflight:
-            slot, m, wr = self.inflight.popleft()
-            with self.io.ordered():
-                wr.wait()
-        stop = self.io.stop_header(self.pending_flags)
-        with self.io.ordered():
-            w1 = dist.isend(stop, 1, group=self.links.fwd[0])
-            w2 = dist.isend(self.io.hid, 1, group=self.links.fwd[0])
-            w1.wait()
-            w2.wait()
-        self.io.drain()
+            self.poll()
+        self.io.send(0, self.seq, 0, self.pending_flags << 8)
+        self.pending_flags = 0
+        self.io.finish()
+        self.io.detach()
+        self.closed = True

@@ -367,6 +367,32 @@ class Shard:
             check(st, self._h, "result_wait")
         return self._result(m, None)
 
+    # ---- cross-process link (pipeline stages in different processes of one box) ----
+    def inbox_export(self, slots: int) -> bytes:
+        """Allocate this stage's inbox of `slots` chunk slots; its CUDA IPC handle (64 bytes)."""
+        h = ctypes.create_string_buffer(64)
+        check(self._L.pp_shard_inbox_export(self._h, slots, h), self._h, "inbox_export")
+        return h.raw
+
+    def outbox_open(self, handle: bytes, slots: int) -> None:
+        """Open the next stage's inbox (its IPC handle) as this stage's outbox."""
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        check(self._L.pp_shard_outbox_open(self._h, buf, slots), self._h, "outbox_open")
+
+    def send(self, seq: int, m: int, mail_ptr: int, info: int) -> None:
+        """Enqueue: the chunk's header and m hidden rows into slot seq of the next stage's inbox,
+        then mail[1] = info and mail[0] = seq + 1 (mail_ptr: registered host memory)."""
+        check(self._L.pp_shard_send(self._h, seq, m, mail_ptr, info), self._h, "send")
+
+    def recv(self, seq: int, m: int) -> None:
+        """Enqueue: slot seq of this stage's inbox into its input and header buffers."""
+        check(self._L.pp_shard_recv(self._h, seq, m), self._h, "recv")
+
+    def send_result(self, host_ptr: int, mail_ptr: int, value: int) -> None:
+        """Enqueue: the step result into host memory at host_ptr, then *mail = value."""
+        check(self._L.pp_shard_send_result(self._h, host_ptr, mail_ptr, value), self._h,
+              "send_result")
+
     def read_result(self, m: int, stream: int = 0, logits: bool = False) -> VerifyResult:
         lg = np.empty((m, self.cfg.vocab_size), np.float32) if logits else None
         vo = self._verify_struct(lg)

@@ -1,5 +1,6 @@
-"""The multi-process pipeline protocol (potpori_b200/distchain.py) on CPU: gloo ranks, host
-stand-ins for the shards (HostStageIO), no GPU.
+"""The multi-process pipeline protocol (potpori_b200/distchain.py) on CPU: gloo ranks for the
+setup, host stand-ins for the shards (HostStageIO) whose inboxes and mailboxes live in the
+chain's shared memory, no GPU.
 
 Checks what the chain of src/node.rs:242-342,466-535 must keep when its stages are separate
 processes: every chunk's header and hidden rows go rank r -> r+1 in order, the last rank's
@@ -44,20 +45,19 @@ class FakeStage:
 def _worker(rank: int, world: int, port: int, q) -> None:
     import torch.distributed as dist
     from potpori_b200.distchain import (FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain,
-                                        HostStageIO, Links, run_stage)
+                                        HostStageIO, run_stage)
     from potpori_b200.target import NonFiniteLogits
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        links = Links(world)
         io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
                          first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH,
                          layer_range=(rank, rank + 1), model_layers=world)
         if rank != 0:
-            q.put((rank, "ms", run_stage(None, rank, world, WIDTH, links, io=io)))
+            q.put((rank, "ms", run_stage(None, rank, world, WIDTH, io=io)))
             return
-        chain = DistChain(None, world, WIDTH, links, io=io)
+        chain = DistChain(None, world, WIDTH, io=io)
         prompt = list(range(10, 29))  # 19 tokens: two 8-row chunks, then three single rows
         assert chain.prefill(prompt) == prompt[-1] + world
         # three chunks in flight, then read in order
@@ -120,12 +120,11 @@ def test_pipeline_protocol_over_gloo(world):
 def _hello_worker(rank: int, world: int, port: int, bad: str, q) -> None:
     import torch.distributed as dist
     from potpori_b200.chain import HandshakeError
-    from potpori_b200.distchain import DistChain, HostStageIO, Links, run_stage
+    from potpori_b200.distchain import DistChain, HostStageIO, run_stage
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        links = Links(world)
         cap, chunk, rng, layers = 256, WIDTH, (rank, rank + 1), world
         if rank == world - 1:  # the last stage is set up differently
             if bad == "chunk":
@@ -142,9 +141,9 @@ def _hello_worker(rank: int, world: int, port: int, bad: str, q) -> None:
                          layer_range=rng, model_layers=layers)
         try:
             if rank == 0:
-                DistChain(None, world, WIDTH, links, io=io)
+                DistChain(None, world, WIDTH, io=io)
             else:
-                run_stage(None, rank, world, WIDTH, links, io=io)
+                run_stage(None, rank, world, WIDTH, io=io)
             q.put((rank, "refused", None))
         except HandshakeError as e:
             q.put((rank, "refused", str(e)))
