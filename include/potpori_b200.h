@@ -212,16 +212,33 @@ pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
 pp_status pp_shard_set_sm_limit(pp_shard* shard, uint32_t ctas);
 uint32_t pp_shard_sm_limit(const pp_shard* shard);
 
-/* Prompt prefill of a shard that holds every layer: positions pos .. pos + t - 1 (t <= 2048)
- * of the prompt `tokens` go through all layers at once and their K/V rows are written into
- * the cache, as the reference's prefill does in chunk-sized verify steps
- * (src/qwen/target.rs:62-84). The projections run on the tensor cores (pp_rows_gemm), the
- * causal attention flash-style over the whole chunk. It produces no logits: the caller
- * runs the last prompt token as a 1-row step (pp_shard_forward_tokens) for its greedy pick.
- * Allocates its row buffers (about 0.2 GB for Qwen3-0.6B, 0.5 GB for 4B) on first use.
- * PP_E_UNSUPPORTED for a shard without every layer, with a head size other than 128 or with
- * other than 1, 2, 4 or 8 query heads per KV head. Synchronous. */
+/* Prompt prefill of a first shard: positions pos .. pos + t - 1 (t <= 2048) of the prompt
+ * `tokens` go through all its layers at once and their K/V rows are written into the cache,
+ * as the reference's prefill does in chunk-sized verify steps (src/qwen/target.rs:62-84,
+ * src/node.rs:538-566). The projections run on the tensor cores (pp_rows_gemm), the causal
+ * attention flash-style over the whole chunk. It produces no logits: the caller runs the last
+ * prompt token as a 1-row step for its greedy pick. A shard that is not the last leaves the t
+ * output rows of its last layer in its prefill buffer for the next stage. Allocates its row
+ * buffers (about 0.2 GB for Qwen3-0.6B, 0.5 GB for 4B) on first use. PP_E_UNSUPPORTED for a
+ * head size other than 128 or other than 1, 2, 4 or 8 query heads per KV head. Synchronous. */
 pp_status pp_shard_prefill(pp_shard* shard, uint32_t pos, const int32_t* tokens, uint32_t t);
+/* The same pass on a later stage over the t rows in its prefill buffer, which
+ * pp_shard_prefill_handoff (same process) or pp_shard_prefill_send (another process) filled,
+ * or `hidden` ([t][hidden] F32 host rows, finite) when not NULL. Synchronous. */
+pp_status pp_shard_prefill_hidden(pp_shard* shard, uint32_t pos, uint32_t t, const float* hidden);
+/* The t output rows a prefill pass left in a shard that is not the last ([t][hidden] F32). */
+pp_status pp_shard_prefill_read(pp_shard* shard, uint32_t t, float* out);
+/* Copy `from`'s t prefill output rows into the prefill buffer of the next stage `to` (a peer
+ * copy when the devices differ). */
+pp_status pp_shard_prefill_handoff(pp_shard* from, pp_shard* to, uint32_t t);
+/* Across processes: the receiving stage exports its prefill buffer (64-byte CUDA IPC handle),
+ * the sending stage opens it and, after its pass, copies its t output rows into it on the
+ * copy engines, then writes the mailbox words (mail[1] = info, mail[0] = seq + 1) as
+ * pp_shard_send does. */
+pp_status pp_shard_prefill_export(pp_shard* shard, void* handle);
+pp_status pp_shard_prefill_open(pp_shard* shard, const void* handle);
+pp_status pp_shard_prefill_send(pp_shard* shard, uint32_t seq, uint32_t t, uint32_t* mail,
+                                uint32_t info);
 
 /* Run every 1-row step of a shard that holds all layers (a draft model's greedy decode, the
  * single-token verify steps) as one persistent cooperative kernel over the shard's SM budget
@@ -273,6 +290,14 @@ pp_status pp_rows_gemm(const uint16_t* w_tiled, uint32_t n, uint32_t k, const fl
 pp_status pp_norm_gemv_static(const uint16_t* w_tiled, const float* x, const float* norm_w,
                               float eps, uint32_t n, uint32_t k, uint32_t m, float* y,
                               uint32_t* err, void* stream);
+
+/* Test hook of the decode kernel's bounded waits (no counterpart in the reference; the
+ * reference bounds its own waits, src/node.rs:47-50): limit_us sets the time limit of its grid
+ * and head barriers (0: the default 200 ms); unreachable = 1 makes every grid barrier wait for
+ * one CTA more than the grid has, so the step's first barrier can only end by running out of
+ * time: the kernel then records the timeout, drains its copies and returns, and the step
+ * reports PP_E_TIMEOUT. The shard stays usable; unreachable = 0 restores normal steps. */
+pp_status pp_shard_set_wait_test(pp_shard* shard, uint32_t limit_us, int32_t unreachable);
 
 /* Tapped-layer outputs: TappedShards (src/node.rs:108-223) and LayerTap
  * (src/transport.rs:148-179). After every step the output rows [m][hidden] of each layer in

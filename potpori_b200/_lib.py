@@ -31,9 +31,11 @@ EXPORTS = [
     "pp_shard_model_layers", "pp_shard_device_bytes", "pp_shard_last_launches",
     "pp_shard_profile_kernels", "pp_shard_stream", "pp_shard_set_graphs", "pp_shard_set_pdl",
     "pp_shard_set_sm_limit", "pp_shard_sm_limit", "pp_shard_decode_greedy",
-    "pp_shard_prefill", "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
+    "pp_shard_prefill", "pp_shard_prefill_hidden", "pp_shard_prefill_read",
+    "pp_shard_prefill_handoff", "pp_shard_prefill_export", "pp_shard_prefill_open",
+    "pp_shard_prefill_send", "pp_shard_set_decode_kernel", "pp_shard_decode_kernel",
     "pp_rows_gemm_work_bytes", "pp_rows_gemm", "pp_norm_gemv_static", "pp_shard_set_taps",
-    "pp_shard_tap_layers", "pp_shard_read_taps", "pp_shard_inbox_export", "pp_shard_outbox_open",
+    "pp_shard_tap_layers", "pp_shard_read_taps", "pp_shard_set_wait_test", "pp_shard_inbox_export", "pp_shard_outbox_open",
     "pp_shard_send", "pp_shard_recv", "pp_shard_send_result", "pp_host_register",
     "pp_host_unregister", "pp_last_error", "pp_version",
 ]
@@ -126,6 +128,12 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_sm_limit": (I32, [P, U32]),
         "pp_shard_sm_limit": (U32, [P]),
         "pp_shard_prefill": (I32, [P, U32, pI32, U32]),
+        "pp_shard_prefill_hidden": (I32, [P, U32, U32, P]),
+        "pp_shard_prefill_read": (I32, [P, U32, P]),
+        "pp_shard_prefill_handoff": (I32, [P, P, U32]),
+        "pp_shard_prefill_export": (I32, [P, P]),
+        "pp_shard_prefill_open": (I32, [P, P]),
+        "pp_shard_prefill_send": (I32, [P, U32, U32, P, U32]),
         "pp_shard_set_decode_kernel": (I32, [P, I32]),
         "pp_shard_decode_kernel": (I32, [P]),
         "pp_shard_decode_greedy": (I32, [P, U32, I32, U32, pI32]),
@@ -135,6 +143,7 @@ def load() -> ctypes.CDLL:
         "pp_shard_set_taps": (I32, [P, ctypes.POINTER(U32), U32]),
         "pp_shard_tap_layers": (U32, [P, ctypes.POINTER(U32), U32]),
         "pp_shard_read_taps": (I32, [P, U32, P, P]),
+        "pp_shard_set_wait_test": (I32, [P, U32, I32]),
         "pp_shard_inbox_export": (I32, [P, U32, P]),
         "pp_shard_outbox_open": (I32, [P, P, U32]),
         "pp_shard_send": (I32, [P, U32, U32, P, U32]),

@@ -104,16 +104,24 @@ class LocalChain:
             raise NonFiniteLogits("the shard produced missing or non-finite logits")
         return r.argmax
 
-    def prefill(self, prompt: List[int]) -> int:
+    def prefill(self, prompt: List[int], one_pass: bool = True) -> int:
         """The greedy pick after the prompt. The reference streams the prompt through the
-        chain in chunk-sized steps (src/node.rs:538-566); a one-shard chain whose shard can
-        (Shard.can_prefill) writes the K/V rows of all but the last token in one pass instead
-        and submits the last token as the step that yields the pick."""
-        if len(self.stages) == 1 and len(prompt) > 1 and self.stages[0].can_prefill():
+        chain in chunk-sized steps (src/node.rs:538-566); when every stage can
+        (Shard.can_prefill), the stages write the K/V rows of all but the last token in one
+        pass each instead, the output rows of each stage handed to the next (a peer copy
+        across devices), and the last token is submitted as the step that yields the pick.
+        Several stages take up to 2048 prompt rows in one pass; one stage any number.
+        one_pass=False keeps the chunked steps."""
+        n = len(prompt) - 1
+        if (one_pass and n > 0 and all(s.can_prefill() for s in self.stages)
+                and (len(self.stages) == 1 or n <= Shard.PREFILL_MAX)):
             while self.inflight:
                 self.poll()
             self.stages[0].prefill(0, prompt[:-1])
-            self.submit(len(prompt) - 1, prompt[-1], [])
+            for prev, st in zip(self.stages, self.stages[1:]):
+                st.prefill_handoff_from(prev, n)
+                st.prefill_hidden(0, n)
+            self.submit(n, prompt[-1], [])
             return self.poll()[-1]
         pos = 0
         while pos < len(prompt):

@@ -39,7 +39,7 @@ namespace pp {
 
 constexpr int kDecSlot = 32768;           // bytes per ring slot
 constexpr int kDecKvHalf = kDecSlot / 2;  // K rows at 0, V rows at 16 KB of a K/V slot
-constexpr uint64_t kDecBarrierNs = 200ull * 1000 * 1000;  // grid barrier time limit
+constexpr uint64_t kDecBarrierNs = 200ull * 1000 * 1000;  // default barrier time limit
 constexpr int kDecKAlign = 512;           // K of the weight copies: a multiple of 8 warps x 64
 constexpr int kDecHd = 128;               // head size the attention takes
 
@@ -78,6 +78,8 @@ struct DecodeArgs {
   int32_t kH, kQ, kI;  // K of the weight copies (dec_kpad of H, Q, I)
   int32_t kO;          // K of the per-head O copy: G * head_dim
   int32_t vec_floats;  // floats of the staged-vector region
+  int32_t extra_arrivals;  // added to every grid barrier's target (a test of the time limit)
+  uint64_t wait_ns;        // time limit of the grid and head barriers
   float eps, inv_scale;
   const uint16_t* embed;    // tiled embedding table (tiled_offset layout)
   const float* final_norm;  // NULL: no head operand
@@ -437,6 +439,7 @@ __device__ __forceinline__ bool dec_grid_sync(const DecodeArgs& a, uint32_t targ
   if (tid == 0) {
     int ok = 1;
     red_release_gpu(&a.sync[0], 1);
+    target += (uint32_t)a.extra_arrivals;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t n = 1; ld_acquire_gpu(&a.sync[0]) < target; ++n) {
       if ((n & 63) == 0) {
@@ -444,7 +447,7 @@ __device__ __forceinline__ bool dec_grid_sync(const DecodeArgs& a, uint32_t targ
           ok = 0;
           break;
         }
-        if (global_timer_ns() - t0 > kDecBarrierNs) {
+        if (global_timer_ns() - t0 > a.wait_ns) {
           atomicOr(&a.res->status, ST_TIMEOUT);
           atomicExch(&a.sync[1], 1u);
           ok = 0;
@@ -696,7 +699,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
           ok = 0;
           break;
         }
-        if (global_timer_ns() - t0 > kDecBarrierNs) {
+        if (global_timer_ns() - t0 > a.wait_ns) {
           atomicOr(&a.res->status, ST_TIMEOUT);
           atomicExch(&a.sync[1], 1u);
           ok = 0;

@@ -176,6 +176,7 @@ struct pp_shard {
   uint32_t inbox_slots = 0;
   uint8_t* outbox = nullptr;
   uint32_t outbox_slots = 0;
+  float* pf_peer = nullptr;  // the next stage's prefill rows, opened through CUDA IPC
   uint32_t desc_next = 0;
   float* h_stage = nullptr;  // pinned [kMaxRows][H]
   int splits = 1, nq_max = 1;
@@ -198,6 +199,8 @@ struct pp_shard {
   uint32_t* dec_sync = nullptr;
   int dec_vec = 0;
   size_t dec_budget = 0;  // dynamic shared memory the decode kernel may use
+  uint64_t dec_wait_ns = kDecBarrierNs;  // barrier time limit (pp_shard_set_wait_test)
+  int32_t dec_unreachable = 0;           // 1: the grid barriers wait for one CTA too many
   // Prompt prefill (pp_shard_prefill): F32 row buffers for up to kPrefillMax rows, the
   // projections' activation blocks (work) and error word, the prompt's tokens.
   struct {
@@ -658,6 +661,8 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   a.vec_floats = s->dec_vec;
   a.eps = s->d.cfg.rms_norm_eps;
   a.inv_scale = 1.0f / sqrtf((float)s->hd);
+  a.extra_arrivals = s->dec_unreachable;
+  a.wait_ns = s->dec_wait_ns;
   a.embed = s->embed;
   a.final_norm = s->final_norm;
   a.rope = s->rope;
@@ -733,12 +738,13 @@ pp_status prefill_gemm(pp_shard* s, const uint16_t* w, int n, int k, int t, floa
   return PP_OK;
 }
 
-// Every layer of a whole-model shard over t prompt rows at positions pos.. (embedding, and per
-// layer RMSNorm into activation blocks, tcgen05 QKV, QK-norm + RoPE + K/V rows into the cache,
-// flash-style causal attention over the whole chunk into activation blocks, tcgen05 O added
-// to the residual rows, RMSNorm into blocks, tcgen05 gate/up, SwiGLU into blocks, tcgen05 down
-// added to the residual rows; the last layer stops after its K/V rows, which is all a
-// prefill leaves behind).
+// Every layer of a shard over t prompt rows at positions pos.. (embedding on the first shard,
+// else the input rows already in pf.x; per layer RMSNorm into activation blocks, tcgen05 QKV,
+// QK-norm + RoPE + K/V rows into the cache, flash-style causal attention over the whole chunk
+// into activation blocks, tcgen05 O added to the residual rows, RMSNorm into blocks, tcgen05
+// gate/up, SwiGLU into blocks, tcgen05 down added to the residual rows; the model's last
+// layer stops after its K/V rows, which is all a prefill leaves behind, and a shard before
+// the last leaves its output rows in pf.x for the next stage).
 pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   cudaStream_t st = s->stream;
   const int H = s->H, Q = s->Q, KV = s->KV, I = s->I, hd = s->hd;
@@ -748,8 +754,10 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
   pp_status r;
   CK(cudaMemsetAsync(s->pf.err, 0, 4, st));
   CK(cudaMemsetAsync(s->d_res, 0, sizeof(StepResult), st));
-  pp_pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
-  CK(cudaGetLastError());
+  if (s->first) {  // a later stage finds its input rows in pf.x
+    pp_pre_embed_kernel<<<t, 256, 0, st>>>(s->embed, (int32_t)(s->Hp / kChunkK), s->pf.tokens, H, s->pf.x);
+    CK(cudaGetLastError());
+  }
   const int bq = (s->G <= 4 ? 64 : 128) / s->G;  // prompt rows per attention CTA
   const int64_t swiglu_units = (int64_t)t * kcI * 8;
   const int swiglu_grid = (int)((swiglu_units + 255) / 256 < 4096 ? (swiglu_units + 255) / 256 : 4096);
@@ -762,7 +770,7 @@ pp_status enqueue_prefill(pp_shard* s, uint32_t pos, int t) {
         s->pf.qkv, t, (int32_t)pos, s->nh, s->nkv, hd, eps, Ld.norm[N_QN], Ld.norm[N_KN], s->rope,
         Ld.kc, Ld.vc, (int32_t)s->d.capacity, s->pf.q);
     CK(cudaGetLastError());
-    if (l + 1 == s->nl) break;
+    if (l + 1 == s->nl && s->last) break;  // the model's last layer: its K/V rows are all
     const dim3 fgrid(s->nkv, (t + bq - 1) / bq);
     if (s->G <= 4)
       pp_pre_flash_kernel<4, 2><<<fgrid, 128, flash_smem_bytes(4, 2), st>>>(
@@ -1085,6 +1093,7 @@ void pp_shard_destroy(pp_shard* s) {
   for (auto& e : s->exec)
     if (e) cudaGraphExecDestroy(e);
   if (s->outbox) cudaIpcCloseMemHandle(s->outbox);
+  if (s->pf_peer) cudaIpcCloseMemHandle(s->pf_peer);
   if (s->inbox) cudaFree(s->inbox);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_desc) cudaFreeHost(s->h_desc);
@@ -1505,23 +1514,21 @@ pp_status pp_shard_forward_tokens(pp_shard* s, uint32_t pos, const int32_t* toke
   return finish_host_step(s, m, out_hidden, verify);
 }
 
-pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uint32_t t) {
-  if (!s || !tokens) return fail(s, PP_E_INVALID, "null argument");
-  if (!(s->first && s->last))
-    return fail(s, PP_E_UNSUPPORTED, "the prompt prefill runs shards that hold every layer");
+static pp_status write_word(pp_shard* s, uint32_t* host_word, uint32_t value);
+
+static pp_status prefill_check(pp_shard* s, uint32_t pos, uint32_t t) {
   if (s->hd != kFlashHd || (s->G != 1 && s->G != 2 && s->G != 4 && s->G != 8))
     return fail(s, PP_E_UNSUPPORTED, "the prompt prefill takes head size 128 and 1, 2, 4 or 8 query heads per KV head");
   if (t == 0 || t > (uint32_t)kPrefillMax) return fail(s, PP_E_INVALID, "t must be 1..2048 rows");
   if ((uint64_t)pos + t > s->d.capacity) return fail(s, PP_E_INVALID, "chunk exceeds KV capacity");
-  for (uint32_t i = 0; i < t; ++i)  // src/qwen/model.rs:383-389
-    if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
-      return fail(s, PP_E_INVALID, "invalid token input");
   if (pp_shard_missing(s, nullptr, 0))
     return fail(s, PP_E_MISSING, "parameters missing; see pp_shard_missing");
-  CK(cudaSetDevice(s->dev));
-  pp_status r = prefill_alloc(s);
-  if (r) return r;
-  CK(cudaMemcpyAsync(s->pf.tokens, tokens, (size_t)t * 4, cudaMemcpyHostToDevice, s->stream));
+  return PP_OK;
+}
+
+// The prefill pass over the rows staged for it; synchronous.
+static pp_status prefill_run(pp_shard* s, uint32_t pos, uint32_t t) {
+  pp_status r;
   if ((r = enqueue_prefill(s, pos, (int)t))) {
     cudaStreamSynchronize(s->stream);
     return r;
@@ -1532,6 +1539,102 @@ pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uin
   CK(cudaStreamSynchronize(s->stream));
   if (err) return fail(s, PP_E_TIMEOUT, "a bounded wait of the prompt projection expired");
   return status_of(s, *s->h_res);
+}
+
+pp_status pp_shard_prefill(pp_shard* s, uint32_t pos, const int32_t* tokens, uint32_t t) {
+  if (!s || !tokens) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->first) return fail(s, PP_E_INVALID, "token input on a shard that is not the first");
+  pp_status r = prefill_check(s, pos, t);
+  if (r) return r;
+  for (uint32_t i = 0; i < t; ++i)  // src/qwen/model.rs:383-389
+    if (tokens[i] < 0 || (uint32_t)tokens[i] >= (uint32_t)s->V)
+      return fail(s, PP_E_INVALID, "invalid token input");
+  CK(cudaSetDevice(s->dev));
+  if ((r = prefill_alloc(s))) return r;
+  CK(cudaMemcpyAsync(s->pf.tokens, tokens, (size_t)t * 4, cudaMemcpyHostToDevice, s->stream));
+  return prefill_run(s, pos, t);
+}
+
+pp_status pp_shard_prefill_hidden(pp_shard* s, uint32_t pos, uint32_t t, const float* hidden) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  if (s->first) return fail(s, PP_E_INVALID, "hidden input on the first shard");
+  pp_status r = prefill_check(s, pos, t);
+  if (r) return r;
+  CK(cudaSetDevice(s->dev));
+  if ((r = prefill_alloc(s))) return r;
+  if (hidden) {
+    for (size_t i = 0; i < (size_t)t * s->H; ++i)  // src/qwen/model.rs:390-392
+      if (!std::isfinite(hidden[i])) return fail(s, PP_E_INVALID, "invalid hidden input");
+    CK(cudaMemcpyAsync(s->pf.x, hidden, (size_t)t * s->H * 4, cudaMemcpyHostToDevice, s->stream));
+  }
+  return prefill_run(s, pos, t);
+}
+
+pp_status pp_shard_prefill_read(pp_shard* s, uint32_t t, float* out) {
+  if (!s || !out) return fail(s, PP_E_INVALID, "null argument");
+  if (s->last) return fail(s, PP_E_INVALID, "the last shard leaves no output rows");
+  if (!s->pf.x || t == 0 || t > (uint32_t)kPrefillMax) return fail(s, PP_E_INVALID, "no rows");
+  CK(cudaSetDevice(s->dev));
+  CK(cudaMemcpyAsync(out, s->pf.x, (size_t)t * s->H * 4, cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_prefill_handoff(pp_shard* from, pp_shard* to, uint32_t t) {
+  pp_shard* s = to;
+  if (!from || !to) return fail(to, PP_E_INVALID, "null shard");
+  if (from->last || to->first || from->H != to->H || from->d.layer_end != to->d.layer_begin)
+    return fail(to, PP_E_INVALID, "shards are not adjacent stages");
+  if (!from->pf.x || t == 0 || t > (uint32_t)kPrefillMax)
+    return fail(to, PP_E_INVALID, "no prefill rows to hand off");
+  CK(cudaSetDevice(to->dev));
+  pp_status r = prefill_alloc(to);
+  if (r) return r;
+  CK(cudaStreamSynchronize(from->stream));
+  const size_t bytes = (size_t)t * to->H * 4;
+  if (from->dev == to->dev)
+    CK(cudaMemcpyAsync(to->pf.x, from->pf.x, bytes, cudaMemcpyDeviceToDevice, to->stream));
+  else
+    CK(cudaMemcpyPeerAsync(to->pf.x, to->dev, from->pf.x, from->dev, bytes, to->stream));
+  return PP_OK;
+}
+
+pp_status pp_shard_prefill_export(pp_shard* s, void* handle) {
+  if (!s || !handle) return fail(s, PP_E_INVALID, "null argument");
+  if (s->first) return fail(s, PP_E_INVALID, "the first stage takes tokens");
+  CK(cudaSetDevice(s->dev));
+  pp_status r = prefill_alloc(s);
+  if (r) return r;
+  CK(cudaStreamSynchronize(s->stream));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, s->pf.x));
+  memcpy(handle, &h, sizeof h);
+  return PP_OK;
+}
+
+pp_status pp_shard_prefill_open(pp_shard* s, const void* handle) {
+  if (!s || !handle) return fail(s, PP_E_INVALID, "null argument");
+  if (s->last) return fail(s, PP_E_INVALID, "the last stage has no next stage");
+  if (s->pf_peer) return fail(s, PP_E_INVALID, "already open");
+  CK(cudaSetDevice(s->dev));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  void* p = nullptr;
+  CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  s->pf_peer = (float*)p;
+  return PP_OK;
+}
+
+pp_status pp_shard_prefill_send(pp_shard* s, uint32_t seq, uint32_t t, uint32_t* mail,
+                                uint32_t info) {
+  if (!s || !mail) return fail(s, PP_E_INVALID, "null argument");
+  if (!s->pf_peer || !s->pf.x) return fail(s, PP_E_INVALID, "no prefill link: pp_shard_prefill_open first");
+  if (t == 0 || t > (uint32_t)kPrefillMax) return fail(s, PP_E_INVALID, "t must be 1..2048 rows");
+  CK(cudaSetDevice(s->dev));
+  CK(cudaMemcpyAsync(s->pf_peer, s->pf.x, (size_t)t * s->H * 4, cudaMemcpyDeviceToDevice, s->stream));
+  pp_status r;
+  if ((r = write_word(s, mail + 1, info))) return r;
+  return write_word(s, mail, seq + 1);
 }
 
 pp_status pp_shard_decode_greedy(pp_shard* s, uint32_t pos, int32_t token, uint32_t n,
@@ -1955,6 +2058,14 @@ int32_t pp_shard_decode_kernel(const pp_shard* s) { return s && s->dec_on ? 1 : 
 pp_status pp_shard_set_pdl(pp_shard* s, int32_t enabled) {
   if (!s) return fail(s, PP_E_INVALID, "null shard");
   s->use_pdl = enabled != 0;
+  drop_graphs(s);
+  return PP_OK;
+}
+
+pp_status pp_shard_set_wait_test(pp_shard* s, uint32_t limit_us, int32_t unreachable) {
+  if (!s) return fail(s, PP_E_INVALID, "null shard");
+  s->dec_wait_ns = limit_us ? (uint64_t)limit_us * 1000 : kDecBarrierNs;
+  s->dec_unreachable = unreachable ? 1 : 0;
   drop_graphs(s);
   return PP_OK;
 }

@@ -51,6 +51,8 @@ RES_SLOT = 256  # bytes per result slot
 RING = 64       # chunk slots of every inbox and of the result ring
 FLAG_WINDOW_START = 2
 FLAG_WINDOW_END = 4
+FLAG_PREFILL = 8  # the message is a prompt prefill: (pos, rows) in the link's parameter slot
+PREFILL_MAX = 2048  # rows of one prefill message
 WAIT_S = 120.0  # a stage that hears nothing for this long ends the session with an error
 
 
@@ -64,12 +66,14 @@ class ChainMemory:
     a result slot per chunk) and, when `data_bytes` is given, the inbox data of host stand-ins
     (RING slots of data_bytes per link). info = rows | flags << 8."""
 
-    def __init__(self, world: int, path: str, create: bool, data_bytes: int = 0):
+    def __init__(self, world: int, path: str, create: bool, data_bytes: int = 0,
+                 extra_bytes: int = 0):
         self.world, self.path, self.data_bytes = world, path, data_bytes
         self.n_words = world * RING * 2  # world - 1 links + the result ring
         self.res_off = self.n_words * 4
-        self.data_off = self.res_off + RING * RES_SLOT
-        self.size = self.data_off + (world - 1) * RING * data_bytes
+        self.par_off = self.res_off + RING * RES_SLOT  # (pos, rows) of prefill messages
+        self.data_off = self.par_off + world * RING * 8
+        self.size = self.data_off + (world - 1) * RING * data_bytes + extra_bytes
         fd = os.open(path, os.O_RDWR | (os.O_CREAT if create else 0), 0o600)
         try:
             if create:
@@ -87,6 +91,11 @@ class ChainMemory:
     def mail(self, link: int, k: int) -> int:
         """Word index of chunk k's mailbox on link `link` (link world - 1: the results)."""
         return (link * RING + k % RING) * 2
+
+    def params(self, link: int, k: int) -> np.ndarray:
+        """The (pos, rows) words of prefill message k on `link`, written by the sender's host
+        before it enqueues the message (so before its mailbox word can be seen)."""
+        return np.ndarray((2,), np.uint32, self.mm, self.par_off + (link * RING + k % RING) * 8)
 
     def result_ints(self, k: int) -> np.ndarray:
         return np.ndarray((RES_INTS,), np.int32, self.mm, self.res_off + (k % RING) * RES_SLOT)
@@ -172,6 +181,25 @@ class CudaStageIO:
         mem = self.mem
         self.shard.send_result(mem.base + mem.res_off + (k % RING) * RES_SLOT,
                                mem.base + mem.mail(mem.world - 1, k) * 4, k + 1)
+
+    def can_prefill(self) -> bool:
+        return self.shard.can_prefill()
+
+    def export_prefill(self) -> bytes:
+        return self.shard.prefill_export()
+
+    def open_prefill(self, handle: bytes) -> None:
+        self.shard.prefill_open(handle)
+
+    def prefill_first(self, pos: int, tokens) -> None:
+        self.shard.prefill(pos, tokens)
+
+    def prefill_rows(self, pos: int, t: int) -> None:
+        self.shard.prefill_hidden(pos, t)
+
+    def prefill_send(self, link: int, k: int, t: int, info: int) -> None:
+        mem = self.mem
+        self.shard.prefill_send(k, t, mem.base + mem.mail(link, k) * 4, info)
 
     def mark_start(self) -> None:
         self._t0.record(self.stream)
@@ -272,6 +300,39 @@ class HostStageIO:
         mem.result_ints(k)[:] = self.res.numpy()
         mem.words[mem.mail(mem.world - 1, k)] = (k + 1) & 0xFFFFFFFF
 
+    def can_prefill(self) -> bool:
+        return hasattr(self.stage, "prefill")
+
+    def export_prefill(self) -> bytes:
+        return b""
+
+    def open_prefill(self, handle: bytes) -> None:
+        pass
+
+    def _rows(self, rank: int) -> np.ndarray:
+        mem = self.mem
+        off = mem.data_off + (mem.world - 1) * RING * mem.data_bytes + rank * self._pf_bytes()
+        return np.ndarray((PREFILL_MAX, self.hidden), np.float32, mem.mm, off)
+
+    def _pf_bytes(self) -> int:
+        return PREFILL_MAX * self.hidden * 4
+
+    def extra_bytes(self, world: int) -> int:
+        return world * self._pf_bytes()
+
+    def prefill_first(self, pos: int, tokens) -> None:
+        self.stage.prefill(pos, np.asarray(tokens), self._rows(self.rank))
+
+    def prefill_rows(self, pos: int, t: int) -> None:
+        self.stage.prefill(pos, None, self._rows(self.rank)[:t])
+
+    def prefill_send(self, link: int, k: int, t: int, info: int) -> None:
+        mem = self.mem
+        self._rows(self.rank + 1)[:t] = self._rows(self.rank)[:t]
+        i = mem.mail(link, k)
+        mem.words[i + 1] = info
+        mem.words[i] = (k + 1) & 0xFFFFFFFF
+
     def mark_start(self) -> None:
         self._t0 = time.perf_counter()
 
@@ -334,19 +395,26 @@ def connect(io, rank: int, world: int) -> ChainMemory:
     opened on the next stage's inbox."""
     negotiate(io, rank, world)
     io.rank = rank
+    can = io.can_prefill()
     mine = {"inbox": io.export_inbox() if rank > 0 else b"", "data": io.data_bytes(),
+            "extra": io.extra_bytes(world) if hasattr(io, "extra_bytes") else 0,
+            "prefill": io.export_prefill() if rank > 0 and can else b"", "can": can,
             "path": f"/dev/shm/potpori_chain_{uuid.uuid4().hex}" if rank == 0 else ""}
     every = [None] * world
     dist.all_gather_object(every, mine)
     path = every[0]["path"]
     data = max(v["data"] for v in every)
-    mem = ChainMemory(world, path, True, data) if rank == 0 else None
+    extra = max(v["extra"] for v in every)
+    mem = ChainMemory(world, path, True, data, extra) if rank == 0 else None
     dist.barrier()
     if rank != 0:
-        mem = ChainMemory(world, path, False, data)
+        mem = ChainMemory(world, path, False, data, extra)
     io.attach(mem)
+    mem.can_prefill = all(v["can"] for v in every)
     if rank + 1 < world:
         io.open_outbox(every[rank + 1]["inbox"])
+        if mem.can_prefill:
+            io.open_prefill(every[rank + 1]["prefill"])
     dist.barrier()
     if rank == 0:  # every rank has mapped it: the name can go
         os.unlink(path)
@@ -364,6 +432,16 @@ def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
         while True:
             info = mem.wait(rank - 1, k)
             m, flags = info & 0xFF, info >> 8
+            if flags & FLAG_PREFILL:
+                # The prompt's rows through this stage in one pass, then on to the next
+                # (src/node.rs:538-566 streams them in chunk-sized frames instead).
+                pos, t = (int(v) for v in mem.params(rank - 1, k))
+                io.prefill_rows(pos, t)
+                if not io.last:
+                    mem.params(rank, k)[:] = (pos, t)
+                    io.prefill_send(rank, k, t, info)
+                k += 1
+                continue
             if flags & FLAG_WINDOW_START and not started:
                 io.mark_start()
                 started = True
@@ -423,23 +501,38 @@ class DistChain:
         io.step()
         io.send(0, self.seq, m, m | (self.pending_flags << 8))
         self.pending_flags = 0
-        self.inflight.append(m)
+        self.inflight.append((self.seq, m))
         self.seq += 1
         self.submitted += 1
 
     def poll(self) -> List[int]:
-        m = self.inflight.popleft()
-        k = self.done
+        k, m = self.inflight.popleft()
         self.mem.wait(self.world - 1, k)
         r = self.mem.result_ints(k).tolist()
-        self.done += 1
+        self.done = k + 1
         if r[RES_NONFINITE] or r[RES_STATUS] & 8:
             raise NonFiniteLogits("the shard produced missing or non-finite logits")
         if r[RES_STATUS] & 5:
             raise RuntimeError(f"chain step failed (status {r[RES_STATUS]})")
         return r[:m]
 
-    def prefill(self, prompt: List[int]) -> int:
+    def prefill(self, prompt: List[int], one_pass: bool = True) -> int:
+        """The greedy pick after the prompt. When every stage can (Shard.can_prefill) and the
+        prompt has at most 2049 tokens, each stage writes the K/V rows of all but the last token
+        in one pass and sends its output rows on (one prefill message per link); the last token
+        is then submitted as the step that yields the pick. Otherwise, or with one_pass=False,
+        the prompt goes in chunk-sized steps, as the reference streams it
+        (src/node.rs:538-566)."""
+        n = len(prompt) - 1
+        if one_pass and 0 < n <= PREFILL_MAX and self.mem.can_prefill:
+            while self.inflight:
+                self.poll()
+            self.io.prefill_first(0, prompt[:-1])
+            self.mem.params(0, self.seq)[:] = (0, n)
+            self.io.prefill_send(0, self.seq, n, FLAG_PREFILL << 8)
+            self.seq += 1
+            self.submit(n, prompt[-1], [])
+            return self.poll()[-1]
         pos = 0
         while pos < len(prompt):
             take = self.chunk if len(prompt) - pos >= self.chunk else 1

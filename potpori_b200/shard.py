@@ -243,19 +243,50 @@ class Shard:
     PREFILL_MAX = 2048
 
     def can_prefill(self) -> bool:
-        """Whether prefill() runs here: a shard with every layer, head size 128 and 1, 2, 4 or 8
-        query heads per KV head (every Qwen3 size)."""
+        """Whether the one-pass prefill runs here: head size 128 and 1, 2, 4 or 8 query heads
+        per KV head (every Qwen3 size)."""
         cfg = self.cfg
-        return (self.first and self.last and cfg.head_dim == 128
-                and cfg.n_heads // cfg.n_kv_heads in (1, 2, 4, 8))
+        return cfg.head_dim == 128 and cfg.n_heads // cfg.n_kv_heads in (1, 2, 4, 8)
 
     def prefill(self, pos: int, tokens: Sequence[int]) -> None:
-        """Write the K/V rows of prompt tokens at pos.. through every layer at once (tensor-core
-        projections), in pieces of up to 2048 rows; no logits."""
+        """First shard: write the K/V rows of prompt tokens at pos.. through every layer at once
+        (tensor-core projections), in pieces of up to 2048 rows; no logits. A shard before the
+        last keeps the output rows of its last layer for the next stage (one piece)."""
         for i in range(0, len(tokens), self.PREFILL_MAX):
             piece = np.asarray(tokens[i:i + self.PREFILL_MAX], np.int32)
             check(self._L.pp_shard_prefill(self._h, pos + i, piece.ctypes.data_as(
                 ctypes.POINTER(ctypes.c_int32)), len(piece)), self._h, f"prefill(pos={pos + i})")
+
+    def prefill_hidden(self, pos: int, t: int, hidden=None) -> None:
+        """Later stage: the prefill pass over t rows in its prefill buffer (filled by a
+        handoff or a send), or over `hidden` [t, hidden] when given."""
+        hp = None
+        if hidden is not None:
+            h = np.ascontiguousarray(np.asarray(hidden, np.float32)).reshape(t, self.cfg.hidden)
+            hp = h.ctypes.data
+        check(self._L.pp_shard_prefill_hidden(self._h, pos, t, hp), self._h,
+              f"prefill_hidden(pos={pos}, t={t})")
+
+    def prefill_read(self, t: int) -> np.ndarray:
+        out = np.empty((t, self.cfg.hidden), np.float32)
+        check(self._L.pp_shard_prefill_read(self._h, t, out.ctypes.data), self._h, "prefill_read")
+        return out
+
+    def prefill_handoff_from(self, prev: "Shard", t: int) -> None:
+        check(self._L.pp_shard_prefill_handoff(prev._h, self._h, t), self._h, "prefill_handoff")
+
+    def prefill_export(self) -> bytes:
+        h = ctypes.create_string_buffer(64)
+        check(self._L.pp_shard_prefill_export(self._h, h), self._h, "prefill_export")
+        return h.raw
+
+    def prefill_open(self, handle: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(handle), 64)
+        check(self._L.pp_shard_prefill_open(self._h, buf), self._h, "prefill_open")
+
+    def prefill_send(self, seq: int, t: int, mail_ptr: int, info: int) -> None:
+        check(self._L.pp_shard_prefill_send(self._h, seq, t, mail_ptr, info), self._h,
+              "prefill_send")
 
     def set_decode_kernel(self, enabled: bool = True) -> None:
         """Run 1-row steps of this whole-model shard as one persistent kernel (plus the vocab
@@ -265,6 +296,12 @@ class Shard:
 
     def decode_kernel(self) -> bool:
         return bool(self._L.pp_shard_decode_kernel(self._h))
+
+    def set_wait_test(self, limit_us: int = 0, unreachable: bool = False) -> None:
+        """Test hook: the decode kernel's barrier time limit (0: default) and, with
+        `unreachable`, barriers that can only end by running out of time."""
+        check(self._L.pp_shard_set_wait_test(self._h, int(limit_us), int(bool(unreachable))),
+              self._h, "set_wait_test")
 
     def _verify_struct(self, want_logits: Optional[np.ndarray]):
         vo = self._vo

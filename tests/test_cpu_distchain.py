@@ -5,8 +5,9 @@ chain's shared memory, no GPU.
 Checks what the chain of src/node.rs:242-342,466-535 must keep when its stages are separate
 processes: every chunk's header and hidden rows go rank r -> r+1 in order, the last rank's
 result comes straight back to rank 0, several chunks are in flight at once (the depth of
-src/specpipe.rs:83-127), prefill feeds the prompt in 8-row chunks and single rows, the timed
-window marks ride on the headers to every stage, a non-finite result surfaces at the head as
+src/specpipe.rs:83-127), prefill feeds the prompt in 8-row chunks and single rows (or, when
+every stage can, all but its last token as one prefill message per link), the timed window
+marks ride on the headers to every stage, a non-finite result surfaces at the head as
 NonFiniteLogits, and the stop header ends every rank.
 """
 import multiprocessing as mp
@@ -42,7 +43,25 @@ class FakeStage:
                 res[48] = 1
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:
+class PrefillStage(FakeStage):
+    """FakeStage that also takes a whole prompt in one pass: the first writes the tokens into
+    column 0 of its output rows, every stage adds 1, and each records what it saw."""
+
+    def __init__(self, first: bool, last: bool):
+        super().__init__(first, last)
+        self.prefilled = []
+
+    def prefill(self, pos, tokens, rows):
+        if self.first:
+            t = len(tokens)
+            rows[:t, 0] = tokens
+        else:
+            t = len(rows)
+        rows[:t, 0] += 1.0
+        self.prefilled.append((pos, t, rows[:t, 0].astype(int).tolist()))
+
+
+def _worker(rank: int, world: int, port: int, one_pass: bool, q) -> None:
     import torch.distributed as dist
     from potpori_b200.distchain import (FLAG_WINDOW_END, FLAG_WINDOW_START, DistChain,
                                         HostStageIO, run_stage)
@@ -51,14 +70,20 @@ def _worker(rank: int, world: int, port: int, q) -> None:
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        io = HostStageIO(FakeStage(rank == 0, rank == world - 1), WIDTH, HIDDEN,
-                         first=rank == 0, last=rank == world - 1, capacity=256, chunk=WIDTH,
-                         layer_range=(rank, rank + 1), model_layers=world)
+        kind = PrefillStage if one_pass else FakeStage
+        stage = kind(rank == 0, rank == world - 1)
+        io = HostStageIO(stage, WIDTH, HIDDEN, first=rank == 0, last=rank == world - 1,
+                         capacity=256, chunk=WIDTH, layer_range=(rank, rank + 1),
+                         model_layers=world)
         if rank != 0:
             q.put((rank, "ms", run_stage(None, rank, world, WIDTH, io=io)))
+            q.put((rank, "prefilled", getattr(stage, "prefilled", None)))
             return
         chain = DistChain(None, world, WIDTH, io=io)
-        prompt = list(range(10, 29))  # 19 tokens: two 8-row chunks, then three single rows
+        # 19 tokens: two 8-row chunks, then three single rows; or one prefill message of 18
+        # rows, then the last token as a step
+        prompt = list(range(10, 29))
+        assert chain.mem.can_prefill == one_pass
         assert chain.prefill(prompt) == prompt[-1] + world
         # three chunks in flight, then read in order
         chunks = [(19, 40, [41, 42, 43]), (23, 50, []), (24, 60, [61, 62, 63, 64, 65, 66, 67])]
@@ -75,7 +100,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
             raise AssertionError("a non-finite result was not reported")
         except NonFiniteLogits:
             pass
-        assert chain.submitted == 2 + 3 + 3 + 1 + 1 + 1
+        assert chain.submitted == (1 if one_pass else 2 + 3) + 3 + 1 + 1 + 1
         chain.stop()
         q.put((0, "ok", True))
     except BaseException as e:  # reported to the test process
@@ -91,12 +116,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("one_pass", [False, True])
 @pytest.mark.parametrize("world", [2, 3])
-def test_pipeline_protocol_over_gloo(world):
+def test_pipeline_protocol_over_gloo(world, one_pass):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, one_pass, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -115,6 +142,10 @@ def test_pipeline_protocol_over_gloo(world):
     # every stage saw both window marks
     for r in range(1, world):
         assert got[(r, "ms")] > 0.0
+    # one prefill message of rows 0..17 through every stage, each adding 1 to column 0
+    for r in range(1, world):
+        want = [(0, 18, [t + r + 1 for t in range(10, 28)])] if one_pass else None
+        assert got[(r, "prefilled")] == want, (r, got[(r, "prefilled")])
 
 
 def _hello_worker(rank: int, world: int, port: int, bad: str, q) -> None:

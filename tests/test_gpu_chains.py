@@ -113,3 +113,61 @@ def test_local_chain_matches_the_oracle(gpu, name, n_stages):
     for s in stages:
         s.close()
     ref.close()
+
+
+def _next_steps(chain, prompt, one_pass, chunks):
+    """A fresh prefill of `prompt` through the chain (one pass per stage, or chunk-sized
+    steps), then the teacher-forced `chunks`; the pick after the prompt and each chunk's
+    logits."""
+    chain.reset()
+    first = chain.prefill(prompt, one_pass=one_pass)
+    return first, [_chain_step_logits(chain, p, toks).logits for p, toks in chunks]
+
+
+@pytest.mark.parametrize("name,n_stages,with_oracle", [("qwen3-1.7b-2stage", 2, True),
+                                                       ("qwen3-4b-3stage", 3, True),
+                                                       ("qwen3-4b-8stage", 4, False),
+                                                       ("qwen3-4b-8stage", 8, False)])
+def test_one_pass_prefill_across_stages(gpu, name, n_stages, with_oracle):
+    """Every stage writes the K/V rows of all but the prompt's last token in one pass and
+    hands its output rows to the next stage. The next steps must match those after the
+    chunk-sized prefill of src/node.rs:538-566 (logits rel-L2 <= 2e-4) and the oracle's
+    (rel-L2 <= 1e-3), with the pick after the prompt the same wherever the top-2 gap is at
+    least 1e-3. The 2,048-token prompt of the Qwen3-4B seed-3 workload is checked against the
+    chunked path only (the oracle cannot run 2,047 rows of a 4B model in a test's time)."""
+    wl = WORKLOADS[name]
+    cfg = wl.target
+    stages = [Shard.random(cfg, r, wl.max_seq, wl.chunk, seed=wl.target_seed)
+              for r in wl.split(n_stages)]
+    chain = LocalChain(stages)
+    assert all(s.can_prefill() for s in stages)
+    prompt = wl.prompt()
+    n = len(prompt)
+    rng = np.random.default_rng(17)
+    chunks = [(n, rng.integers(0, cfg.vocab_size, wl.chunk).tolist()),
+              (n + wl.chunk, rng.integers(0, cfg.vocab_size, wl.chunk).tolist()),
+              (n + 2 * wl.chunk, [int(rng.integers(0, cfg.vocab_size))])]
+    first1, got = _next_steps(chain, prompt, True, chunks)
+    first8, want = _next_steps(chain, prompt, False, chunks)
+    for k, (a, b) in enumerate(zip(got, want)):
+        e = rel_l2(a, b)
+        assert e <= 2e-4, f"chunk {k}: one-pass vs chunked prefill rel-L2 {e:.2e}"
+    if with_oracle:
+        ref = oracle.OracleShard(cfg, 0, cfg.layers, wl.max_seq, wl.chunk)
+        ref.init_random(wl.target_seed)
+        last = _oracle_prefill(ref, prompt, wl.chunk)
+        for k, (p, toks) in enumerate(chunks):
+            e = rel_l2(got[k], ref.forward(p, tokens=toks))
+            assert e <= 1e-3, f"chunk {k}: one-pass prefill vs oracle rel-L2 {e:.2e}"
+        ref.close()
+        t1, t2 = oracle.top2(last)
+        if t1 - t2 >= TIE_GAP:
+            assert first1 == first8 == oracle.argmax(last)
+    else:
+        # the logits of the prompt's last row, from the chunked session's cache
+        last = _chain_step_logits(chain, n - 1, [prompt[-1]]).logits[0]
+        t1, t2 = oracle.top2(last)
+        if t1 - t2 >= TIE_GAP:
+            assert first1 == first8 == oracle.argmax(last)
+    for s in stages:
+        s.close()

@@ -7,6 +7,8 @@ Qwen3-0.6B layer ranges (seed 0) must give the picks, top-1 logits and accept co
 whole-model shard for the prompt's chunks, and the depth-4 pipelined driver of
 src/specpipe.rs over it, with the same weights as draft, the whole shard's committed stream
 (src/node.rs:242-342,466-535 head/middle/tail, direct return of the result to the head).
+A one-pass prefill (one prefill message per link) must then give the whole shard's picks for
+the same chunks wherever its top-2 gap is at least 1e-3.
 """
 import multiprocessing as mp
 import os
@@ -18,6 +20,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 NEW = 16
+TIE_GAP = 1e-3
 
 
 def _free_port() -> int:
@@ -30,6 +33,7 @@ def _worker(rank: int, world: int, port: int, ranges, q) -> None:
     import torch
     import torch.distributed as dist
 
+    import oracle
     from potpori_b200.config import QWEN3_0_6B
     from potpori_b200.distchain import DistChain, run_stage
     from potpori_b200.shard import Shard
@@ -54,7 +58,7 @@ def _worker(rank: int, world: int, port: int, ranges, q) -> None:
         chain = DistChain(stage, world, 8)
         prompt = np.random.default_rng(11).integers(0, cfg.vocab_size, 29).tolist()
         # The prompt in chunk-sized steps, then three chunks in flight at once.
-        got_first = chain.prefill(prompt)
+        got_first = chain.prefill(prompt, one_pass=False)
         pos, want_first = 0, None
         while pos < len(prompt):
             take = 8 if len(prompt) - pos >= 8 else 1
@@ -86,6 +90,28 @@ def _worker(rank: int, world: int, port: int, ranges, q) -> None:
             p += 1
         assert drv.out == want, (drv.out, want)
         assert drv.stats().toks_per_traversal() > 2  # the drafts were accepted
+        # One pass per stage over the same cache rows (one prefill message per link), then the
+        # three chunks: the whole shard's picks wherever its top-2 gap is at least 1e-3.
+        assert chain.mem.can_prefill
+        whole.reset()
+        pos = 0
+        while pos < len(prompt):
+            take = 8 if len(prompt) - pos >= 8 else 1
+            res = whole.verify_tokens(pos, prompt[pos:pos + take], logits=True)
+            pos += take
+        first = chain.prefill(prompt)
+        t1, t2 = oracle.top2(res.logits[-1])
+        if t1 - t2 >= TIE_GAP:
+            assert first == res.argmax[-1]
+        for p, toks in chunks:
+            chain.submit(p, toks[0], toks[1:])
+        for p, toks in chunks:
+            got = chain.poll()
+            want = whole.verify_tokens(p, toks, logits=True)
+            for r in range(len(toks)):
+                t1, t2 = oracle.top2(want.logits[r])
+                if t1 - t2 >= TIE_GAP:
+                    assert got[r] == want.argmax[r], (p, r)
         chain.stop()
         draft.model.shard.close()
         whole.close()

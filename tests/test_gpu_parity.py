@@ -411,10 +411,15 @@ def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
             e = rel_l2(got, other)
             assert e <= 2e-4, f"{cfg.layers}-layer model, step {step}: {e:.2e} against the chunked path"
             cur = int(np.argmax(want))
-    part = Shard.random(QWEN3_0_6B, (0, 2), 64, 8, seed=0)
-    assert not part.can_prefill()
+    later = Shard.random(QWEN3_0_6B, (2, 4), 64, 8, seed=0)
     with pytest.raises(PPError) as e:
-        part.prefill(0, [1, 2, 3])
+        later.prefill(0, [1, 2, 3])  # token input on a later stage
+    assert e.value.status == PP_E_INVALID
+    tiny = Shard(TINY, (0, 2), 8, 2)
+    tiny.load(tiny_weights())
+    assert not tiny.can_prefill()
+    with pytest.raises(PPError) as e:
+        tiny.prefill(0, [1, 2, 3])  # head size 4
     assert e.value.status == PP_E_UNSUPPORTED
 
 
@@ -451,3 +456,28 @@ def test_prefill_past_2048_keys_matches_the_chunked_path(gpu):
         cur = int(np.argmax(other))
     pre.close()
     chk.close()
+
+
+def test_bounded_wait_times_out_and_the_shard_recovers(gpu):
+    """A device wait that nothing can end (the decode kernel's first grid barrier made to
+    wait for one CTA more than the grid has, pp_shard_set_wait_test) runs out after its time
+    limit: the step returns PP_E_TIMEOUT instead of hanging, the GPU and the shard stay
+    usable, and the next normal steps match the oracle (the reference bounds its waits too,
+    src/node.rs:47-50)."""
+    from potpori_b200._lib import PP_E_TIMEOUT
+
+    cfg, seed, cap = QWEN3_0_6B, 0, 64
+    dev = Shard.random(cfg, (0, cfg.layers), cap, 8, seed=seed)
+    dev.set_decode_kernel(True)
+    ref = _oracle_whole(cfg, seed, cap, 8)
+    dev.set_wait_test(limit_us=5000, unreachable=True)
+    for _ in range(2):
+        with pytest.raises(PPError) as e:
+            dev.forward_tokens(0, [7])
+        assert e.value.status == PP_E_TIMEOUT
+    dev.set_wait_test(0, False)
+    for pos, tok in enumerate([7, 8, 9]):
+        got = dev.forward_tokens(pos, [tok])[0]
+        want = ref.forward(pos, tokens=[tok])[0]
+        _step_logits_agree(got, want, 0.0, f"pos {pos} after the timeouts")
+    dev.close()
