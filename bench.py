@@ -314,6 +314,7 @@ def run_ours(args):
     ev1.record(stream)
     if world > 1:
         chain.mark(FLAG_WINDOW_END)
+        chain.send_marks()
     torch.cuda.synchronize()
     t1 = time.perf_counter()
     clocks = sampler.stop()

@@ -43,8 +43,13 @@ constexpr uint64_t kDecBarrierNs = 200ull * 1000 * 1000;  // default barrier tim
 constexpr int kDecKAlign = 512;           // K of the weight copies: a multiple of 8 warps x 64
 constexpr int kDecHd = 128;               // head size the attention takes
 
-// K of a decode weight copy (zero columns past K).
-__host__ __device__ inline int dec_kpad(int k) { return (k + kDecKAlign - 1) / kDecKAlign * kDecKAlign; }
+// K of a decode weight copy (zero columns past K): a multiple of 512, and of 1024 above 4096
+// and 2048 above 8192, so the kp / 64 units of a warp's columns split evenly over the lanes of
+// a row (32 / dec_slot_rows(kp) lanes).
+__host__ __device__ inline int dec_kpad(int k) {
+  const int a = k > 8192 ? 2048 : k > 4096 ? 1024 : kDecKAlign;
+  return (k + a - 1) / a * a;
+}
 // Rows per weight slot for rows of kp columns: the largest power of two <= 32 that fits (a lane
 // per row at 32, so at most 32).
 __host__ __device__ inline int dec_slot_rows(int kp) {
@@ -271,44 +276,52 @@ __device__ __forceinline__ void dec_release(DecRing& r, int lane) {
 
 // A lane's part of one GEMV phase: slots of R rows of kp columns; the lanes of a warp take the
 // rows (lpr = 32 / R lanes per row), and warp w the columns [w kp / 8, (w + 1) kp / 8), of
-// which the lane takes upl consecutive 16-byte units starting at unit u0 (of the whole row).
+// which the lane takes upl 16-byte units: unit u0 + us t of the whole row for t < upl.
+// The eight lanes of a quarter warp (one shared-memory wavefront of 16-byte loads) must read
+// eight different bank groups:
+//  * R >= 8: lane l takes row l % R and the contiguous slice l / R of the warp's units; a
+//    quarter warp is eight consecutive rows of one slice, whose row swizzles differ;
+//  * R < 8 (lpr >= 8): lane l takes row l / lpr and every lpr-th unit from l % lpr; a quarter
+//    warp is eight consecutive units of one row.
 struct DecLane {
-  int lpr, upl, row, sub, u0;
+  int lpr, upl, row, sub, u0, us;
 };
 
 __device__ __forceinline__ DecLane dec_lane(int kp, int R, int warp, int lane) {
   DecLane d;
   d.lpr = 32 / R;
   d.upl = (kp >> 6) / d.lpr;
-  d.row = lane / d.lpr;
-  d.sub = lane - d.row * d.lpr;
-  d.u0 = warp * (kp >> 6) + d.sub * d.upl;
+  if (R >= 8) {
+    d.row = lane & (R - 1);
+    d.sub = lane / R;
+    d.u0 = warp * (kp >> 6) + d.sub * d.upl;
+    d.us = 1;
+  } else {
+    d.row = lane / d.lpr;
+    d.sub = lane - d.row * d.lpr;
+    d.u0 = warp * (kp >> 6) + d.sub;
+    d.us = d.lpr;
+  }
   return d;
 }
 
-// Staged input vectors are padded: 16 bytes after every upl units (8 floats per unit), so the
-// slices that the lanes of one row read at the same time start in different bank groups.
-// Float index of column c (upl units per slice):
-__device__ __forceinline__ int dec_vpad(int c, int upl) { return c + 4 * ((c >> 3) / upl); }
-
-// The lane's slice of the staged input vector, 8 floats per unit, held for the whole phase.
+// The lane's units of the staged input vector, 8 floats per unit, held for the whole phase.
 __device__ __forceinline__ void dec_load_x(const float* vec, const DecLane& d, float4 (&x)[16]) {
-  const float4* v4 = (const float4*)(vec + dec_vpad(8 * d.u0, d.upl));  // a slice is contiguous
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     const bool in = t < d.upl;
-    x[2 * t] = in ? v4[2 * t] : make_float4(0.f, 0.f, 0.f, 0.f);
-    x[2 * t + 1] = in ? v4[2 * t + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4* v4 = (const float4*)(vec + 8 * (d.u0 + d.us * t));
+    x[2 * t] = in ? v4[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[2 * t + 1] = in ? v4[1] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
 // Stages K floats of src plus, when given, the `nadd` vectors add[j][0..K) (the heads' shares
-// of O, summed in head order), times w when given, into vec in the padded layout of kp columns
-// in slices of upl units (zeros past K); the CTA's own rows [o0, o1) of the sum also go to
-// xown when given. Returns the sum of squares of the sum, reduced in the same order in every
-// CTA.
+// of O, summed in head order), times w when given, into vec[0..kp) (zeros past K); the CTA's
+// own rows [o0, o1) of the sum also go to xown when given. Returns the sum of squares of the
+// sum, reduced in the same order in every CTA.
 __device__ __forceinline__ float dec_stage_vec(const float* src, const float* add, int nadd,
-                                               const float* w, int K, int kp, int upl, float* vec,
+                                               const float* w, int K, int kp, float* vec,
                                                float* red, int tid, float* xown, int o0, int o1) {
   constexpr int T = kConsumerWarps * 32, B = 4;  // float4s per thread per batch of loads
   float ss = 0.f;
@@ -357,7 +370,7 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* ad
           x.z *= ww[k].z;
           x.w *= ww[k].w;
         }
-        *(float4*)(vec + dec_vpad(4 * q, upl)) = x;
+        *(float4*)(vec + 4 * q) = x;
       }
     }
   }
@@ -385,7 +398,7 @@ __device__ __forceinline__ void dec_slot(const uint8_t* slot, int n, int i, int 
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     if (t < d.upl) {
-      const uint4 v = *(const uint4*)(row + (((d.u0 + t) ^ key) << 4));
+      const uint4 v = *(const uint4*)(row + (((d.u0 + d.us * t) ^ key) << 4));
       ffma2(a0, make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x[2 * t].x, x[2 * t].y));
       ffma2(a1, make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x[2 * t].z, x[2 * t].w));
       ffma2(a0, make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x[2 * t + 1].x, x[2 * t + 1].y));
@@ -393,7 +406,11 @@ __device__ __forceinline__ void dec_slot(const uint8_t* slot, int n, int i, int 
     }
   }
   float s = (a0.x + a0.y) + (a1.x + a1.y);
-  for (int o = d.lpr >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (d.us == 1) {  // the lanes of a row are R apart
+    for (int o = 32 / d.lpr; o < 32; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  } else {          // the lanes of a row are adjacent
+    for (int o = d.lpr >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  }
   if (mine && d.sub == 0) part[(i + d.row) * kConsumerWarps + warp] = s;
 }
 
@@ -513,7 +530,7 @@ __device__ __forceinline__ void dec_attn_key(DecAttnState<G>& st, const float (&
 template <int G>  // query heads per KV head (a.G)
 __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeLayer& L,
                                               const DecPlan& P, DecRing& r, bool live, int pos,
-                                              int layer, float* vec, float* ah, int upl_o,
+                                              int layer, float* vec, float* ah,
                                               int* flag, bool* live_out, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   constexpr int hd = kDecHd, half = hd / 2;
@@ -686,8 +703,8 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   consumer_sync();
   // Every unit of the head waits for the head's S partials of this layer (the counter counts
   // the units of every layer so far), then merges all of them itself: exp(max_s - max)
-  // weights in split order. The merged output (G query heads x head_dim) goes to `ah`, in
-  // the padded slices of the O rows' phase (`upl_o` units per slice).
+  // weights in split order. The merged output (G query heads x head_dim) goes to `ah`, the
+  // input vector of the O rows' phase.
   if (tid == 0) {
     int ok = 1;
     red_release_gpu(&a.sync[2 + h], 1u);
@@ -747,7 +764,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
       Ls += Ss[g * S + sp] * f;
       O += __ldcg(col + (size_t)sp * stride) * f;
     }
-    ah[dec_vpad(e, upl_o)] = O / Ls;
+    ah[e] = O / Ls;
   }
   consumer_sync();
   return true;
@@ -858,7 +875,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
               v.z *= ww.z;
               v.w *= ww.w;
             }
-            *(float4*)(vec + dec_vpad(4 * q, d.upl)) = v;
+            *(float4*)(vec + 4 * q) = v;
           }
           t = warp_sum(t);
           if (lane == 0) red[warp] = t;
@@ -868,7 +885,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
           for (int i = 0; i < kConsumerWarps; ++i) ss += red[i];
           consumer_sync();
         } else {
-          ss = dec_stage_vec(a.x, nullptr, 0, L.n_attn, a.H, a.kH, d.upl, vec, red, tid, nullptr, 0, 0);
+          ss = dec_stage_vec(a.x, nullptr, 0, L.n_attn, a.H, a.kH, vec, red, tid, nullptr, 0, 0);
         }
         rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
@@ -885,7 +902,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
     if (P.h >= 0) {
       const DecLane d = dec_lane(a.kO, P.rps_oh, warp, lane);
       bool hlive = live;
-      if (!dec_attention<G>(a, L, P, r, live, pos, l, vec, ah, d.upl, flag, &hlive, tid)) {
+      if (!dec_attention<G>(a, L, P, r, live, pos, l, vec, ah, flag, &hlive, tid)) {
         lost = true;
         break;
       }
@@ -906,8 +923,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
       const DecLane d = dec_lane(a.kH, P.rps_gu, warp, lane);
       float rinv = 1.f;
       if (live) {
-        const float ss = dec_stage_vec(a.x, a.opart, a.nkv, L.n_ffn, a.H, a.kH, d.upl, vec, red,
-                                       tid, xown, P.o0, P.o1);
+        const float ss = dec_stage_vec(a.x, a.opart, a.nkv, L.n_ffn, a.H, a.kH, vec, red, tid,
+                                       xown, P.o0, P.o1);
         rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
       float4 x[16];
@@ -926,7 +943,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
     // ---- down + residual.
     {
       const DecLane d = dec_lane(a.kI, P.rps_d, warp, lane);
-      if (live) dec_stage_vec(a.act, nullptr, 0, nullptr, a.I, a.kI, d.upl, vec, red, tid, nullptr, 0, 0);
+      if (live) dec_stage_vec(a.act, nullptr, 0, nullptr, a.I, a.kI, vec, red, tid, nullptr, 0, 0);
       float4 x[16];
       dec_load_x(vec, d, x);
       if (!dec_rows(r, live, P.o1 - P.o0, P.o0, a.kI, P.rps_d, d, x, part, warp, lane, tid, false,

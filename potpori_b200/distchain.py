@@ -52,6 +52,7 @@ RING = 64       # chunk slots of every inbox and of the result ring
 FLAG_WINDOW_START = 2
 FLAG_WINDOW_END = 4
 FLAG_PREFILL = 8  # the message is a prompt prefill: (pos, rows) in the link's parameter slot
+FLAG_MARKS = 16   # the message has no rows and carries only its flags (timed-window marks)
 PREFILL_MAX = 2048  # rows of one prefill message
 WAIT_S = 120.0  # a stage that hears nothing for this long ends the session with an error
 
@@ -451,6 +452,9 @@ def run_stage(shard, rank: int, world: int, width: int, io=None) -> float:
             if m == 0:
                 if not io.last:
                     io.send(rank, k, 0, info)
+                if flags & FLAG_MARKS:
+                    k += 1
+                    continue
                 break
             io.recv(k, m)
             io.step()
@@ -488,6 +492,15 @@ class DistChain:
     def mark(self, flags: int) -> None:
         """Put flag bits on the next chunk sent (timed-window marks)."""
         self.pending_flags |= flags
+
+    def send_marks(self) -> None:
+        """Send the pending flag bits now, in a message without rows that every stage passes
+        on after the chunks sent before it (so a stage's timed window ends with its share of
+        those chunks, not with the next chunk)."""
+        if self.pending_flags:
+            self.io.send(0, self.seq, 0, (self.pending_flags | FLAG_MARKS) << 8)
+            self.pending_flags = 0
+            self.seq += 1
 
     def submit(self, pos: int, cur: int, drafts: List[int]) -> None:
         # A slot of every inbox is reused RING chunks later; with at most RING / 2 chunks

@@ -91,6 +91,7 @@ def _worker(rank: int, world: int, port: int, one_pass: bool, q) -> None:
         for pos, cur, ds in chunks:
             chain.submit(pos, cur, ds)
         chain.mark(FLAG_WINDOW_END)
+        chain.send_marks()  # a message without rows: every stage ends its window on it
         chain.submit(32, 70, [71])
         for _, cur, ds in chunks + [(32, 70, [71])]:
             assert chain.poll() == [t + world for t in [cur] + ds]

@@ -371,6 +371,40 @@ def test_decode_kernel_matches_the_oracle_and_the_layer_kernels(gpu):
     print(f"decode kernel: worst rel-L2 {worst:.2e} vs oracle, {worst_lay:.2e} vs layer kernels")
 
 
+@pytest.mark.parametrize("H,I,nh,G", [(2048, 6144, 16, 2), (2560, 9728, 32, 4),
+                                      (1024, 4608, 16, 2), (1024, 3072, 8, 1)])
+def test_decode_kernel_row_layouts(gpu, H, I, nh, G):
+    """The decode kernel's GEMV slots take R = 32, 16, 8, 4, 2 or 1 rows of the padded K at a
+    time, with the lanes of a row either R apart (contiguous column slices) or adjacent (every
+    lpr-th 16-byte unit); two-layer models of the Qwen3-1.7B and Qwen3-4B geometries, an
+    intermediate size whose padded K (5120) splits 80 units over 16 lanes, and one query head
+    per KV head: 1-row steps at 1 and at 300 cached positions give the oracle's logits
+    (rel-L2 <= 1e-3) and the per-layer kernels' (rel-L2 <= 2e-4)."""
+    from potpori_b200.config import QwenConfig
+    cfg = QwenConfig(layers=2, hidden=H, intermediate=I, head_dim=128, n_heads=nh,
+                     n_kv_heads=nh // G, vocab_size=1000, rms_norm_eps=1e-6, rope_theta=1e6)
+    dec = Shard.random(cfg, (0, 2), 512, 8, seed=9)
+    lay = Shard.random(cfg, (0, 2), 512, 8, seed=9)
+    dec.set_decode_kernel(True)
+    ref = _oracle_whole(cfg, 9, 512, 8)
+    rng = np.random.default_rng(H + I)
+    worst = 0.0
+    for pos in (0, 1):
+        t = int(rng.integers(0, cfg.vocab_size))
+        got, other = dec.forward_tokens(pos, [t])[0], lay.forward_tokens(pos, [t])[0]
+        worst = _step_logits_agree(got, ref.forward(pos, tokens=[t])[0], worst, f"pos {pos}")
+        assert rel_l2(got, other) <= 2e-4
+    for sh in (dec, lay, ref):
+        sh.fill_kv(3, 300)
+    for pos in (300, 301):
+        t = int(rng.integers(0, cfg.vocab_size))
+        got, other = dec.forward_tokens(pos, [t])[0], lay.forward_tokens(pos, [t])[0]
+        worst = _step_logits_agree(got, ref.forward(pos, tokens=[t])[0], worst, f"pos {pos}")
+        assert rel_l2(got, other) <= 2e-4
+    for sh in (dec, lay, ref):
+        sh.close()
+
+
 def test_prefill_matches_the_chunked_path_and_the_oracle(gpu):
     """pp_shard_prefill (all layers over a prompt chunk at once: tensor-core projections,
     flash-style causal attention) leaves the K/V rows of the reference's chunked prefill
