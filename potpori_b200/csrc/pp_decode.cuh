@@ -42,6 +42,14 @@ constexpr int kDecKvHalf = kDecSlot / 2;  // K rows at 0, V rows at 16 KB of a K
 constexpr uint64_t kDecBarrierNs = 200ull * 1000 * 1000;  // default barrier time limit
 constexpr int kDecKAlign = 512;           // K of the weight copies: a multiple of 8 warps x 64
 constexpr int kDecHd = 128;               // head size the attention takes
+// Three warpgroups: two of consumer warps and one whose first thread is the producer. The block
+// launches at 168 registers a thread (65,536 / 384); the producer warpgroup gives back all but
+// 40 and the consumer warpgroups take them: 128 x 40 + 256 x 232 = 384 x 168.
+constexpr int kDecThreads = 384;
+constexpr int kDecMaxAdds = 8;  // KV heads whose O shares the gate/up staging sums
+constexpr int kDecProducerRegs = 40, kDecConsumerRegs = 232;
+static_assert(128 * kDecProducerRegs + 256 * kDecConsumerRegs <= kDecThreads * 168,
+              "the register split must fit the launch's registers");
 
 // K of a decode weight copy (zero columns past K): a multiple of 512, and of 1024 above 4096
 // and 2048 above 8192, so the kp / 64 units of a warp's columns split evenly over the lanes of
@@ -324,38 +332,45 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* ad
                                                const float* w, int K, int kp, float* vec,
                                                float* red, int tid, float* xown, int o0, int o1) {
   constexpr int T = kConsumerWarps * 32, B = 4;  // float4s per thread per batch of loads
+  const int step = add ? 1 : B;                   // with adds: one float4 of every source
   float ss = 0.f;
-  for (int q0 = 0; q0 < (kp >> 2); q0 += B * T) {
+  for (int q0 = 0; q0 < (kp >> 2); q0 += step * T) {
     float4 v[B], ww[B];
-#pragma unroll
-    for (int k = 0; k < B; ++k) {  // every load of the batch in flight together
-      const int q = q0 + tid + k * T;
-      const bool in = q < (K >> 2);
-      v[k] = in ? __ldcg((const float4*)src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-      ww[k] = (in && w) ? ((const float4*)w)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
-    }
     if (add) {
-      for (int j = 0; j < nadd; ++j) {
-        float4 t[B];
+      // Every source's float4 in flight together, summed in head order.
+      const int q = q0 + tid;
+      const bool in = q < (K >> 2);
+      float4 t[kDecMaxAdds];
 #pragma unroll
-        for (int k = 0; k < B; ++k) {
-          const int q = q0 + tid + k * T;
-          t[k] = q < (K >> 2) ? __ldcg((const float4*)(add + (size_t)j * K) + q)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+      for (int j = 0; j < kDecMaxAdds; ++j)
+        if (j < nadd)
+          t[j] = in ? __ldcg((const float4*)(add + (size_t)j * K) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[0] = in ? __ldcg((const float4*)src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ww[0] = (in && w) ? ((const float4*)w)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
 #pragma unroll
-        for (int k = 0; k < B; ++k) {
-          v[k].x += t[k].x;
-          v[k].y += t[k].y;
-          v[k].z += t[k].z;
-          v[k].w += t[k].w;
+      for (int j = 0; j < kDecMaxAdds; ++j) {
+        if (j < nadd) {
+          v[0].x += t[j].x;
+          v[0].y += t[j].y;
+          v[0].z += t[j].z;
+          v[0].w += t[j].w;
         }
+      }
+#pragma unroll
+      for (int k = 1; k < B; ++k) v[k] = ww[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+#pragma unroll
+      for (int k = 0; k < B; ++k) {  // every load of the batch in flight together
+        const int q = q0 + tid + k * T;
+        const bool in = q < (K >> 2);
+        v[k] = in ? __ldcg((const float4*)src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        ww[k] = (in && w) ? ((const float4*)w)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
       }
     }
 #pragma unroll
     for (int k = 0; k < B; ++k) {
       const int q = q0 + tid + k * T;
-      if (q < (kp >> 2)) {
+      if (k < step && q < (kp >> 2)) {
         float4 x = v[k];
         if (xown && 4 * q + 3 >= o0 && 4 * q < o1) {
           const float e[4] = {x.x, x.y, x.z, x.w};
@@ -387,23 +402,34 @@ __device__ __forceinline__ float dec_stage_vec(const float* src, const float* ad
 // One slot of a GEMV phase: rows [i, i + n) of the phase, whose first row is row g0 of the
 // weight copy (the key of its unit swizzle). Each lane dots its units of its row, the lanes of
 // a row are summed, and the warp's sum of row i + j goes to part[(i + j) * 8 + warp].
+// U: the lane's units per row when known at compile time (all of them loaded before the first
+// product), 0 for d.upl <= 8 at run time.
+template <int U>
 __device__ __forceinline__ void dec_slot(const uint8_t* slot, int n, int i, int g0, int kp,
                                          const DecLane& d, const float4 (&x)[16], float* part,
                                          int warp) {
+  constexpr int UM = U ? U : 8;
   const bool mine = d.row < n;
   const int rr = mine ? d.row : 0;  // a lane without a row reads row 0 and drops the sum
   const uint8_t* row = slot + (size_t)rr * kp * 2;
   const int key = (g0 + i + rr) & 7;
   float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+  const auto dot = [&](const uint4& v, int t) {
+    ffma2(a0, make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x[2 * t].x, x[2 * t].y));
+    ffma2(a1, make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x[2 * t].z, x[2 * t].w));
+    ffma2(a0, make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x[2 * t + 1].x, x[2 * t + 1].y));
+    ffma2(a1, make_float2(bf16lo(v.w), bf16hi(v.w)), make_float2(x[2 * t + 1].z, x[2 * t + 1].w));
+  };
+  if constexpr (U > 0) {
+    uint4 v[UM];
 #pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    if (t < d.upl) {
-      const uint4 v = *(const uint4*)(row + (((d.u0 + d.us * t) ^ key) << 4));
-      ffma2(a0, make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x[2 * t].x, x[2 * t].y));
-      ffma2(a1, make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x[2 * t].z, x[2 * t].w));
-      ffma2(a0, make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x[2 * t + 1].x, x[2 * t + 1].y));
-      ffma2(a1, make_float2(bf16lo(v.w), bf16hi(v.w)), make_float2(x[2 * t + 1].z, x[2 * t + 1].w));
-    }
+    for (int t = 0; t < UM; ++t) v[t] = *(const uint4*)(row + (((d.u0 + d.us * t) ^ key) << 4));
+#pragma unroll
+    for (int t = 0; t < UM; ++t) dot(v[t], t);
+  } else {
+#pragma unroll
+    for (int t = 0; t < UM; ++t)
+      if (t < d.upl) dot(*(const uint4*)(row + (((d.u0 + d.us * t) ^ key) << 4)), t);
   }
   float s = (a0.x + a0.y) + (a1.x + a1.y);
   if (d.us == 1) {  // the lanes of a row are R apart
@@ -427,7 +453,14 @@ __device__ __forceinline__ bool dec_rows(DecRing& r, bool live, int rows, int g0
   for (int i = 0; i < rows; i += R) {
     const int n = rows - i < R ? rows - i : R;
     if (!dec_take(r)) return false;
-    if (live) dec_slot(r.cur(), n, i, g0, kp, d, x, part, warp);
+    if (live) {
+      switch (d.upl) {  // the units per lane of the Qwen3-0.6B phases: QKV and gate/up, down, O
+        case 8: dec_slot<8>(r.cur(), n, i, g0, kp, d, x, part, warp); break;
+        case 6: dec_slot<6>(r.cur(), n, i, g0, kp, d, x, part, warp); break;
+        case 4: dec_slot<4>(r.cur(), n, i, g0, kp, d, x, part, warp); break;
+        default: dec_slot<0>(r.cur(), n, i, g0, kp, d, x, part, warp); break;
+      }
+    }
     dec_release(r, lane);  // this warp's reads of the slot are done (the sums depend on them)
   }
   if (!live) return true;
@@ -733,6 +766,15 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   }
   float* Ms = mrg;           // [G][S] (the warps' partials are no longer needed)
   float* Ss = mrg + G * S;   // [G][S]
+  // The thread's first output element's column of the S partials and the (max, sum) pairs go
+  // out as one batch of loads (one L2 round trip).
+  const auto column = [&](int e) { return a.part + (size_t)(h * G + e / hd) * S * stride + 4 + e % hd; };
+  float pv[32];
+  if (tid < G * hd) {
+    const float* col = column(tid);
+#pragma unroll
+    for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
+  }
   for (int e = tid; e < G * S; e += kConsumerWarps * 32) {
     const int g = e / S, sp = e - g * S;
     const float2 ml = __ldcg((const float2*)(a.part + ((size_t)(h * G + g) * S + sp) * stride));
@@ -741,11 +783,12 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
   }
   consumer_sync();
   for (int e = tid; e < G * hd; e += kConsumerWarps * 32) {
-    const int g = e / hd, d = e - g * hd;
-    const float* col = a.part + (size_t)(h * G + g) * S * stride + 4 + d;
-    float pv[32];
+    const int g = e / hd;
+    const float* col = column(e);
+    if (e != tid) {
 #pragma unroll
-    for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
+      for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
+    }
     float M = -INFINITY;
     for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
     float Ls = 0.f, O = 0.f;
@@ -771,7 +814,7 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
 }
 
 template <int G>  // query heads per KV head (a.G)
-__global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int NG = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
@@ -807,8 +850,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   const DecPlan P = dec_plan(a, b, NG, pos);
 
   // ------------------------------------------------------------------ producer thread
-  if (warp == kConsumerWarps) {
-    if (lane != 0) return;
+  if (warp >= kConsumerWarps) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDecProducerRegs));
+    if (warp != kConsumerWarps || lane != 0) return;
     bool ok = true;
     for (int l = 0; l < a.nl && ok; ++l) {
       const DecodeLayer& L = a.layers[l];
@@ -835,6 +879,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) pp_decode_step_kernel(const D
   }
 
   // ------------------------------------------------------------------ consumer warps
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kDecConsumerRegs));
   // Per layer, four grid barriers and one barrier among the units of each KV head:
   //   QKV (input RMSNorm) | attention: each unit's partial, the head's units meet, every unit
   //   merges the head's splits and computes its rows of the head's share of O | gate/up (the

@@ -679,7 +679,7 @@ pp_status enqueue_decode_step(pp_shard* s, cudaStream_t st) {
   a.res = s->d_res;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(kDecThreads);
   cfg.dynamicSmemBytes =
       DecodeSmem(ns, s->dec_vec, decode_own_cap(s, grid),
                  decode_part_rows(s->H, s->Q, s->KV, s->I, s->nkv, grid)).total();
@@ -2025,10 +2025,11 @@ pp_status pp_shard_set_decode_kernel(pp_shard* s, int32_t enabled) {
     if (!(s->first && s->last))
       return fail(s, PP_E_UNSUPPORTED, "the decode kernel runs shards that hold every layer");
     // A gate/up pair of rows (two rows of the padded H) and a row of the padded Q and I must
-    // fit one ring slot; the attention takes head size 128 and up to 4 query heads per KV head.
+    // fit one ring slot; the attention takes head size 128 and up to 4 query heads per KV head,
+    // and the gate/up input sums the O shares of at most 8 KV heads.
     if (s->H % 8 || s->Q % 8 || s->I % 8 || 4 * dec_kpad(s->H) > kDecSlot ||
         2 * dec_kpad(s->Q) > kDecSlot || 2 * dec_kpad(s->I) > kDecSlot || s->hd != kDecHd ||
-        (s->G != 1 && s->G != 2 && s->G != 4))
+        (s->G != 1 && s->G != 2 && s->G != 4) || s->nkv > kDecMaxAdds)
       return fail(s, PP_E_UNSUPPORTED, "geometry outside the decode kernel's row and slot sizes");
     const int vec = decode_vec_floats(s->H, s->Q, s->I, s->hd, s->G);
     size_t budget = dyn_smem_limit(s, pp_decode_step_kernel<1>);
