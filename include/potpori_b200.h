@@ -244,13 +244,13 @@ pp_status pp_shard_prefill_send(pp_shard* shard, uint32_t seq, uint32_t t, uint3
  * single-token verify steps) as one persistent cooperative kernel over the shard's SM budget
  * followed by the vocabulary head, instead of six kernels per layer (enabled = 1; 0 returns
  * to the per-layer kernels). The kernel streams a row-major copy of the layer weights (K
- * padded to a multiple of 512), made on first use after every weight upload and held until
- * the shard is destroyed (0.9 GB for Qwen3-0.6B). Same step semantics as the per-layer path
- * (src/qwen/model.rs:366-412 for one token); the F32 summation order differs, within the
- * parity tolerances. PP_E_UNSUPPORTED for
- * a shard without every layer or outside the kernel's sizes (hidden <= 8192, q_dim and
- * intermediate <= 16384, all multiples of 8; head size 128 with 1, 2 or 4 query heads per KV
- * head). No counterpart in the reference. */
+ * padded to a multiple of 512, of 1024 above 4096 and of 2048 above 8192), made on first use
+ * after every weight upload and held until the shard is destroyed (0.9 GB for Qwen3-0.6B).
+ * Same step semantics as the per-layer path (src/qwen/model.rs:366-412 for one token); the
+ * F32 summation order differs, within the parity tolerances. PP_E_UNSUPPORTED for a shard
+ * without every layer or outside the kernel's sizes (hidden <= 8192, q_dim and intermediate
+ * <= 16384, all multiples of 8; head size 128 with 1, 2 or 4 query heads per KV head and at
+ * most 8 KV heads). No counterpart in the reference. */
 pp_status pp_shard_set_decode_kernel(pp_shard* shard, int32_t enabled);
 int32_t pp_shard_decode_kernel(const pp_shard* shard);
 
