@@ -85,6 +85,47 @@ __device__ __forceinline__ void attn_init_barriers(const AttnSmem& L, uint8_t* s
   fence_barrier_init();
 }
 
+// Key range of split s: 32-key tiles [t0, t1) of the keys visible to the chunk's last row,
+// keys [t0 * 32, kend).
+__device__ __forceinline__ void attn_split_range(const AttnArgs& a, int s, int& t0, int& t1,
+                                                 int& kend) {
+  const int c = a.desc->pos + a.desc->m;  // keys visible to the last row
+  const int ntiles = (c + kAttnTile - 1) / kAttnTile;
+  const int tps = (ntiles + a.splits - 1) / a.splits;
+  t0 = s * tps;
+  t1 = min(ntiles, t0 + tps);
+  kend = min(c, t1 * kAttnTile);
+}
+
+// Bulk copy of the K and V rows of tile `tile` (rows j0 .. min(j0 + 32, kend)) of KV head h into
+// ring buffer `bi`, completing on bar[bi].
+__device__ __forceinline__ void attn_issue_tile(const AttnArgs& a, const AttnSmem& L, uint8_t* sm,
+                                                int h, int tile, int kend, int bi) {
+  const int rowb = L.rowb;
+  uint64_t* bar = (uint64_t*)(sm + L.bar_off());
+  const int j0 = tile * kAttnTile;
+  const uint32_t bytes = (uint32_t)min(kAttnTile, kend - j0) * rowb;
+  uint8_t* dst = sm + (size_t)bi * 2 * kAttnTile * rowb;
+  mbar_arrive_expect_tx(&bar[bi], 2 * bytes);
+  bulk_load(dst, a.kcache + ((size_t)h * a.capacity + j0) * rowb, bytes, &bar[bi]);
+  bulk_load(dst + (size_t)kAttnTile * rowb, a.vcache + ((size_t)h * a.capacity + j0) * rowb, bytes,
+            &bar[bi]);
+}
+
+// Before the step's QKV kernel has finished (thread 0, the CTA's first unit): the first ring
+// buffers' worth of this split's tiles whose keys all precede pos — rows written by earlier
+// steps, which the QKV kernel does not touch. Returns the number of tiles issued.
+__device__ __forceinline__ int attn_prefetch(const AttnArgs& a, int h, int s, const AttnSmem& L,
+                                             uint8_t* sm) {
+  int t0, t1, kend;
+  attn_split_range(a, s, t0, t1, kend);
+  const int pos = a.desc->pos;
+  int n = 0;
+  for (int tile = t0; tile < t1 && n < L.stages && (tile + 1) * kAttnTile <= pos; ++tile, ++n)
+    attn_issue_tile(a, L, sm, h, tile, kend, n);
+  return n;
+}
+
 // One (KV head h, key split s) unit on the 8 consumer warps (threads 0..255), NT query tiles
 // of 8 (NT = ceil(G*MT / 8)). Per 32-key tile, on the tensor cores (m16n8k16 BF16, F32
 // accumulate), every F32 operand carried as hi + lo BF16 and the three products
@@ -100,11 +141,12 @@ __device__ __forceinline__ void attn_init_barriers(const AttnSmem& L, uint8_t* s
 // K/V tiles are contiguous 32-row blocks of the cache, fetched by thread 0 with one bulk copy
 // each into a ring of L.stages buffers (mbarrier completion, bounded waits). `uses` counts the
 // tiles this CTA has taken through the ring before (buffer and parity of the next one); it is
-// advanced on return. Writes the split's partial (max, sum, unnormalised output) and returns
-// false when a wait expired (ST_TIMEOUT set, copies in flight drained).
+// advanced on return. `issued` tiles of the unit were requested already (attn_prefetch, thread
+// 0 only). Writes the split's partial (max, sum, unnormalised output) and returns false when a
+// wait expired (ST_TIMEOUT set, copies in flight drained).
 template <int MT, int NT>
 __device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const AttnSmem& L,
-                                          uint8_t* sm, uint32_t& uses) {
+                                          uint8_t* sm, uint32_t& uses, int issued = 0) {
   const int hd = a.head_dim, hdk = kv_hdk(hd), mask = kv_swz_mask(hd);
   const int rowb = L.rowb, S = L.stages;
   constexpr int NQ8 = 8 * NT;
@@ -122,24 +164,13 @@ __device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const
   const int pos = a.desc->pos, m = a.desc->m;
   const int G = a.n_heads / a.n_kv;
   const int nq = G * MT;
-  const int c = pos + m;  // keys visible to the last row
-  const int ntiles = (c + kAttnTile - 1) / kAttnTile;
-  const int tps = (ntiles + a.splits - 1) / a.splits;
-  const int t0 = s * tps, t1 = min(ntiles, t0 + tps);
-  const int kend = min(c, t1 * kAttnTile);  // this split covers keys [t0*32, kend)
-  const uint8_t* kb = a.kcache + (size_t)h * a.capacity * rowb;
-  const uint8_t* vb = a.vcache + (size_t)h * a.capacity * rowb;
+  int t0, t1, kend;  // this split covers keys [t0*32, kend)
+  attn_split_range(a, s, t0, t1, kend);
 
-  int next_issue = t0;  // thread 0: first tile not yet requested
+  int next_issue = t0 + issued;  // thread 0: first tile not yet requested
   auto issue = [&](int tile) {
     const uint32_t k = uses + (uint32_t)(tile - t0);
-    const int bi = (int)(k % (uint32_t)S);
-    const int j0 = tile * kAttnTile;
-    const uint32_t bytes = (uint32_t)min(kAttnTile, kend - j0) * rowb;
-    uint8_t* dst = kvs + (size_t)bi * 2 * kAttnTile * rowb;
-    mbar_arrive_expect_tx(&bar[bi], 2 * bytes);
-    bulk_load(dst, kb + (size_t)j0 * rowb, bytes, &bar[bi]);
-    bulk_load(dst + (size_t)kAttnTile * rowb, vb + (size_t)j0 * rowb, bytes, &bar[bi]);
+    attn_issue_tile(a, L, sm, h, tile, kend, (int)(k % (uint32_t)S));
   };
   if (tid == 0) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -158,12 +189,24 @@ __device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const
     for (int j = 0; j < 4; ++j)
       v[j] = (valid && d0 + 4 * j < hd) ? *(const float4*)(src + d0 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
     uint8_t* row = qsm + (size_t)qi * rowb;
+    // Two 16-byte units (dims d0 .. d0 + 7 and d0 + 8 .. d0 + 15) of hi and of lo parts, each
+    // stored whole where kv_offset puts it.
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      kv_store(row, qi, d0 + 4 * j + 0, hd, v[j].x);
-      kv_store(row, qi, d0 + 4 * j + 1, hd, v[j].y);
-      kv_store(row, qi, d0 + 4 * j + 2, hd, v[j].z);
-      kv_store(row, qi, d0 + 4 * j + 3, hd, v[j].w);
+    for (int u = 0; u < 2; ++u) {
+      const float x[8] = {v[2 * u].x, v[2 * u].y, v[2 * u].z, v[2 * u].w,
+                          v[2 * u + 1].x, v[2 * u + 1].y, v[2 * u + 1].z, v[2 * u + 1].w};
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        uint16_t h0, l0, h1, l1;
+        split_bf16(x[2 * p], h0, l0);
+        split_bf16(x[2 * p + 1], h1, l1);
+        hw[p] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[p] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+      }
+      const int d = d0 + 8 * u;
+      *(uint4*)(row + kv_offset(qi, d, 0, hd)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *(uint4*)(row + kv_offset(qi, d, 1, hd)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
   }
   for (int q = tid; q < NQ8; q += kAttnThreads) {
@@ -228,22 +271,45 @@ __device__ __forceinline__ bool attn_unit(const AttnArgs& a, int h, int s, const
     }
     consumer_sync();
 
-    // ---- 2. online softmax, a warp per query, lane = key
-    for (int q = warp; q < NQ8; q += 8) {
-      const float sc = S_s[q * 33 + lane];
-      const float mo = m_s[q];
-      const float mn = fmaxf(mo, warp_max(sc));
-      const float alpha = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
-      const float p = (sc == -INFINITY) ? 0.f : __expf(sc - mn);
-      const float ps = warp_sum(p);
-      uint16_t ph, pl;
-      split_bf16(p, ph, pl);
-      *(uint16_t*)(P_s + (size_t)q * 80 + lane * 2) = ph;
-      *(uint16_t*)(P_s + (size_t)(NQ8 + q) * 80 + lane * 2) = pl;
-      if (lane == 0) {
-        m_s[q] = mn;
-        l_s[q] = l_s[q] * alpha + ps;
-        al_s[q] = alpha;
+    // ---- 2. online softmax, lane = key; warp w takes queries w, w + 8, ... (NT of them), their
+    // shuffle reductions interleaved
+    {
+      float sc[NT], mo[NT], mx[NT];
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const int q = warp + 8 * i;
+        sc[i] = S_s[q * 33 + lane];
+        mo[i] = m_s[q];
+        mx[i] = sc[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < NT; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
+      float p[NT], ps[NT], alpha[NT];
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        mx[i] = fmaxf(mo[i], mx[i]);
+        alpha[i] = (mo[i] == -INFINITY) ? 0.f : __expf(mo[i] - mx[i]);
+        p[i] = (sc[i] == -INFINITY) ? 0.f : __expf(sc[i] - mx[i]);
+        ps[i] = p[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < NT; ++i) ps[i] += __shfl_xor_sync(0xffffffffu, ps[i], o);
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const int q = warp + 8 * i;
+        uint16_t ph, pl;
+        split_bf16(p[i], ph, pl);
+        *(uint16_t*)(P_s + (size_t)q * 80 + lane * 2) = ph;
+        *(uint16_t*)(P_s + (size_t)(NQ8 + q) * 80 + lane * 2) = pl;
+        if (lane == 0) {
+          m_s[q] = mx[i];
+          l_s[q] = l_s[q] * alpha[i] + ps[i];
+          al_s[q] = alpha[i];
+        }
       }
     }
     consumer_sync();
@@ -324,11 +390,15 @@ __global__ void __launch_bounds__(kAttnThreads) pp_attn_split_kernel(const AttnA
   const AttnSmem L(a.head_dim, NT, kAttnStages);
   if (threadIdx.x == 0) pdl_launch_dependents();
   if (bad_step(a.desc, a.capacity, MT)) return;
-  if (threadIdx.x == 0) attn_init_barriers(L, sm);
+  int issued = 0;
+  if (threadIdx.x == 0) {
+    attn_init_barriers(L, sm);
+    issued = attn_prefetch(a, blockIdx.x, blockIdx.y, L, sm);
+  }
   pdl_wait();
   consumer_sync();  // barrier init visible to every thread
   uint32_t uses = 0;
-  attn_unit<MT, NT>(a, blockIdx.x, blockIdx.y, L, sm, uses);
+  attn_unit<MT, NT>(a, blockIdx.x, blockIdx.y, L, sm, uses, issued);
 }
 
 // Merge of the splits of one (query head hq, chunk row r) by `nthr` threads (t = 0..nthr-1,
