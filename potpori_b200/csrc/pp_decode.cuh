@@ -552,6 +552,50 @@ __device__ __forceinline__ void dec_attn_key(DecAttnState<G>& st, const float (&
   }
 }
 
+// Two keys a then b for the lane's group: their scores are formed and reduced together (two
+// independent chains), then the state takes key a and then key b exactly as two dec_attn_key
+// calls would.
+template <int G>
+__device__ __forceinline__ void dec_attn_key2(DecAttnState<G>& st, const float (&q)[G][16],
+                                              const float (&ka)[16], const float (&va)[16], bool va_ok,
+                                              const float (&kb)[16], const float (&vb)[16], bool vb_ok,
+                                              float inv_scale) {
+  float sa[G], sb[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float2 acc = make_float2(0.f, 0.f), bcc = acc;
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      ffma2(acc, make_float2(q[g][e], q[g][e + 1]), make_float2(ka[e], ka[e + 1]));
+      ffma2(bcc, make_float2(q[g][e], q[g][e + 1]), make_float2(kb[e], kb[e + 1]));
+    }
+    sa[g] = acc.x + acc.y;
+    sb[g] = bcc.x + bcc.y;
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sa[g] += __shfl_xor_sync(0xffffffffu, sa[g], o);
+      sb[g] += __shfl_xor_sync(0xffffffffu, sb[g], o);
+    }
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    if (w == 0 ? !va_ok : !vb_ok) continue;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float s = (w == 0 ? sa[g] : sb[g]) * inv_scale;
+      const float mn = fmaxf(st.m[g], s);
+      const float al = __expf(st.m[g] - mn);  // 0 for the first key (m = -inf)
+      const float p = __expf(s - mn);
+      st.l[g] = st.l[g] * al + p;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) st.o[g][e] = st.o[g][e] * al + p * (w == 0 ? va[e] : vb[e]);
+      st.m[g] = mn;
+    }
+  }
+}
+
 // Attention unit (KV head h, split s) for the single query position pos: QK-RMSNorm + RoPE
 // of the G query heads and of the new key (tiny.rs:24-37), the new K/V row written by the
 // unit that holds pos, online softmax over the streamed cached rows (tiny.rs:77-101), the
@@ -648,21 +692,27 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
       o[7] = bf16hi(hi.w) + bf16hi(lo.w);
     }
   };
+  // Warps 0-3 take the even slots and warps 4-7 the odd ones, so two slots are worked on at
+  // once; in its slots a lane group takes keys 4 (w % 4) + kg + 16 j (two at a time). Every
+  // warp waits for every slot before releasing it (no warp runs a ring cycle ahead).
   const int npos = P.pe - P.p0;
-  for (int i0 = 0; i0 < npos; i0 += P.kvps) {
+  const int wh = warp >> 2, wq = warp & 3;
+  for (int i0 = 0, si = 0; i0 < npos; i0 += P.kvps, ++si) {
     const int n = npos - i0 < P.kvps ? npos - i0 : P.kvps;
     if (!dec_take(r)) return false;
-    if (live) {
+    if (live && (si & 1) == wh) {
       const uint8_t* ks = r.cur();
       const uint8_t* vs = ks + kDecKvHalf;
-      for (int kk = 4 * warp + kg; kk - kg < n; kk += 4 * kConsumerWarps) {
-        const bool valid = kk < n;
-        const int ki = valid ? kk : 0;
-        const int j = P.p0 + i0 + ki;  // absolute position (the swizzle key)
-        float k[16], v[16];
-        load_row(ks + (size_t)ki * P.rowb, j, k);
-        load_row(vs + (size_t)ki * P.rowb, j, v);
-        dec_attn_key<G>(st, q, k, v, valid, a.inv_scale);
+      for (int kk = 4 * wq + kg; kk - kg < n; kk += 32) {
+        const int kb = kk + 16;
+        const bool va = kk < n, vb = kb < n;
+        const int ia = va ? kk : 0, ib = vb ? kb : 0;
+        float k0[16], v0[16], k1[16], v1[16];
+        load_row(ks + (size_t)ia * P.rowb, P.p0 + i0 + ia, k0);
+        load_row(vs + (size_t)ia * P.rowb, P.p0 + i0 + ia, v0);
+        load_row(ks + (size_t)ib * P.rowb, P.p0 + i0 + ib, k1);
+        load_row(vs + (size_t)ib * P.rowb, P.p0 + i0 + ib, v1);
+        dec_attn_key2<G>(st, q, k0, v0, va, k1, v1, vb, a.inv_scale);
       }
     }
     dec_release(r, lane);
@@ -782,6 +832,15 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
     Ss[e] = ml.y;
   }
   consumer_sync();
+  // The merge weight exp(max_s - max) of every (query head, split), formed once.
+  float* Wf = Ss + G * S;  // [G][S]
+  for (int e = tid; e < G * S; e += kConsumerWarps * 32) {
+    const int g = e / S;
+    float M = -INFINITY;
+    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
+    Wf[e] = Ms[e] == -INFINITY ? 0.f : expf(Ms[e] - M);
+  }
+  consumer_sync();
   for (int e = tid; e < G * hd; e += kConsumerWarps * 32) {
     const int g = e / hd;
     const float* col = column(e);
@@ -789,21 +848,17 @@ __device__ __forceinline__ bool dec_attention(const DecodeArgs& a, const DecodeL
 #pragma unroll
       for (int sp = 0; sp < 32; ++sp) pv[sp] = sp < S ? __ldcg(col + (size_t)sp * stride) : 0.f;
     }
-    float M = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, Ms[g * S + sp]);
     float Ls = 0.f, O = 0.f;
 #pragma unroll
     for (int sp = 0; sp < 32; ++sp) {
       if (sp < S) {
-        const float ms = Ms[g * S + sp];
-        const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+        const float f = Wf[g * S + sp];
         Ls += Ss[g * S + sp] * f;
         O += pv[sp] * f;
       }
     }
     for (int sp = 32; sp < S; ++sp) {
-      const float ms = Ms[g * S + sp];
-      const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+      const float f = Wf[g * S + sp];
       Ls += Ss[g * S + sp] * f;
       O += __ldcg(col + (size_t)sp * stride) * f;
     }
