@@ -34,6 +34,7 @@
 // x * (1 / sqrt(mean(x^2) + eps)) * w, attention scores q.k / sqrt(head_dim).
 #pragma once
 #include "pp_common.cuh"
+#include "pp_gemv.cuh"  // ldmatrix_x4, mma_bf16
 
 namespace pp {
 
@@ -440,6 +441,132 @@ __device__ __forceinline__ void dec_slot(const uint8_t* slot, int n, int i, int 
   if (mine && d.sub == 0) part[(i + d.row) * kConsumerWarps + warp] = s;
 }
 
+// ---- GEMV slots on the tensor cores ------------------------------------------------------------
+// For K up to 2048 a slot is done with mma.sync m16n8k16 (BF16 in, F32 accumulate): warp w
+// takes the same columns [w kp / 8, (w + 1) kp / 8) = KS steps of 16, the weights of 16 rows x 16
+// columns as A (ldmatrix from the swizzled row-major copy), and the phase's input as B with its
+// hi part in column 0 and its lo part in column 1 (x = hi + lo to 2^-17, the split the per-layer
+// GEMVs use), so D[r][0] + D[r][1] is the row's dot product over the warp's columns.
+// B fragment of the lane (m16n8k16, "col" B): b0 = B[k][n], B[k + 1][n], b1 = the same at k + 8,
+// with n = lane / 4 and k = 2 (lane % 4) of each 16-column step.
+// The staged input (kp F32 values at vec) becomes its hi parts (BF16, vec[0 .. kp / 2) as
+// floats) and lo parts (after them), in place: each value is split once per CTA.
+__device__ __forceinline__ void dec_split_vec(float* vec, int kp, int tid) {
+  constexpr int T = kConsumerWarps * 32;
+  float v[8];  // kp <= 2048: at most 8 values a thread
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = tid + j * T < kp ? vec[tid + j * T] : 0.f;
+  consumer_sync();
+  uint16_t* hi = (uint16_t*)vec;
+  uint16_t* lo = hi + kp;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (tid + j * T < kp) split_bf16(v[j], hi[tid + j * T], lo[tid + j * T]);
+  consumer_sync();
+}
+
+template <int KS>
+__device__ __forceinline__ void dec_load_xb(const float* vec, int kp, int warp, int lane,
+                                            uint32_t (&xb)[KS][2]) {
+  const int n = lane >> 2, kq = (lane & 3) * 2;
+  const int c0 = warp * (kp >> 3);
+  const uint16_t* src = (const uint16_t*)vec + (n == 1 ? kp : 0) + c0 + kq;  // hi or lo parts
+#pragma unroll
+  for (int t = 0; t < KS; ++t) {
+    xb[t][0] = n < 2 ? *(const uint32_t*)(src + 16 * t) : 0u;
+    xb[t][1] = n < 2 ? *(const uint32_t*)(src + 16 * t + 8) : 0u;
+  }
+}
+
+// One slot of MT 16-row tiles (rows [i, i + n) of the phase, the first row g0 of the weight copy):
+// the warp's partial sum of each row goes to part[row * 8 + warp]. Rows past n read row 0 and are
+// dropped.
+template <int KS, int MT>
+__device__ __forceinline__ void dec_slot_mma(const uint8_t* slot, int n, int i, int g0, int kp,
+                                             const uint32_t (&xb)[KS][2], float* part, int warp,
+                                             int lane) {
+  const int mi = lane >> 3;
+  const int u0 = (warp * (kp >> 3)) >> 3;  // the warp's first 16-byte unit
+  constexpr int NC = KS < 4 ? KS : 4;       // independent accumulator chains (k steps mod NC)
+  float d[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    float c[NC][4];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+    const int ra = mt * 16 + (mi & 1) * 8 + (lane & 7);
+    const int rr = ra < n ? ra : 0;
+    const uint8_t* row = slot + (size_t)rr * kp * 2;
+    const int key = (g0 + i + rr) & 7;
+#pragma unroll
+    for (int t = 0; t < KS; ++t) {
+      uint32_t af[4];
+      ldmatrix_x4(af, row + (((u0 + 2 * t + (mi >> 1)) ^ key) << 4));
+      mma_bf16(c[t % NC], af, xb[t][0], xb[t][1]);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v = c[0][q];
+#pragma unroll
+      for (int j = 1; j < NC; ++j) v += c[j][q];
+      d[mt][q] = v;
+    }
+  }
+  if ((lane & 3) == 0) {
+    const int g = lane >> 2;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      if (mt * 16 + g < n) part[(i + mt * 16 + g) * kConsumerWarps + warp] = d[mt][0] + d[mt][1];
+      if (mt * 16 + g + 8 < n) part[(i + mt * 16 + g + 8) * kConsumerWarps + warp] = d[mt][2] + d[mt][3];
+    }
+  }
+}
+
+// The part table's rows summed in warp order, then epi for every row (or gate/up pair), one per
+// thread (after the slots of a phase).
+template <typename Epi>
+__device__ __forceinline__ void dec_rows_epilogue(int rows, const float* part, int tid, bool pairs,
+                                                  Epi&& epi) {
+  consumer_sync();
+  const int outs = pairs ? rows >> 1 : rows;
+  for (int t = tid; t < outs; t += kConsumerWarps * 32) {
+    const float4* p = (const float4*)(part + (size_t)(pairs ? 2 * t : t) * kConsumerWarps);
+    const float4 a0 = p[0], a1 = p[1];
+    const float v0 = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
+    float v1 = 0.f;
+    if (pairs) {
+      const float4 b0 = p[2], b1 = p[3];
+      v1 = ((b0.x + b0.y) + (b0.z + b0.w)) + ((b1.x + b1.y) + (b1.z + b1.w));
+    }
+    epi(pairs ? 2 * t : t, v0, v1);
+  }
+}
+
+// dec_rows on the tensor cores (slots of R <= 32 rows, K = 128 KS); the staged input at vec is
+// split into its hi and lo parts in place first.
+template <int KS, typename Epi>
+__device__ __forceinline__ bool dec_rows_mma(DecRing& r, bool live, int rows, int g0, int kp, int R,
+                                             float* vec, float* part, int warp, int lane,
+                                             int tid, bool pairs, Epi&& epi) {
+  uint32_t xb[KS][2];
+  if (live) dec_split_vec(vec, kp, tid);
+  dec_load_xb<KS>(vec, kp, warp, lane, xb);
+  for (int i = 0; i < rows; i += R) {
+    const int n = rows - i < R ? rows - i : R;
+    if (!dec_take(r)) return false;
+    if (live) {
+      if (R > 16)
+        dec_slot_mma<KS, 2>(r.cur(), n, i, g0, kp, xb, part, warp, lane);
+      else
+        dec_slot_mma<KS, 1>(r.cur(), n, i, g0, kp, xb, part, warp, lane);
+    }
+    dec_release(r, lane);
+  }
+  if (!live) return true;
+  dec_rows_epilogue(rows, part, tid, pairs, epi);
+  return true;
+}
+
 // Consumes one weight segment of `rows` rows (from row g0 of the weight copy) in slots of R,
 // then sums the warps' partials of every row (in warp order) and runs epi(row, value, -) for
 // every row — or, with pairs, epi(row, gate, up) for each gate/up pair (row, row + 1) — one
@@ -464,20 +591,29 @@ __device__ __forceinline__ bool dec_rows(DecRing& r, bool live, int rows, int g0
     dec_release(r, lane);  // this warp's reads of the slot are done (the sums depend on them)
   }
   if (!live) return true;
-  consumer_sync();
-  const int outs = pairs ? rows >> 1 : rows;
-  for (int t = tid; t < outs; t += kConsumerWarps * 32) {
-    const float4* p = (const float4*)(part + (size_t)(pairs ? 2 * t : t) * kConsumerWarps);
-    const float4 a0 = p[0], a1 = p[1];
-    const float v0 = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
-    float v1 = 0.f;
-    if (pairs) {
-      const float4 b0 = p[2], b1 = p[3];
-      v1 = ((b0.x + b0.y) + (b0.z + b0.w)) + ((b1.x + b1.y) + (b1.z + b1.w));
-    }
-    epi(pairs ? 2 * t : t, v0, v1);
-  }
+  dec_rows_epilogue(rows, part, tid, pairs, epi);
   return true;
+}
+
+// A GEMV phase over the staged input `vec` (kp columns): on the tensor cores for kp = 256, 1024
+// and 2048, on the CUDA cores otherwise. Measured on the Qwen3-0.6B step (2048 cached
+// positions): the tensor cores for O (256) and QKV, gate/up (1024) with down (3072) on the CUDA
+// cores 747 us, all on the CUDA cores 789 us, all four on the tensor cores 812 us.
+template <typename Epi>
+__device__ __forceinline__ bool dec_phase(DecRing& r, bool live, int rows, int g0, int kp, int R,
+                                          float* vec, float* part, int warp, int lane,
+                                          int tid, bool pairs, Epi&& epi) {
+  switch (kp) {
+    case 256: return dec_rows_mma<2>(r, live, rows, g0, kp, R, vec, part, warp, lane, tid, pairs, epi);
+    case 1024: return dec_rows_mma<8>(r, live, rows, g0, kp, R, vec, part, warp, lane, tid, pairs, epi);
+    case 2048: return dec_rows_mma<16>(r, live, rows, g0, kp, R, vec, part, warp, lane, tid, pairs, epi);
+    default: {
+      const DecLane d = dec_lane(kp, R, warp, lane);
+      float4 x[16];
+      dec_load_x(vec, d, x);
+      return dec_rows(r, live, rows, g0, kp, R, d, x, part, warp, lane, tid, pairs, epi);
+    }
+  }
 }
 
 // Grid barrier among the consumers of all CTAs (the producers never wait on it): barrier
@@ -948,7 +1084,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const De
     // ---- QKV with the input RMSNorm; layer 0 gathers the token's embedding row
     // (src/qwen/model.rs:239-241), also the first residual.
     {
-      const DecLane d = dec_lane(a.kH, P.rps_qkv, warp, lane);
       float rinv = 1.f;
       if (live) {
         float ss;
@@ -989,10 +1124,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const De
         }
         rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
-      float4 x[16];
-      dec_load_x(vec, d, x);
-      if (!dec_rows(r, live, P.q1 - P.q0, P.q0, a.kH, P.rps_qkv, d, x, part, warp, lane, tid,
-                    false, [&](int rr, float v, float) { a.qkv[P.q0 + rr] = v * rinv; })) {
+      if (!dec_phase(r, live, P.q1 - P.q0, P.q0, a.kH, P.rps_qkv, vec, part, warp, lane, tid,
+                     false, [&](int rr, float v, float) { a.qkv[P.q0 + rr] = v * rinv; })) {
         lost = true;
         break;
       }
@@ -1000,18 +1133,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const De
     live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // ---- attention, then this unit's rows of its head's share of O (src/qwen/model.rs:304).
     if (P.h >= 0) {
-      const DecLane d = dec_lane(a.kO, P.rps_oh, warp, lane);
       bool hlive = live;
       if (!dec_attention<G>(a, L, P, r, live, pos, l, vec, ah, flag, &hlive, tid)) {
         lost = true;
         break;
       }
       live = hlive;
-      float4 x[16];
-      dec_load_x(ah, d, x);
       float* op = a.opart + (size_t)P.h * a.H + P.r0;
-      if (!dec_rows(r, live, P.r1 - P.r0, P.r0, a.kO, P.rps_oh, d, x, part, warp, lane, tid,
-                    false, [&](int rr, float v, float) { op[rr] = v; })) {
+      if (!dec_phase(r, live, P.r1 - P.r0, P.r0, a.kO, P.rps_oh, ah, part, warp, lane, tid,
+                     false, [&](int rr, float v, float) { op[rr] = v; })) {
         lost = true;
         break;
       }
@@ -1020,17 +1150,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const De
     // ---- gate/up: the residual after the attention (x plus every head's share of O; this
     // CTA keeps its own rows), the post-attention RMSNorm, SwiGLU (tiny.rs:111-115).
     {
-      const DecLane d = dec_lane(a.kH, P.rps_gu, warp, lane);
       float rinv = 1.f;
       if (live) {
         const float ss = dec_stage_vec(a.x, a.opart, a.nkv, L.n_ffn, a.H, a.kH, vec, red, tid,
                                        xown, P.o0, P.o1);
         rinv = 1.0f / sqrtf(ss / (float)a.H + a.eps);
       }
-      float4 x[16];
-      dec_load_x(vec, d, x);
-      if (!dec_rows(r, live, 2 * (P.j1 - P.j0), 2 * P.j0, a.kH, P.rps_gu, d, x, part, warp, lane,
-                    tid, true, [&](int rr, float g, float u) {
+      if (!dec_phase(r, live, 2 * (P.j1 - P.j0), 2 * P.j0, a.kH, P.rps_gu, vec, part, warp, lane,
+                     tid, true, [&](int rr, float g, float u) {
                       g *= rinv;
                       u *= rinv;
                       a.act[P.j0 + (rr >> 1)] = g / (1.0f + expf(-g)) * u;
@@ -1042,12 +1169,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) pp_decode_step_kernel(const De
     live = live && dec_grid_sync(a, ++nb * (uint32_t)NG, flag, tid);
     // ---- down + residual.
     {
-      const DecLane d = dec_lane(a.kI, P.rps_d, warp, lane);
       if (live) dec_stage_vec(a.act, nullptr, 0, nullptr, a.I, a.kI, vec, red, tid, nullptr, 0, 0);
-      float4 x[16];
-      dec_load_x(vec, d, x);
-      if (!dec_rows(r, live, P.o1 - P.o0, P.o0, a.kI, P.rps_d, d, x, part, warp, lane, tid, false,
-                    [&](int rr, float v, float) {
+      if (!dec_phase(r, live, P.o1 - P.o0, P.o0, a.kI, P.rps_d, vec, part, warp, lane, tid, false,
+                     [&](int rr, float v, float) {
                       v += xown[rr];
                       xown[rr] = v;
                       a.x[P.o0 + rr] = v;
