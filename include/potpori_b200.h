@@ -109,7 +109,7 @@ pp_status pp_shard_forward_hidden(pp_shard* shard, uint32_t pos, uint32_t m, con
 /* Device-resident step for in-box pipeline stages (replaces the QUIC hop of
  * src/node.rs:466-496 with device buffers). The step reads its input from the shard's own
  * input buffer (pp_shard_buffers) and its step header from the device header buffer, both
- * of which a peer copy or NCCL receive may fill; no host synchronisation. stream: a
+ * of which a peer copy may fill (pp_shard_handoff, pp_shard_recv); no host synchronisation. stream: a
  * cudaStream_t (NULL = the shard's stream). max_rows selects the compiled chunk width
  * (1, 2, 4, 8 or 16 rows). */
 pp_status pp_shard_step_device(pp_shard* shard, uint32_t max_rows, void* stream);
@@ -205,8 +205,9 @@ pp_status pp_shard_set_graphs(pp_shard* shard, int32_t enabled);
 pp_status pp_shard_set_pdl(pp_shard* shard, int32_t enabled);
 /* Most CTAs (one per SM) any kernel of this shard launches; 0 = every SM, the default. The
  * split-K GEMVs and the split attention assume all their CTAs are resident at once, so SMs
- * held by other work on the device (the kernels that serve NCCL transfers between pipeline
- * stages) must be left out of the budget, or the CTAs that do not fit run as a second wave.
+ * held by other work on the device (another model's long-running kernels, or transfer
+ * kernels of a communication library) must be left out of the budget, or the CTAs that do
+ * not fit run as a second wave.
  * No counterpart in the reference. Must be at least n_kv_heads. Results stay within the
  * parity tolerances: the split partition (the summation order) depends on the budget. */
 pp_status pp_shard_set_sm_limit(pp_shard* shard, uint32_t ctas);

@@ -234,7 +234,8 @@ class Shard:
 
     def set_sm_limit(self, ctas: int) -> None:
         """Most CTAs (SMs) any kernel of this shard uses; 0 = all. Leave out SMs that other
-        work on the device holds (e.g. NCCL transfer kernels between pipeline stages)."""
+        work on the device holds (another model's long-running kernels, transfer kernels of a
+        communication library)."""
         check(self._L.pp_shard_set_sm_limit(self._h, int(ctas)), self._h, "set_sm_limit")
 
     def sm_limit(self) -> int:
